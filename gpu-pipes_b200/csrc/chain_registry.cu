@@ -1,0 +1,74 @@
+// Table of compiled chains and the spec matcher.
+#include <cstring>
+#include <mutex>
+
+#include "chain_registry.h"
+
+namespace gp {
+
+// launchers defined in the instance translation units
+#define GP_DECLARE(fn) int fn(const LaunchCtx&);
+GP_DECLARE(launch_mgn_ln_f16_k384)
+GP_DECLARE(launch_mgn_ln_f16_k256)
+GP_DECLARE(launch_mgn_ln_f16_k128)
+GP_DECLARE(launch_mgn_ln_bf16_k384)
+GP_DECLARE(launch_mgn_ln_bf16_k256)
+GP_DECLARE(launch_mgn_ln_bf16_k128)
+GP_DECLARE(launch_mgn_nl_f16_k384)
+GP_DECLARE(launch_mgn_nl_f16_k256)
+GP_DECLARE(launch_mgn_nl_f16_k128)
+GP_DECLARE(launch_probe_1l_f16_k128)
+GP_DECLARE(launch_probe_2l_f16_k128)
+#undef GP_DECLARE
+
+#define R GP_ACT_RELU
+#define NO GP_ACT_NONE
+static const ChainEntry kChains[] = {
+    // MeshGraphNet MLP + LayerNorm (mgn_fullmlp), fp16 and bf16
+    {"mgn_ln_f16_k384", GP_F16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k384},
+    {"mgn_ln_f16_k256", GP_F16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k256},
+    {"mgn_ln_f16_k128", GP_F16, 3, {128, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k128},
+    {"mgn_ln_bf16_k384", GP_BF16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k384},
+    {"mgn_ln_bf16_k256", GP_BF16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k256},
+    {"mgn_ln_bf16_k128", GP_BF16, 3, {128, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k128},
+    // same chain without LayerNorm (mgn_linears, test_mlp)
+    {"mgn_nl_f16_k384", GP_F16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_NONE, launch_mgn_nl_f16_k384},
+    {"mgn_nl_f16_k256", GP_F16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_NONE, launch_mgn_nl_f16_k256},
+    {"mgn_nl_f16_k128", GP_F16, 3, {128, 128, 128, 128}, {R, R, NO}, GP_TAIL_NONE, launch_mgn_nl_f16_k128},
+    // single GEMM and two-GEMM probes (known-answer tests of the tcgen05 paths)
+    {"probe_1l_f16_k128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128},
+    {"probe_2l_f16_k128", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128},
+};
+#undef R
+#undef NO
+
+const ChainEntry* find_chain(const gp_mlp_spec& s) {
+  for (const ChainEntry& e : kChains) {
+    if (e.dtype != s.dtype || e.n_layers != s.n_layers || e.tail != s.tail) continue;
+    bool ok = true;
+    for (int l = 0; ok && l <= s.n_layers; ++l) ok = e.widths[l] == s.widths[l];
+    for (int l = 0; ok && l < s.n_layers; ++l) {
+      const bool last_normed = (l == s.n_layers - 1) && s.tail != GP_TAIL_NONE;
+      if (!last_normed) ok = e.act[l] == s.act[l];
+    }
+    if (ok) return &e;
+  }
+  return nullptr;
+}
+
+int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask) {
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(mu);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (*done_mask & bit) return GP_OK;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return set_error(GP_ERR_CUDA, "cudaFuncSetAttribute(%d bytes): %s", bytes, cudaGetErrorString(e));
+  *done_mask |= bit;
+  return GP_OK;
+}
+
+}  // namespace gp

@@ -1,0 +1,45 @@
+// Registry of compiled fused-chain kernels: the host looks a gp_mlp_spec up here and calls the
+// matching launcher. One entry per template instantiation.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "../../include/gpipes.h"
+#include "chain_common.cuh"
+
+namespace gp {
+
+struct LaunchCtx {
+  const gp_mlp_spec* spec;
+  int64_t m;
+  const void* x;
+  void* out;
+  const void* w[kMaxLayers];
+  cudaStream_t stream;
+  int sm_count;
+  ChainArgs args;
+};
+
+using LaunchFn = int (*)(const LaunchCtx&);
+
+struct ChainEntry {
+  const char* name;
+  int dtype;
+  int n_layers;
+  int widths[kMaxLayers + 1];
+  int act[kMaxLayers];
+  int tail;
+  LaunchFn launch;
+};
+
+const ChainEntry* find_chain(const gp_mlp_spec& s);
+
+// helpers implemented in gp_abi.cu
+int set_error(int code, const char* fmt, ...);
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                 uint32_t box_cols, uint32_t box_rows);
+
+// Sets the dynamic shared memory attribute of `kern` once per device.
+int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask);
+
+}  // namespace gp

@@ -1,0 +1,313 @@
+// C ABI of libgpipes.so: argument validation, per-device state, TMA descriptor creation and
+// dispatch of a layer chain to a compiled fused-chain kernel.
+//
+// Reference boundary being replaced: the per-app pybind11 wrappers
+// apps/<app>/pipelined/<app>_pl_ext.cu (e.g. apps/mgn_fullmlp/pipelined/mgn_fullmlp_pl_ext.cu:24-93),
+// which assert widths, lazily allocate a process-static queue scratch (global_queue_space(),
+// apps/mgn_fullmlp/pipelined/mgn_fullmlp_pl.cuh:255-266) and launch on the legacy default stream.
+// Here: widths are runtime-checked against compiled instantiations, errors are returned (never
+// abort), state is per device (created under a mutex), the kernels need no global scratch at all,
+// and the launch goes to the caller's stream.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/gpipes.h"
+#include "chain_common.cuh"
+#include "chain_registry.h"
+
+namespace gp {
+
+// ------------------------------------------------------------------------------------------------
+// errors
+// ------------------------------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+void clear_error() { t_last_error.clear(); }
+
+// ------------------------------------------------------------------------------------------------
+// global knobs
+// ------------------------------------------------------------------------------------------------
+static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+static std::atomic<int> g_inject{0};
+static std::atomic<uint64_t> g_launches{0};
+
+static bool sync_check_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GP_SYNC_CHECK");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
+// ------------------------------------------------------------------------------------------------
+// per-device state
+// ------------------------------------------------------------------------------------------------
+struct DeviceState {
+  int sm_count = 0;
+  int* status = nullptr;  // device status word
+};
+
+static std::mutex g_mu;
+static std::vector<DeviceState*> g_states;
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(GP_ERR_DRIVER, "cuTensorMapEncodeTiled entry point unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  if (static_cast<int>(g_states.size()) <= dev) g_states.resize(dev + 1, nullptr);
+  if (g_states[dev] == nullptr) {
+    auto* st = new DeviceState();
+    e = cudaDeviceGetAttribute(&st->sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+      delete st;
+      return set_error(GP_ERR_CUDA, "device attribute: %s", cudaGetErrorString(e));
+    }
+    e = cudaMalloc(&st->status, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(st->status, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      delete st;
+      return set_error(GP_ERR_CUDA, "status word: %s", cudaGetErrorString(e));
+    }
+    g_states[dev] = st;
+  }
+  *out = g_states[dev];
+  return GP_OK;
+}
+
+// 2-D tensor map over a row-major [rows, cols] 16-bit matrix, box [box_rows, box_cols], 128-byte
+// swizzle, zero fill outside the tensor.
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                 uint32_t box_cols, uint32_t box_rows) {
+  const CUtensorMapDataType dt =
+      dtype == GP_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(GP_ERR_DRIVER, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu", (int)r,
+                     (unsigned long long)rows, (unsigned long long)cols);
+  return GP_OK;
+}
+
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static int validate(const gp_mlp_spec* spec, int64_t m, const void* x, const void* const* w,
+                    const void* const* b, const void* gamma, const void* beta, const void* out) {
+  if (spec == nullptr) return set_error(GP_ERR_ARG, "spec is NULL");
+  if (spec->n_layers < 1 || spec->n_layers > GP_MAX_LAYERS)
+    return set_error(GP_ERR_SHAPE, "n_layers %d out of range [1, %d]", spec->n_layers, GP_MAX_LAYERS);
+  if (spec->dtype != GP_F16 && spec->dtype != GP_BF16)
+    return set_error(GP_ERR_ARG, "dtype %d unknown", spec->dtype);
+  if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
+  if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
+  for (int l = 0; l <= spec->n_layers; ++l)
+    if (spec->widths[l] <= 0 || spec->widths[l] % 8 != 0)
+      return set_error(GP_ERR_SHAPE, "width[%d] = %d must be a positive multiple of 8", l, spec->widths[l]);
+  if (x == nullptr || out == nullptr || w == nullptr)
+    return set_error(GP_ERR_ARG, "x, w and out must not be NULL");
+  if (!aligned(x, 16) || !aligned(out, 16))
+    return set_error(GP_ERR_ALIGN, "x and out must be 16-byte aligned");
+  for (int l = 0; l < spec->n_layers; ++l) {
+    if (w[l] == nullptr) return set_error(GP_ERR_ARG, "w[%d] is NULL", l);
+    if (!aligned(w[l], 16)) return set_error(GP_ERR_ALIGN, "w[%d] must be 16-byte aligned", l);
+    if (b != nullptr && b[l] != nullptr && !aligned(b[l], 4))
+      return set_error(GP_ERR_ALIGN, "b[%d] must be 4-byte aligned", l);
+  }
+  if ((gamma != nullptr && !aligned(gamma, 4)) || (beta != nullptr && !aligned(beta, 4)))
+    return set_error(GP_ERR_ALIGN, "gamma and beta must be 4-byte aligned");
+  if (spec->tail < GP_TAIL_NONE || spec->tail > GP_TAIL_RESIDUAL_LN)
+    return set_error(GP_ERR_ARG, "tail %d unknown", spec->tail);
+  if (spec->tail == GP_TAIL_RESIDUAL_LN && spec->widths[0] != spec->widths[spec->n_layers])
+    return set_error(GP_ERR_SHAPE, "residual tail needs K0 == N_last (%d vs %d)", spec->widths[0],
+                     spec->widths[spec->n_layers]);
+  return GP_OK;
+}
+
+int finish_launch(cudaStream_t stream, int dev_status_check) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "launch: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (dev_status_check && sync_check_enabled()) {
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "sync: %s", cudaGetErrorString(e));
+    DeviceState* st = nullptr;
+    int rc = get_device_state(&st);
+    if (rc != GP_OK) return rc;
+    int h = 0;
+    e = cudaMemcpy(&h, st->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+    if (h != 0) return set_error(GP_ERR_TIMEOUT, "device wait ran out (status 0x%x)", h);
+  }
+  return GP_OK;
+}
+
+int fused_mlp(const gp_mlp_spec* spec, int64_t m, const void* x, const void* const* w,
+              const void* const* b, const void* gamma, const void* beta, void* out,
+              cudaStream_t stream) {
+  clear_error();
+  int rc = validate(spec, m, x, w, b, gamma, beta, out);
+  if (rc != GP_OK) return rc;
+  const ChainEntry* ent = find_chain(*spec);
+  if (ent == nullptr) {
+    std::string desc;
+    for (int l = 0; l <= spec->n_layers; ++l) desc += std::to_string(spec->widths[l]) + (l < spec->n_layers ? "->" : "");
+    return set_error(GP_ERR_UNSUPPORTED, "no compiled kernel for chain %s (dtype %d, tail %d)",
+                     desc.c_str(), spec->dtype, spec->tail);
+  }
+  if (m == 0) return GP_OK;
+  DeviceState* st = nullptr;
+  rc = get_device_state(&st);
+  if (rc != GP_OK) return rc;
+
+  LaunchCtx c{};
+  c.spec = spec;
+  c.m = m;
+  c.x = x;
+  c.out = out;
+  c.stream = stream;
+  c.sm_count = st->sm_count;
+  c.args.m = m;
+  c.args.num_tiles = static_cast<int>((m + kBM - 1) / kBM);
+  for (int l = 0; l < spec->n_layers; ++l) {
+    c.w[l] = w[l];
+    c.args.bias[l] = b != nullptr ? b[l] : nullptr;
+  }
+  c.args.gamma = gamma;
+  c.args.beta = beta;
+  c.args.resid = x;
+  c.args.ln_eps = spec->ln_eps;
+  c.args.status = st->status;
+  c.args.timeout_ns = g_timeout_ns.load();
+  c.args.inject = g_inject.load();
+  rc = ent->launch(c);
+  if (rc != GP_OK) return rc;
+  return finish_launch(stream, 1);
+}
+
+}  // namespace gp
+
+// ================================================================================================
+// extern "C"
+// ================================================================================================
+using namespace gp;
+
+extern "C" {
+
+int gp_fused_mlp_out(const gp_mlp_spec* spec, int64_t m, const void* x, const void* const* w,
+                     const void* const* b, const void* gamma, const void* beta, void* out,
+                     void* stream) {
+  return fused_mlp(spec, m, x, w, b, gamma, beta, out, static_cast<cudaStream_t>(stream));
+}
+
+static gp_mlp_spec mgn_spec(int k0, int tail, int dtype) {
+  gp_mlp_spec s{};
+  s.n_layers = 3;
+  s.widths[0] = k0;
+  s.widths[1] = s.widths[2] = s.widths[3] = 128;
+  s.act[0] = GP_ACT_RELU;
+  s.act[1] = GP_ACT_RELU;
+  s.act[2] = GP_ACT_NONE;
+  s.tail = tail;
+  s.dtype = dtype;
+  s.ln_eps = 1e-5f;
+  return s;
+}
+
+int gp_mgn_fullmlp_out(int64_t m, int k0, const void* x, const void* w1, const void* b1,
+                       const void* w2, const void* b2, const void* w3, const void* b3,
+                       const void* gamma, const void* beta, void* out, void* stream) {
+  gp_mlp_spec s = mgn_spec(k0, GP_TAIL_LAYERNORM, GP_F16);
+  const void* w[3] = {w1, w2, w3};
+  const void* b[3] = {b1, b2, b3};
+  return fused_mlp(&s, m, x, w, b, gamma, beta, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_mgn_linears_out(int64_t m, int k0, const void* x, const void* w1, const void* b1,
+                       const void* w2, const void* b2, const void* w3, const void* b3, void* out,
+                       void* stream) {
+  gp_mlp_spec s = mgn_spec(k0, GP_TAIL_NONE, GP_F16);
+  const void* w[3] = {w1, w2, w3};
+  const void* b[3] = {b1, b2, b3};
+  return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_testmlp_out(int64_t m, const void* x, const void* w1, const void* b1, const void* w2,
+                   const void* b2, const void* w3, const void* b3, void* out, void* stream) {
+  gp_mlp_spec s = mgn_spec(128, GP_TAIL_NONE, GP_F16);
+  const void* w[3] = {w1, w2, w3};
+  const void* b[3] = {b1, b2, b3};
+  return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+const char* gp_last_error(void) { return t_last_error.c_str(); }
+
+int gp_device_status(int device, int clear, int* status_out) {
+  clear_error();
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  int h = 0;
+  if (rc == GP_OK) {
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&h, st->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(st->status, 0, sizeof(int));
+    if (e == cudaSuccess && clear) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "status: %s", cudaGetErrorString(e));
+  }
+  cudaSetDevice(prev);
+  if (status_out != nullptr) *status_out = h;
+  return rc;
+}
+
+int gp_set_timeout_ns(uint64_t ns) {
+  g_timeout_ns.store(ns == 0 ? 2000000000ull : ns);
+  return GP_OK;
+}
+
+int gp_set_fault_injection(int mode) {
+  if (mode < 0 || mode > 1) return set_error(GP_ERR_ARG, "fault injection mode %d unknown", mode);
+  g_inject.store(mode);
+  return GP_OK;
+}
+
+uint64_t gp_launch_count(void) { return g_launches.load(); }
+
+}  // extern "C"

@@ -1,0 +1,149 @@
+"""Reference-compatible entry points: `cuda_ext.<app>(...)` and `cuda_ext.<app>_out(...)`.
+
+The reference exposes each app as a pybind11 extension, e.g.
+apps/mgn_fullmlp/pipelined/mgn_fullmlp_pl_ext.cu:24-93:
+    mgn_fullmlp_out(x, w1, b1, w2, b2, w3, b3, gamma, beta, out) -> None
+    mgn_fullmlp(x, w1, b1, w2, b2, w3, b3, gamma, beta) -> out
+with weights in [K, N] layout (`linear.weight.t().contiguous()`, apps/mgn_fullmlp/pipelined/val.py:17-19).
+The same names and argument meanings are kept here, so the reference's val.py / perf.py call
+pattern (`ext.cuda_ext.mgn_fullmlp(...)`) works unchanged. Differences, all deliberate:
+  * checks raise RuntimeError (the reference's TORCH_CHECK does too; its width `assert`s abort
+    the process instead),
+  * the launch goes to torch's current stream (the reference uses the legacy default stream),
+  * M need not be a multiple of the reference's `n_rows * mblk`.
+Each call goes through the C ABI (libgpipes.so) with raw device pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float16: L.GP_F16, torch.bfloat16: L.GP_BF16}
+
+
+def _check_input(name: str, t: torch.Tensor | None, dtype: torch.dtype | None = None) -> None:
+    if t is None:
+        return
+    if not isinstance(t, torch.Tensor):
+        raise RuntimeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def fused_mlp_out(x, weights, biases, out, *, acts, tail=L.TAIL_NONE, gamma=None, beta=None,
+                  ln_eps=1e-5) -> None:
+    """Generic chain: out = tail(act_L(... act_1(x W_1 + b_1) ...)). Weights are [K, N]."""
+    _check_input("x", x)
+    dt = _DT.get(x.dtype)
+    if dt is None:
+        raise RuntimeError(f"x must be float16 or bfloat16, got {x.dtype}")
+    for i, (w, b) in enumerate(zip(weights, biases)):
+        _check_input(f"w{i + 1}", w, x.dtype)
+        _check_input(f"b{i + 1}", b, x.dtype)
+    _check_input("gamma", gamma, x.dtype)
+    _check_input("beta", beta, x.dtype)
+    _check_input("out", out, x.dtype)
+    if x.dim() != 2 or out.dim() != 2:
+        raise RuntimeError("x and out must be 2-D")
+    widths = [x.shape[1]] + [w.shape[1] for w in weights]
+    for i, w in enumerate(weights):
+        if w.dim() != 2 or w.shape[0] != widths[i]:
+            raise RuntimeError(f"w{i + 1} has shape {tuple(w.shape)}, expected [{widths[i]}, N]")
+    if out.shape[0] != x.shape[0] or out.shape[1] != widths[-1]:
+        raise RuntimeError(f"out has shape {tuple(out.shape)}, expected [{x.shape[0]}, {widths[-1]}]")
+    spec = L.make_spec(widths, acts, tail, dt, ln_eps)
+    n = len(weights)
+    wp = (ctypes.c_void_p * n)(*[w.data_ptr() for w in weights])
+    bp = (ctypes.c_void_p * n)(*[(b.data_ptr() if b is not None else None) for b in biases])
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_fused_mlp_out(ctypes.byref(spec), x.shape[0], _ptr(x), wp, bp,
+                                         _ptr(gamma), _ptr(beta), _ptr(out), _stream(x)))
+
+
+# ------------------------------------------------------------------------------------------------
+# MeshGraphNet family (apps/mgn_fullmlp, apps/mgn_linears, apps/test_mlp)
+# ------------------------------------------------------------------------------------------------
+def _mgn_checks(x, ws, bs, out, extra=()):
+    _check_input("x", x, torch.float16)
+    for i, (w, b) in enumerate(zip(ws, bs)):
+        _check_input(f"w{i + 1}", w, torch.float16)
+        _check_input(f"b{i + 1}", b, torch.float16)
+    for name, t in extra:
+        _check_input(name, t, torch.float16)
+    _check_input("out", out, torch.float16)
+    k0 = x.shape[1]
+    shapes = [(k0, 128), (128, 128), (128, 128)]
+    for i, (w, shp) in enumerate(zip(ws, shapes)):
+        if tuple(w.shape) != shp:
+            raise RuntimeError(f"w{i + 1} has shape {tuple(w.shape)}, expected {shp}")
+    for i, b in enumerate(bs):
+        if b is not None and tuple(b.shape) != (128,):
+            raise RuntimeError(f"b{i + 1} has shape {tuple(b.shape)}, expected (128,)")
+    if tuple(out.shape) != (x.shape[0], 128):
+        raise RuntimeError(f"out has shape {tuple(out.shape)}, expected ({x.shape[0]}, 128)")
+
+
+def mgn_fullmlp_out(x, w1, b1, w2, b2, w3, b3, gamma, beta, out) -> None:
+    """x [M, K0] (K0 in 128/256/384) -> out [M, 128]; 3 Linear (ReLU, ReLU, none) + LayerNorm."""
+    _mgn_checks(x, (w1, w2, w3), (b1, b2, b3), out, (("gamma", gamma), ("beta", beta)))
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_mgn_fullmlp_out(x.shape[0], x.shape[1], _ptr(x), _ptr(w1), _ptr(b1),
+                                           _ptr(w2), _ptr(b2), _ptr(w3), _ptr(b3), _ptr(gamma),
+                                           _ptr(beta), _ptr(out), _stream(x)))
+
+
+def mgn_fullmlp(x, w1, b1, w2, b2, w3, b3, gamma, beta) -> torch.Tensor:
+    out = torch.zeros(x.shape[0], 128, dtype=x.dtype, device=x.device)
+    mgn_fullmlp_out(x, w1, b1, w2, b2, w3, b3, gamma, beta, out)
+    return out
+
+
+def mgn_linears_out(x, w1, b1, w2, b2, w3, b3, out) -> None:
+    _mgn_checks(x, (w1, w2, w3), (b1, b2, b3), out)
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_mgn_linears_out(x.shape[0], x.shape[1], _ptr(x), _ptr(w1), _ptr(b1),
+                                           _ptr(w2), _ptr(b2), _ptr(w3), _ptr(b3), _ptr(out),
+                                           _stream(x)))
+
+
+def mgn_linears(x, w1, b1, w2, b2, w3, b3) -> torch.Tensor:
+    out = torch.zeros(x.shape[0], 128, dtype=x.dtype, device=x.device)
+    mgn_linears_out(x, w1, b1, w2, b2, w3, b3, out)
+    return out
+
+
+def testmlp_out(x, w1, b1, w2, b2, w3, b3, out) -> None:
+    if x.shape[1] != 128:
+        raise RuntimeError(f"x has {x.shape[1]} columns, expected 128")
+    _mgn_checks(x, (w1, w2, w3), (b1, b2, b3), out)
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_testmlp_out(x.shape[0], _ptr(x), _ptr(w1), _ptr(b1), _ptr(w2),
+                                       _ptr(b2), _ptr(w3), _ptr(b3), _ptr(out), _stream(x)))
+
+
+def testmlp(x, w1, b1, w2, b2, w3, b3) -> torch.Tensor:
+    out = torch.zeros(x.shape[0], 128, dtype=x.dtype, device=x.device)
+    testmlp_out(x, w1, b1, w2, b2, w3, b3, out)
+    return out
+
+
+def run_workload_out(w, x, weights, ln, out) -> None:
+    """Run a workloads.Workload chain through the generic C entry point."""
+    gamma, beta = ln if ln is not None else (None, None)
+    fused_mlp_out(x, [p[0] for p in weights], [p[1] for p in weights], out, acts=w.acts,
+                  tail=w.tail, gamma=gamma, beta=beta, ln_eps=w.ln_eps)

@@ -1,0 +1,136 @@
+/*
+ * gpipes.h -- C ABI of the B200 fused-MLP library (libgpipes.so).
+ *
+ * Each gp_<app>_out entry point replaces one reference launch function: same argument order
+ * (x, then w_i, b_i per layer, then LayerNorm gamma/beta, then out), all caller-owned device
+ * pointers, plus the row count and the caller's CUDA stream. The reference binds these through
+ * pybind11 (`cuda_ext.<app>_out`); a ctypes / cgo / JNI binding of this header is a drop-in.
+ *
+ * Conventions (shared by every entry point):
+ *   - x     [m, K0]        row-major, 16-bit (fp16 unless the entry point takes a dtype)
+ *   - w_l   [K_l, N_l]     row-major, i.e. the transpose of torch.nn.Linear.weight, exactly as the
+ *                          reference passes `weight.t().contiguous()`
+ *                          (apps/mgn_fullmlp/pipelined/val.py:17-19)
+ *   - b_l   [N_l]          16-bit; NULL means "no bias"
+ *   - gamma, beta [N_last] 16-bit LayerNorm affine parameters; NULL means 1 / 0
+ *   - out   [m, N_last]    row-major, 16-bit, written completely
+ *   - x, w_l and out must be 16-byte aligned and their row pitch a multiple of 16 bytes;
+ *     b_l, gamma, beta must be 4-byte aligned.
+ *   - stream is a cudaStream_t (NULL = legacy default stream). Calls are asynchronous.
+ *   - Accumulation is fp32; hidden activations are rounded to the 16-bit input type.
+ *   - m may be 0 (no-op) and need not be a multiple of the 128-row tile.
+ *
+ * Return value: GP_OK or a negative gp_status; gp_last_error() gives a message (thread-local).
+ * Device-side timeouts (a bounded wait that ran out) are reported asynchronously through
+ * gp_device_status(); with the environment variable GP_SYNC_CHECK=1 every call synchronises its
+ * stream and returns GP_ERR_TIMEOUT itself.
+ */
+#ifndef GPIPES_H_
+#define GPIPES_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GP_MAX_LAYERS 10
+
+#if defined(__GNUC__)
+#define GP_API __attribute__((visibility("default")))
+#else
+#define GP_API
+#endif
+
+typedef enum gp_status {
+  GP_OK = 0,
+  GP_ERR_ARG = -1,          /* null pointer or negative size */
+  GP_ERR_SHAPE = -2,        /* widths do not match the entry point */
+  GP_ERR_ALIGN = -3,        /* pointer or pitch violates the alignment rules above */
+  GP_ERR_UNSUPPORTED = -4,  /* no compiled kernel for this layer chain */
+  GP_ERR_CUDA = -5,         /* CUDA runtime / launch error */
+  GP_ERR_TIMEOUT = -6,      /* a device-side bounded wait ran out (kernel aborted cleanly) */
+  GP_ERR_DRIVER = -7        /* TMA descriptor creation failed */
+} gp_status;
+
+typedef enum gp_dtype { GP_F16 = 0, GP_BF16 = 1 } gp_dtype;
+
+typedef enum gp_act {
+  GP_ACT_NONE = 0,
+  GP_ACT_RELU = 1,
+  GP_ACT_GELU_TANH = 2,
+  GP_ACT_SILU = 3,
+  GP_ACT_SIGMOID = 4
+} gp_act;
+
+typedef enum gp_tail {
+  GP_TAIL_NONE = 0,         /* out = act_last(x_L W_L + b_L) */
+  GP_TAIL_LAYERNORM = 1,    /* out = LN(x_L W_L + b_L) */
+  GP_TAIL_RESIDUAL_LN = 2   /* out = LN(x_L W_L + b_L + x) (BERT FFN) */
+} gp_tail;
+
+/* A layer chain. widths[0] is the stored (padded) input width K0; layer l maps widths[l] to
+ * widths[l+1] and applies act[l] (the last layer's act is ignored when tail is a LayerNorm). */
+typedef struct gp_mlp_spec {
+  int n_layers;
+  int widths[GP_MAX_LAYERS + 1];
+  int act[GP_MAX_LAYERS];
+  int tail;         /* gp_tail */
+  int dtype;        /* gp_dtype */
+  float ln_eps;
+} gp_mlp_spec;
+
+/* ---------------------------------------------------------------------------------------------
+ * Generic entry point: any chain for which a kernel is compiled (the per-app functions below
+ * wrap it). No reference counterpart (the reference fixes one chain per app at compile time).
+ * ------------------------------------------------------------------------------------------- */
+GP_API int gp_fused_mlp_out(const gp_mlp_spec* spec, int64_t m, const void* x,
+                     const void* const* w, const void* const* b,
+                     const void* gamma, const void* beta, void* out, void* stream);
+
+/* MeshGraphNet MLP + LayerNorm, fp16, eps 1e-5.
+ * Replaces mgn_fullmlp_out (apps/mgn_fullmlp/pipelined/mgn_fullmlp_pl_ext.cu:24-71), which fixes
+ * k0 = 384; k0 = 256 is the MeshGraphNet node MLP, k0 = 128 also accepted.
+ * Chain: k0 -> 128 (ReLU) -> 128 (ReLU) -> 128, LayerNorm(128). */
+GP_API int gp_mgn_fullmlp_out(int64_t m, int k0, const void* x,
+                       const void* w1, const void* b1, const void* w2, const void* b2,
+                       const void* w3, const void* b3, const void* gamma, const void* beta,
+                       void* out, void* stream);
+
+/* Same chain without the LayerNorm.
+ * Replaces mgn_linears_out (apps/mgn_linears/pipelined/mgn_linears_pl_ext.cu:24-66). */
+GP_API int gp_mgn_linears_out(int64_t m, int k0, const void* x,
+                       const void* w1, const void* b1, const void* w2, const void* b2,
+                       const void* w3, const void* b3, void* out, void* stream);
+
+/* 128 -> 128 (ReLU) -> 128 (ReLU) -> 128, fp16.
+ * Replaces testmlp_out (apps/test_mlp/pipelined/test_mlp_pl_ext.cu:37-82). */
+GP_API int gp_testmlp_out(int64_t m, const void* x,
+                   const void* w1, const void* b1, const void* w2, const void* b2,
+                   const void* w3, const void* b3, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Diagnostics and control (no reference counterpart: the reference has no error reporting).
+ * ------------------------------------------------------------------------------------------- */
+/* Message describing the last error on this thread ("" if none). */
+GP_API const char* gp_last_error(void);
+
+/* Synchronise `device` and read its status word (0 = ok, else a device-side code); with
+ * clear != 0 reset it to 0. Returns GP_OK or GP_ERR_CUDA. */
+GP_API int gp_device_status(int device, int clear, int* status_out);
+
+/* Budget of every device-side wait, in nanoseconds (default 2e9). 0 restores the default. */
+GP_API int gp_set_timeout_ns(uint64_t ns);
+
+/* Fault injection for tests: mode 1 makes the producer skip every input load so the consumers'
+ * bounded waits run out (no GPU fault; the kernel exits with a timeout status). 0 = off. */
+GP_API int gp_set_fault_injection(int mode);
+
+/* Number of kernels this library has launched in this process (for launch-count claims). */
+GP_API uint64_t gp_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPIPES_H_ */

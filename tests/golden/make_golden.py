@@ -1,0 +1,181 @@
+"""Generate the golden fixtures in this directory from the REFERENCE's own PyTorch models.
+
+Run in a checkout that has the reference source tree (default /root/reference, or $GP_REFERENCE):
+    python tests/golden/make_golden.py
+It imports the reference's model classes straight from its sources
+(common/mlps.py MgnMlp/DlrmMlp, apps/bert_ffn/torch/model.py BertFfn,
+apps/gc_edges/torch/model.py GraphCastEdges, apps/nerf_full/torch/model.py Nerf), loads seeded
+weights into them, runs them in fp32 on the CPU and stores inputs and outputs as .npz. It also
+stores the reference's known-answer LayerNorm row (misc_tests/layer_norm/torch_val.py:87-116),
+parsed from that file as text.
+
+Weights are not stored: `layer_params()` below regenerates them bit-exactly from the seed (the
+tests import it), and each fixture keeps a float64 checksum of them to detect drift.
+"""
+from __future__ import annotations
+
+import importlib.util
+import math
+import os
+import re
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent.parent
+
+
+def layer_params(seed: int, dims: list[int], dtype=torch.float16, init="kaiming"):
+    """Seeded [K, N] weights and [N] biases for Linear(dims[i] -> dims[i+1]), rounded to dtype."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for k, n in zip(dims[:-1], dims[1:]):
+        if init == "kaiming":
+            bound = 1.0 / math.sqrt(k)
+            w = (torch.rand(n, k, generator=g) * 2 - 1) * bound
+        elif init == "normal002":
+            w = torch.randn(n, k, generator=g) * 0.02
+        else:
+            bound = math.sqrt(6.0 / (k + n))
+            w = (torch.rand(n, k, generator=g) * 2 - 1) * bound
+        b = (torch.rand(n, generator=g) * 2 - 1) / math.sqrt(k)
+        out.append((w.t().contiguous().to(dtype), b.to(dtype)))
+    return out
+
+
+def checksum(layers) -> float:
+    return float(sum(w.double().sum() + b.double().sum() for w, b in layers))
+
+
+def _load(ref: Path, rel: str, name: str):
+    spec = importlib.util.spec_from_file_location(name, ref / rel)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _set_linear(lin, w_kn, b):
+    with torch.no_grad():
+        lin.weight.copy_(w_kn.float().t())
+        lin.bias.copy_(b.float())
+
+
+def _u16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _save(name: str, **arrays):
+    np.savez_compressed(HERE / f"{name}.npz", **arrays)
+    print("wrote", name, {k: v.shape for k, v in arrays.items()})
+
+
+def main() -> None:
+    ref = Path(os.environ.get("GP_REFERENCE", "/root/reference"))
+    mlps = _load(ref, "common/mlps.py", "ref_mlps")
+    torch.manual_seed(0)
+    rows = 48
+
+    # ---- MgnMlp (common/mlps.py:3-20) in the four shapes the resident kernel serves
+    for name, k0, ln, seed in (("mgn_fullmlp_k384", 384, True, 11), ("mgn_fullmlp_k256", 256, True, 12),
+                               ("mgn_linears_k384", 384, False, 13), ("testmlp_k128", 128, False, 14)):
+        layers = layer_params(seed, [k0, 128, 128, 128])
+        net = mlps.MgnMlp(k0, [128, 128, 128], layernorm=ln).eval()
+        for i, (w, b) in enumerate(layers):
+            _set_linear(net.model[i][0], w, b)
+        g = torch.Generator().manual_seed(seed + 100)
+        x = torch.randn(rows, k0, generator=g).half()
+        gamma = beta = None
+        if ln:
+            gamma = (1 + 0.1 * torch.randn(128, generator=g)).half()
+            beta = (0.1 * torch.randn(128, generator=g)).half()
+            with torch.no_grad():
+                net.model[3].weight.copy_(gamma.float())
+                net.model[3].bias.copy_(beta.float())
+        with torch.no_grad():
+            y = net(x.float())
+        extra = {} if not ln else {"gamma": _u16(gamma), "beta": _u16(beta)}
+        _save(name, seed=np.int64(seed), dims=np.array([k0, 128, 128, 128]), x=_u16(x),
+              y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)), **extra)
+
+    # ---- DlrmMlp (common/mlps.py:23-35): bottom (ReLU everywhere) and top (sigmoid last)
+    for name, dims, sig, seed in (("dlrm_bot", [16, 512, 256, 128], None, 21),
+                                  ("dlrm_top", [480, 1024, 1024, 512, 256, 1], 4, 22)):
+        layers = layer_params(seed, dims, init="xavier")
+        net = mlps.DlrmMlp(dims, sigmoid_i=sig).eval()
+        lins = [m for m in net.model if isinstance(m, torch.nn.Linear)]
+        for lin, (w, b) in zip(lins, layers):
+            _set_linear(lin, w, b)
+        g = torch.Generator().manual_seed(seed + 100)
+        x = torch.randn(rows, dims[0], generator=g).half()
+        with torch.no_grad():
+            y = net(x.float())
+        _save(name, seed=np.int64(seed), dims=np.array(dims), x=_u16(x),
+              y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)),
+              sigmoid_i=np.int64(-1 if sig is None else sig))
+
+    # ---- BertFfn (apps/bert_ffn/torch/model.py:4-15), the reference's own 128/512 ReLU shape
+    bert = _load(ref, "apps/bert_ffn/torch/model.py", "ref_bert")
+    seed = 31
+    layers = layer_params(seed, [128, 512, 128], dtype=torch.bfloat16, init="normal002")
+    net = bert.BertFfn(128, 512).eval()
+    _set_linear(net.ffn[0], *layers[0])
+    _set_linear(net.ffn[2], *layers[1])
+    g = torch.Generator().manual_seed(seed + 100)
+    x = torch.randn(rows, 128, generator=g).bfloat16()
+    with torch.no_grad():
+        y = net(x.float())
+    _save("bert_ffn_128", seed=np.int64(seed), dims=np.array([128, 512, 128]), x=_u16(x),
+          y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
+
+    # ---- GraphCastEdges (apps/gc_edges/torch/model.py:4-14), ReLU as in the reference
+    gc = _load(ref, "apps/gc_edges/torch/model.py", "ref_gc")
+    seed = 41
+    layers = layer_params(seed, [1536, 512, 512], dtype=torch.bfloat16)
+    net = gc.GraphCastEdges().eval()
+    _set_linear(net.mlp[0], *layers[0])
+    _set_linear(net.mlp[2], *layers[1])
+    g = torch.Generator().manual_seed(seed + 100)
+    x = torch.randn(16, 1536, generator=g).bfloat16()
+    with torch.no_grad():
+        y = net(x.float())
+    _save("gc_edges_relu", seed=np.int64(seed), dims=np.array([1536, 512, 512]), x=_u16(x),
+          y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
+
+    # ---- Nerf (apps/nerf_full/torch/model.py:5-66) without view directions, out_ch=4
+    nf = _load(ref, "apps/nerf_full/torch/model.py", "ref_nerf")
+    seed = 51
+    net = nf.Nerf(in_x_ch=63, use_viewdirs=False, out_ch=4).eval()
+    lins = [m for m in list(net.preskip) + list(net.postskip) if isinstance(m, torch.nn.Linear)]
+    lins.append(net.decode)
+    dims_in = [lin.in_features for lin in lins]
+    dims_out = [lin.out_features for lin in lins]
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for lin, k, n in zip(lins, dims_in, dims_out):
+        p = layer_params(int(torch.randint(0, 2**31 - 1, (1,), generator=g)), [k, n])[0]
+        layers.append(p)
+        _set_linear(lin, *p)
+    gx = torch.Generator().manual_seed(seed + 100)
+    x = (torch.rand(rows, 63, generator=gx) * 2 - 1).half()
+    with torch.no_grad():
+        y = net(x.float())
+    _save("nerf_63", seed=np.int64(seed), dims_in=np.array(dims_in), dims_out=np.array(dims_out),
+          x=_u16(x), y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
+
+    # ---- known-answer LayerNorm row from misc_tests/layer_norm/torch_val.py:87-116
+    src = (ref / "misc_tests/layer_norm/torch_val.py").read_text()
+    body = src[src.index("def manual_test"):]
+    lit = body[body.index("torch.tensor([") + len("torch.tensor(["):body.index("]", body.index("torch.tensor(["))]
+    vals = [float(v) for v in re.findall(r"-?\d+\.\d+", lit)]
+    assert len(vals) == 128, len(vals)
+    row = torch.tensor(vals, dtype=torch.float16)
+    y = torch.nn.functional.layer_norm(row.float()[None], [128])[0]
+    _save("ln_known_row", x=_u16(row), y=y.numpy().astype(np.float32))
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, str(ROOT))
+    main()

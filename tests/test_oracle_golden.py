@@ -1,0 +1,99 @@
+"""The CPU oracle (oracle/mlp_oracle.py) against golden outputs of the reference's own PyTorch
+models (tests/golden/*.npz, produced by tests/golden/make_golden.py)."""
+import torch
+
+from tests._util import load_golden, u16_to
+from oracle import mlp_oracle as O
+from tests.golden.make_golden import checksum, layer_params
+
+TOL = dict(atol=2e-5, rtol=1e-5)
+
+
+def _layers(g, dims, dtype=torch.float16, init="kaiming"):
+    layers = layer_params(int(g["seed"]), list(dims), dtype=dtype, init=init)
+    assert abs(checksum(layers) - float(g["wsum"])) < 1e-6, "weight generator drifted"
+    return layers
+
+
+def test_mgn_fullmlp_matches_reference_model():
+    for name in ("mgn_fullmlp_k384", "mgn_fullmlp_k256"):
+        g = load_golden(name)
+        layers = _layers(g, g["dims"])
+        x = u16_to(g["x"], torch.float16)
+        ln = (u16_to(g["gamma"], torch.float16), u16_to(g["beta"], torch.float16))
+        y = O.chain_forward(x, layers, [O.ACT_RELU, O.ACT_RELU, O.ACT_NONE], O.TAIL_LAYERNORM, ln, 1e-5)
+        torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+        torch.testing.assert_close(O.mgn_mlp(x, layers, ln), torch.from_numpy(g["y"]), **TOL)
+
+
+def test_mgn_linears_and_testmlp_match_reference_model():
+    for name in ("mgn_linears_k384", "testmlp_k128"):
+        g = load_golden(name)
+        layers = _layers(g, g["dims"])
+        x = u16_to(g["x"], torch.float16)
+        y = O.chain_forward(x, layers, [O.ACT_RELU, O.ACT_RELU, O.ACT_NONE])
+        torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+
+
+def test_dlrm_matches_reference_model():
+    for name in ("dlrm_bot", "dlrm_top"):
+        g = load_golden(name)
+        layers = _layers(g, g["dims"], init="xavier")
+        x = u16_to(g["x"], torch.float16)
+        sig = int(g["sigmoid_i"])
+        y = O.dlrm_mlp(x, layers, None if sig < 0 else sig)
+        torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+        acts = [O.ACT_SIGMOID if i == sig else O.ACT_RELU for i in range(len(layers))]
+        torch.testing.assert_close(O.chain_forward(x, layers, acts), torch.from_numpy(g["y"]), **TOL)
+
+
+def test_bert_ffn_matches_reference_model():
+    g = load_golden("bert_ffn_128")
+    layers = _layers(g, g["dims"], dtype=torch.bfloat16, init="normal002")
+    x = u16_to(g["x"], torch.bfloat16)
+    ln = (torch.ones(128), torch.zeros(128))
+    y = O.bert_ffn(x, layers, ln, act_id=O.ACT_RELU, ln_eps=1e-5)
+    torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+    y2 = O.chain_forward(x, layers, [O.ACT_RELU, O.ACT_NONE], O.TAIL_RESIDUAL_LN, ln, 1e-5)
+    torch.testing.assert_close(y2, torch.from_numpy(g["y"]), **TOL)
+
+
+def test_gc_edges_matches_reference_model():
+    g = load_golden("gc_edges_relu")
+    layers = _layers(g, g["dims"], dtype=torch.bfloat16)
+    x = u16_to(g["x"], torch.bfloat16)
+    ln = (torch.ones(512), torch.zeros(512))
+    y = O.gc_edges(x, layers, ln, act_id=O.ACT_RELU)
+    torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+
+
+def test_nerf_matches_reference_model():
+    g = load_golden("nerf_63")
+    gen = torch.Generator().manual_seed(int(g["seed"]))
+    layers = []
+    for k, n in zip(g["dims_in"], g["dims_out"]):
+        s = int(torch.randint(0, 2**31 - 1, (1,), generator=gen))
+        layers.append(layer_params(s, [int(k), int(n)])[0])
+    assert abs(checksum(layers) - float(g["wsum"])) < 1e-6
+    x = u16_to(g["x"], torch.float16)
+    y = O.nerf(x, layers, skip=4)
+    torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+
+
+def test_layernorm_known_row():
+    """misc_tests/layer_norm/torch_val.py:87-116: one 128-value row, gamma=1, beta=0."""
+    g = load_golden("ln_known_row")
+    x = u16_to(g["x"], torch.float16).float()[None]
+    y = O.layernorm(x, None, None, 1e-5)[0]
+    torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
+
+
+def test_compare_thresholds():
+    e = torch.randn(1000, 64)
+    assert O.compare(e + 1e-4, e)["ok"]
+    bad = e.clone()
+    bad[3, 7] += 0.5
+    assert not O.compare(bad, e)["ok"]
+    nan = e.clone()
+    nan[0, 0] = float("nan")
+    assert not O.compare(nan, e)["ok"]
