@@ -1,0 +1,324 @@
+"""Benchmark of the fused-MLP hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+A step is one pass of the fused MLP over one batch: M rows of the configured workload (default
+`mgn_node`: MeshGraphNet node MLP, 1,048,576 rows, 256->128->128->128 + LayerNorm, fp16 -- the
+second benchmark config, the one the headline metric is quoted on that fits one GPU).
+
+Multi-GPU (torchrun, one process per GPU): rows are independent, so each rank runs its own
+M-row slice of an N*M-row job (weak scaling, no collective on the data path; NCCL is used only
+for the barrier and the max-over-ranks of the timing).
+
+Reported:
+  value       rows/s over all ranks, inputs already resident in HBM, CUDA-event timed
+  e2e         same metric through the public API with the host->device copy of x (pinned) and
+              the device->host copy of the output inside every timed step
+  roofline    the fused kernel against the measured HBM bandwidth (the path is HBM-bound:
+              768 B/row vs 131,072 FLOP/row, arithmetic intensity 171 < ridge 253)
+  cpu_baseline the CPU oracle (the reference's PyTorch fp32 model, restated) on a bounded sample
+  clocks      nvidia-smi samples taken during the timed region
+
+`--impl reference` times the reference's CPU implementation (PyTorch fp32 model, restated in
+oracle/) on this host with all cores, on the same config and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+import __graft_entry__  # noqa: E402
+
+__graft_entry__.load_package()
+from gpu_pipes_b200 import _lib as L  # noqa: E402
+from gpu_pipes_b200 import workloads as W  # noqa: E402
+
+L2_BYTES = 126 * 2**20
+# DRAM bytes (read + write) per launch of the fused kernel from one ncu capture, per row,
+# keyed by workload (profiles/mlp_resident_mgn_node.md). None until measured.
+NCU_TRAFFIC_PER_ROW = {"mgn_node": None, "mgn_edge": None}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--config", default="mgn_node", choices=sorted(W.WORKLOADS))
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--m", type=int, default=0, help="override rows per GPU (testing only)")
+    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--cpu-seconds", type=float, default=8.0)
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_oracle_rate(w, seconds: float) -> dict:
+    """The CPU oracle on whole 65,536-row chunks for about `seconds` (at least one chunk)."""
+    from oracle import mlp_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    layers, ln = W.make_weights(w)
+    x = W.make_input_chunk(w, 0)
+    O.workload_forward(w, x[:4096], layers, ln)  # warm-up
+    rows, t0 = 0, time.perf_counter()
+    while True:
+        O.workload_forward(w, x, layers, ln)
+        rows += x.shape[0]
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": rows / dt, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} rows of {w.name} in {rows // W.CHUNK_ROWS} x 65,536-row chunks, "
+                      f"fp32 PyTorch on the host ({dt:.1f} s)"}
+
+
+def run_reference(args, w, rank: int):
+    """Reference arm: the reference's PyTorch fp32 model (restated in oracle/) on the CPU."""
+    if rank != 0:
+        return
+    from oracle import mlp_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    layers, ln = W.make_weights(w)
+    # size each step so the whole run takes about a minute
+    x_cal = W.make_input(w, 0, 4096)
+    t0 = time.perf_counter()
+    O.workload_forward(w, x_cal, layers, ln)
+    per_row = (time.perf_counter() - t0) / 4096
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    rows = int(min(w.m, max(256, budget / max(per_row, 1e-9))))
+    x = W.make_input(w, 0, rows)
+    for _ in range(args.warmup):
+        O.workload_forward(w, x, layers, ln)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.workload_forward(w, x, layers, ln)
+    dt = time.perf_counter() - t0
+    val = rows * args.steps / dt
+    line = {
+        "impl": "reference", "metric": "fused-MLP rows/s", "value": val, "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "rows_per_step_sampled": rows, "rows_per_gpu": w.m,
+                   "chain": w.widths, "description": w.description},
+        "tflops": val * w.flop_per_row / 1e12,
+        "cpu_baseline": {"value": val, "unit": "rows/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{rows} rows per step of {w.name}, PyTorch fp32 on the host"},
+        "e2e": {"value": val, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    base = W.WORKLOADS[args.config]
+    w = base.with_m(args.m) if args.m else base
+
+    if args.impl == "reference":
+        run_reference(args, w, rank)
+        return
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+    from gpu_pipes_b200 import cuda_ext
+
+    # ---- data: rank r owns rows [r*M, (r+1)*M) of the N*M-row job
+    row0 = rank * w.m
+    x_host = W.make_input(w.with_m(row0 + w.m), row0, w.m).pin_memory()
+    layers, ln = W.make_weights(w)
+    x = x_host.to(dev)
+    wd = [(a.to(dev), b.to(dev)) for a, b in layers]
+    lnd = None if ln is None else tuple(t.to(dev) for t in ln)
+    out = torch.empty(w.m, w.n_out, dtype=w.dtype, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        cuda_ext.run_workload_out(w, x, wd, lnd, out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.25)
+    launches0 = L.launch_count()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    launches = L.launch_count() - launches0
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    rows_total = w.m * world
+    value = rows_total / (ms_step / 1e3)
+
+    # ---- end to end through the public API: pinned host x -> device -> kernel -> host out
+    out_host = torch.empty(w.m, w.n_out, dtype=w.dtype).pin_memory()
+    x_dev2 = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev2.copy_(x_host, non_blocking=True)
+        cuda_ext.run_workload_out(w, x_dev2, wd, lnd, out)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_value = rows_total / (e_ms / args.e2e_steps / 1e3)
+
+    status = L.device_status(local)
+    hbm_gbs, tflops_peak, peak_src = measured_peaks()
+    alg_bytes = w.m * w.bytes_per_row  # per launch
+    achieved = alg_bytes / (ms_step / 1e3) / 1e9
+    tr = NCU_TRAFFIC_PER_ROW.get(w.name)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_oracle_rate(w, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": "fused-MLP rows/s", "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16" if w.dtype == torch.float16 else "bf16", "data": "synthetic",
+            "config": {"workload": w.name, "rows_per_gpu": w.m, "global_rows": rows_total,
+                       "chain": w.widths, "tail": ["none", "layernorm", "residual+layernorm"][w.tail],
+                       "description": w.description,
+                       "l2": "inputs larger than L2 (x %d MB + out %d MB per GPU > 126 MB)" % (
+                           w.m * w.k0 * 2 >> 20, w.m * w.n_out * 2 >> 20),
+                       "parallelism": f"rows sharded over {world} GPU(s), weights replicated"},
+            "tflops": value * w.flop_per_row / 1e12,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
+                         "frac": achieved / hbm_gbs,
+                         "traffic": None if tr is None else tr * w.m,
+                         "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)",
+                         "kernel": "mlp_resident_kernel",
+                         "algorithmic_bytes_per_launch": alg_bytes},
+            "e2e": {"value": e2e_value, "unit": "rows/s",
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
