@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=8.0)
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--kernel-only", action="store_true",
+                   help="time the kernel only (no e2e, CPU baseline or clock sampling); for ncu")
     return p.parse_args()
 
 
@@ -232,8 +234,9 @@ def main():
         torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.25)
+    if not args.kernel_only:
+        sampler.start()
+        time.sleep(0.25)
     launches0 = L.launch_count()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -252,6 +255,14 @@ def main():
     ms_step = ms / args.steps
     rows_total = w.m * world
     value = rows_total / (ms_step / 1e3)
+
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"workload": w.name, "rows_per_gpu": w.m, "ms_per_step": ms_step,
+                              "rows_per_s": value, "gpu_launches": launches}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     # ---- end to end through the public API: pinned host x -> device -> kernel -> host out
     out_host = torch.empty(w.m, w.n_out, dtype=w.dtype).pin_memory()
