@@ -36,8 +36,9 @@ const ChainEntry* find_chain(const gp_mlp_spec& s);
 
 // helpers implemented in gp_abi.cu
 int set_error(int code, const char* fmt, ...);
+// swizzle_bytes: 128, 64, 32 or 0 (none)
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
-                 uint32_t box_cols, uint32_t box_rows);
+                 uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
 // Sets the dynamic shared memory attribute of `kern` once per device.
 int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask);

@@ -26,6 +26,7 @@ enum DeviceStatus : int {
   kDevTimeoutMma = 0x200,       // MMA issuer gave up waiting for operands
   kDevTimeoutEpilogue = 0x300,  // epilogue gave up waiting for an accumulator
   kDevTimeoutWeights = 0x400,   // weight staging never completed
+  kDevBadSmemAlign = 0x500,     // dynamic shared memory not 1024-byte aligned
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -67,6 +68,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       "{\n\t"
       ".reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe of a phase (no suspend).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t"
       "}\n"
       : "=r"(ok)
@@ -262,6 +278,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// 32 lanes x 32 bits, 8 consecutive columns.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------
 // UMMA descriptors
 // ------------------------------------------------------------------------------------------------
@@ -303,9 +327,16 @@ struct Elem;
 template <>
 struct Elem<__half> {
   static constexpr int kIsBf16 = 0;
+  static constexpr uint32_t kOneLow = 0x3C00u;  // 1.0 in the low half, 0 in the high half
   __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  __device__ __forceinline__ static uint32_t pack_relu(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
   }
   __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
 };
@@ -313,9 +344,16 @@ struct Elem<__half> {
 template <>
 struct Elem<__nv_bfloat16> {
   static constexpr int kIsBf16 = 1;
+  static constexpr uint32_t kOneLow = 0x3F80u;
   __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  __device__ __forceinline__ static uint32_t pack_relu(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
   }
   __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 };

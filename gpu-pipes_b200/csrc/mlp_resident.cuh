@@ -1,4 +1,5 @@
-// Fused MLP chain with weights resident in shared memory ("narrow" chains: hidden width <= 128).
+// Fused MLP chain with weights resident in shared memory ("narrow" chains: every layer 128 wide
+// or less after the first).
 //
 // Covers the reference apps whose every layer is at most 128 wide:
 //   mgn_fullmlp  apps/mgn_fullmlp/pipelined/mgn_fullmlp_pl.cuh:205-252   384->128->128->128 + LN
@@ -10,24 +11,28 @@
 // CTAs through L2-resident ring queues (common/mpmcq.cuh, common/pipes.cuh), this kernel runs the
 // whole chain for a 128-row tile inside one persistent CTA:
 //
-//   warp 0      TMA producer: all weights once (smem-resident for the CTA's lifetime), then the
-//               x tiles as 128x64 K panels through an mbarrier ring.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2-9   two epilogue groups of four warps (one per TMEM accumulator buffer); thread t of a
-//               group owns row t of its tile (TMEM lane t).
+//   warp 0        TMA producer: all weights once (smem-resident for the CTA's lifetime), then the
+//                 x tiles as 128x64 K panels through an mbarrier ring.
+//   warp 1        TMEM allocator + single-thread tcgen05.mma issuer.
+//   warps 2..     NBUF epilogue groups of four warps (one per TMEM accumulator buffer); thread t
+//                 of a group owns row t of its tile (TMEM lane t).
 //
-// Two row tiles are in flight (TMEM buffers b = 0, 1), so the tensor core works on one tile while
-// the epilogue of the other runs. Per buffer (256 TMEM columns):
-//   cols [0, N)          fp32 accumulator of the current layer
-//   cols [128, 128+N/2)  16-bit activation of the previous layer, two values per column; it is the
-//                        A operand (tcgen05.mma A-from-TMEM) of the next layer.
-// Hidden activations therefore never leave the SM: HBM traffic is x, the weights once per CTA,
-// and the final output.
+// With NBUF = 2, two row tiles are in flight, so the tensor core works on one tile while the
+// epilogue of the other runs; the MMA thread picks whichever buffer's next job is ready (no
+// head-of-line blocking on an x panel still in flight). TMEM columns:
+//   buffer b: [256b, 256b+N)        fp32 accumulator of the current layer
+//             [256b+128, +N/2)      16-bit activation of the previous layer, two values per
+//                                   column: the A operand (A-from-TMEM) of the next layer
+//   [192, 200)                      the "ones" operand: row r = (1, 0, ..., 0) over 16 K elements
+//
+// Bias: each layer starts with one extra K=16 MMA, A = ones (TMEM) x B = bias slice (smem, row 0 =
+// bias, rows 1..15 multiplied by zero), so the accumulator already holds x W + b and the epilogue
+// does no bias arithmetic. Hidden layers then need one cvt (with ReLU) per pair of values.
 //
 // Layer 0 is A[smem x panel, K-major SW128] x B[smem W, N-major SW128]; layers >= 1 are
-// A[TMEM activation] x B[smem W]. The epilogue of the last layer applies bias, activation or
-// LayerNorm (thread-local: one thread holds one full row) and stores through a per-warp swizzled
-// staging buffer with TMA.
+// A[TMEM activation] x B[smem W]. The epilogue of the last layer applies the activation or the
+// LayerNorm (thread-local: one thread holds one full row; packed f32x2 arithmetic) and stores
+// through a per-warp 32x32 swizzled (SW64) staging tile with TMA.
 #pragma once
 
 #include "chain_common.cuh"
@@ -35,35 +40,40 @@
 
 namespace gp {
 
-template <int K0_, int N_, int NL_>
+template <int K0_, int N_, int NL_, int NBUF_>
 struct ResidentLayout {
-  static constexpr int K0 = K0_, N = N_, NL = NL_;
+  static constexpr int K0 = K0_, N = N_, NL = NL_, NBUF = NBUF_;
   static_assert(K0 % kPanel == 0 && K0 >= kPanel, "K0 must be a multiple of 64");
   static_assert(N % kPanel == 0 && N >= 64 && N <= 128, "hidden width must be 64 or 128");
   static_assert(NL >= 1 && NL <= kMaxLayers, "layer count");
+  static_assert(NBUF == 1 || NBUF == 2, "one or two tiles in flight");
   static constexpr int kW0Bytes = K0 * N * 2;
   static constexpr int kWhBytes = N * N * 2;
   static constexpr int kWBytes = kW0Bytes + (NL - 1) * kWhBytes;
-  static constexpr int kStageBytes = 32 * 128;  // per epilogue warp: 32 rows x 64 cols x 2 B
-  static constexpr int kNumEpiWarps = 8;
+  static constexpr int kBiasBytes = NL * (N / 64) * 1024 + 1024;  // + one trailing zero atom
+  static constexpr int kNumEpiWarps = 4 * NBUF;
+  static constexpr int kStageBytes = 32 * 64;  // per epilogue warp: 32 rows x 32 cols x 2 B
   static constexpr int kStgBytes = kNumEpiWarps * kStageBytes;
+  static constexpr int kLnBytes = 2 * N * 4;  // fp32 gamma, beta
   static constexpr int kBarBytes = 256;
-  static constexpr int kAlignSlack = 1024;
-  static constexpr int kXStagesRaw =
-      (kSmemLimit - kAlignSlack - kBarBytes - kWBytes - kStgBytes) / kPanelBytes;
+  static constexpr int kFixed = kWBytes + kBiasBytes + kStgBytes + kLnBytes + kBarBytes;
+  static constexpr int kXStagesRaw = (kSmemLimit - kFixed) / kPanelBytes;
   static constexpr int kXStages = kXStagesRaw > 8 ? 8 : kXStagesRaw;
   static_assert(kXStages >= 2, "weights do not fit in shared memory");
-  // offsets from the 1024-aligned base
+  // offsets from the (1024-aligned) dynamic shared memory base
   static constexpr int kOffW = 0;
   static constexpr int kOffX = kOffW + kWBytes;
-  static constexpr int kOffStg = kOffX + kXStages * kPanelBytes;
-  static constexpr int kOffBar = kOffStg + kStgBytes;
-  static constexpr int kSmemBytes = kOffBar + kBarBytes + kAlignSlack;
+  static constexpr int kOffBias = kOffX + kXStages * kPanelBytes;
+  static constexpr int kOffStg = kOffBias + kBiasBytes;
+  static constexpr int kOffLn = kOffStg + kStgBytes;
+  static constexpr int kOffBar = kOffLn + kLnBytes;
+  static constexpr int kSmemBytes = kOffBar + kBarBytes;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
-  static constexpr int kThreads = 320;
+  static constexpr int kThreads = 64 + 32 * kNumEpiWarps;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kBufCols = 256;
   static constexpr int kActCol = 128;
+  static constexpr int kOnesCol = 192;
 };
 
 __device__ __forceinline__ uint32_t w_layer_offset(int l, int w0_bytes, int wh_bytes) {
@@ -73,122 +83,117 @@ __device__ __forceinline__ uint32_t w_layer_offset(int l, int w0_bytes, int wh_b
 // ------------------------------------------------------------------------------------------------
 // Epilogue pieces. `v` holds one row's fp32 accumulators (thread = row), 32 columns per block.
 // ------------------------------------------------------------------------------------------------
-template <int ACT>
-__device__ __forceinline__ float act_c(float v) {
-  return apply_act(ACT, v);
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t act_pack(float lo, float hi) {
+  if constexpr (ACT == kActRelu) {
+    return Elem<T>::pack_relu(lo, hi);
+  } else {
+    return Elem<T>::pack(apply_act(ACT, lo), apply_act(ACT, hi));
+  }
 }
 
-template <typename T>
-__device__ __forceinline__ void unpack2(uint32_t bits, float& lo, float& hi) {
-  lo = Elem<T>::to_f(*reinterpret_cast<const T*>(&bits));
-  hi = Elem<T>::to_f(*(reinterpret_cast<const T*>(&bits) + 1));
-}
-
-// bias + activation, packed to 16 bits and written to TMEM (two values per column).
+// activation, packed to 16 bits and written to TMEM (two values per column).
 template <typename T, int N, int ACT>
-__device__ __forceinline__ void epi_hidden(const uint32_t (&v)[N / 32][32], const uint32_t* bias2,
-                                           uint32_t t_act) {
+__device__ __forceinline__ void epi_hidden(const uint32_t (&v)[N / 32][32], uint32_t t_act) {
 #pragma unroll
   for (int c = 0; c < N / 32; ++c) {
     uint32_t pk[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float b0 = 0.f, b1 = 0.f;
-      if (bias2 != nullptr) unpack2<T>(__ldg(bias2 + c * 16 + j), b0, b1);
-      pk[j] = Elem<T>::pack(act_c<ACT>(__uint_as_float(v[c][2 * j]) + b0),
-                            act_c<ACT>(__uint_as_float(v[c][2 * j + 1]) + b1));
-    }
+    for (int j = 0; j < 16; ++j)
+      pk[j] = act_pack<T, ACT>(__uint_as_float(v[c][2 * j]), __uint_as_float(v[c][2 * j + 1]));
     tmem_st16(t_act + c * 16, pk);
   }
 }
 
-template <typename T, int N>
-__device__ __forceinline__ void epi_bias(const uint32_t (&v)[N / 32][32], const uint32_t* bias2,
-                                         float (&y)[N]) {
+// Mean and rstd of one row (one-pass sum / sum of squares in fp32, four f32x2 chains).
+template <int N>
+__device__ __forceinline__ void row_stats(const uint32_t (&v)[N / 32][32], float eps, float& mean,
+                                          float& rstd) {
+  float2 s[4], q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    s[i] = make_float2(0.f, 0.f);
+    q[i] = make_float2(0.f, 0.f);
+  }
 #pragma unroll
   for (int c = 0; c < N / 32; ++c)
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      float b0 = 0.f, b1 = 0.f;
-      if (bias2 != nullptr) unpack2<T>(__ldg(bias2 + c * 16 + j), b0, b1);
-      y[c * 32 + 2 * j] = __uint_as_float(v[c][2 * j]) + b0;
-      y[c * 32 + 2 * j + 1] = __uint_as_float(v[c][2 * j + 1]) + b1;
+      const float2 p = make_float2(__uint_as_float(v[c][2 * j]), __uint_as_float(v[c][2 * j + 1]));
+      s[j & 3] = __fadd2_rn(s[j & 3], p);
+      q[j & 3] = __ffma2_rn(p, p, q[j & 3]);
     }
+  const float2 s01 = __fadd2_rn(__fadd2_rn(s[0], s[1]), __fadd2_rn(s[2], s[3]));
+  const float2 q01 = __fadd2_rn(__fadd2_rn(q[0], q[1]), __fadd2_rn(q[2], q[3]));
+  mean = (s01.x + s01.y) * (1.0f / N);
+  const float var = fmaxf((q01.x + q01.y) * (1.0f / N) - mean * mean, 0.0f);
+  rstd = rsqrtf(var + eps);
 }
 
-template <int N, int ACT>
-__device__ __forceinline__ void apply_act_row(float (&y)[N]) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) y[i] = act_c<ACT>(y[i]);
+template <typename T, int ACT>
+__device__ __forceinline__ uint32_t act_pack_f2(float2 y) {
+  return act_pack<T, ACT>(y.x, y.y);
 }
 
-// LayerNorm of one row held entirely by this thread: biased variance, two passes
-// (mean, then squared deviations), as torch.nn.LayerNorm and common/layer_norm_v2.cuh:34-68.
-template <typename T, int N>
-__device__ __forceinline__ void row_layernorm(float (&y)[N], const void* gamma, const void* beta,
-                                              float eps) {
-  float sum = 0.f;
+// Write 32 values of this thread's row (c32 = 32-column block) into a 32-row x 64-byte staging
+// tile with the TMA SWIZZLE_64B pattern (16-byte chunk j of row r lands at j ^ ((r >> 1) & 3)),
+// applying the tail: LayerNorm (mean/rstd/gamma/beta) or the activation.
+template <typename T, int TAIL, int ACT>
+__device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint32_t (&vc)[32],
+                                              const float* ln_g, const float* ln_b, float rstd,
+                                              float nmr) {
 #pragma unroll
-  for (int i = 0; i < N; ++i) sum += y[i];
-  const float mean = sum * (1.0f / N);
-  float sq = 0.f;
+  for (int j = 0; j < 4; ++j) {
+    uint32_t pk[4];
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    const float d = y[i] - mean;
-    sq += d * d;
-  }
-  const float rstd = rsqrtf(sq * (1.0f / N) + eps);
-  const uint32_t* g2 = reinterpret_cast<const uint32_t*>(gamma);
-  const uint32_t* be2 = reinterpret_cast<const uint32_t*>(beta);
-#pragma unroll
-  for (int i = 0; i < N / 2; ++i) {
-    float g0 = 1.f, g1 = 1.f, e0 = 0.f, e1 = 0.f;
-    if (g2 != nullptr) unpack2<T>(__ldg(g2 + i), g0, g1);
-    if (be2 != nullptr) unpack2<T>(__ldg(be2 + i), e0, e1);
-    y[2 * i] = (y[2 * i] - mean) * rstd * g0 + e0;
-    y[2 * i + 1] = (y[2 * i + 1] - mean) * rstd * g1 + e1;
-  }
-}
-
-// Write 64 values of this thread's row into a 32-row x 128-byte staging tile with the TMA
-// SWIZZLE_128B pattern (16-byte chunk j of row r lands at chunk j ^ (r % 8)).
-template <typename T>
-__device__ __forceinline__ void stage_row_chunk64(uint8_t* stg, int lane, const float* y) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint4 pk;
-    pk.x = Elem<T>::pack(y[j * 8 + 0], y[j * 8 + 1]);
-    pk.y = Elem<T>::pack(y[j * 8 + 2], y[j * 8 + 3]);
-    pk.z = Elem<T>::pack(y[j * 8 + 4], y[j * 8 + 5]);
-    pk.w = Elem<T>::pack(y[j * 8 + 6], y[j * 8 + 7]);
-    *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) * 16)) = pk;
+    for (int e = 0; e < 4; ++e) {
+      const int i = j * 8 + e * 2;  // column within the 32-block
+      float2 y = make_float2(__uint_as_float(vc[i]), __uint_as_float(vc[i + 1]));
+      if constexpr (TAIL == kTailLayerNorm) {
+        const float2 g = *reinterpret_cast<const float2*>(ln_g + i);
+        const float2 b = *reinterpret_cast<const float2*>(ln_b + i);
+        y = __ffma2_rn(y, make_float2(rstd, rstd), make_float2(nmr, nmr));  // (v - mean) * rstd
+        y = __ffma2_rn(y, g, b);
+        pk[e] = Elem<T>::pack(y.x, y.y);
+      } else {
+        pk[e] = act_pack_f2<T, ACT>(y);
+      }
+    }
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) =
+        make_uint4(pk[0], pk[1], pk[2], pk[3]);
   }
 }
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL>
-__global__ void __launch_bounds__(320, 1)
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF>
+__global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
     mlp_resident_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
-  using L = ResidentLayout<K0, N, NL>;
+  using L = ResidentLayout<K0, N, NL, NBUF>;
   constexpr int kXS = L::kXStages;
   constexpr int kPanels0 = K0 / kPanel;
   constexpr uint32_t kIdesc = make_idesc_f16(kBM, N, Elem<T>::kIsBf16, 0, 1);
+  constexpr int kLastAct = static_cast<int>((ACTS >> (4 * (NL - 1))) & 15u);
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  // barrier slots
-  uint64_t* x_full = bars;                // [kXS]
-  uint64_t* x_empty = bars + 8;           // [kXS]
-  uint64_t* w_full = bars + 16;           // [1]
-  uint64_t* acc_full = bars + 17;         // [2]
-  uint64_t* act_ready = bars + 19;        // [2]
-  uint64_t* mma_done = bars + 21;         // [1]
+  uint64_t* x_full = bars;         // [kXS]
+  uint64_t* x_empty = bars + 8;    // [kXS]
+  uint64_t* w_full = bars + 16;    // [1]
+  uint64_t* acc_full = bars + 17;  // [NBUF]
+  uint64_t* act_ready = bars + 19; // [NBUF]
+  uint64_t* mma_done = bars + 21;  // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+  float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
+  float* ln_b = ln_g + N;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+
+  // the swizzled operand layouts assume a 1024-byte aligned shared window
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXS; ++s) {
@@ -196,7 +201,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(smem_u32(&x_empty[s]), 1);
     }
     mbar_init(smem_u32(w_full), 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&act_ready[b]), 4);
     }
@@ -212,10 +217,40 @@ __global__ void __launch_bounds__(320, 1)
     tmem_alloc(smem_u32(tmem_holder), L::kTmemCols);
     tmem_relinquish();
   }
+  // bias slices (row 0 of each 8-row x 128-byte atom; rows 1..7 and a trailing atom are zero)
+  // and the LayerNorm parameters in fp32
+  for (int i = threadIdx.x; i < L::kBiasBytes / 16; i += blockDim.x) {
+    const int atom = i >> 6, chunk = i & 63;  // 64 chunks of 16 B per atom
+    uint4 val = make_uint4(0, 0, 0, 0);
+    const int l = atom / (N / 64), nb = atom % (N / 64);
+    if (chunk < 8 && l < NL && args.bias[l] != nullptr) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(args.bias[l]) + (nb * 8 + chunk) * 4;
+      val = make_uint4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+    }
+    *reinterpret_cast<uint4*>(smem + L::kOffBias + i * 16) = val;
+  }
+  if constexpr (TAIL == kTailLayerNorm) {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+      const T* g = reinterpret_cast<const T*>(args.gamma);
+      const T* b = reinterpret_cast<const T*>(args.beta);
+      ln_g[i] = g != nullptr ? Elem<T>::to_f(g[i]) : 1.0f;
+      ln_b[i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
+    }
+  }
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (warp >= 2 && warp < 6) {
+    // the ones operand: lane r, column 192 = (1.0, 0.0), columns 193..199 = 0
+    uint32_t ones[8] = {Elem<T>::kOneLow, 0, 0, 0, 0, 0, 0, 0};
+    tmem_st8(tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + L::kOnesCol, ones);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
   const int num_tiles = args.num_tiles;
@@ -229,7 +264,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll 1
       for (int l = 0; l < NL; ++l) {
         const int kl = l == 0 ? K0 : N;
-        const uint32_t wbase = smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
+        const uint32_t wbase =
+            smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
         for (int kp = 0; kp < kl / kPanel; ++kp)
           for (int nb = 0; nb < N / kPanel; ++nb)
             tma_load_2d_hint(wbase + nb * (kl * 128) + kp * (kPanel * 128), &tm.w[l],
@@ -241,7 +277,8 @@ __global__ void __launch_bounds__(320, 1)
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
 #pragma unroll 1
         for (int p = 0; p < kPanels0; ++p) {
-          if (!mbar_wait(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer)) goto producer_done;
+          if (!mbar_wait(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer))
+            goto producer_done;
           if (!args.inject) {
             mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
             tma_load_2d_hint(smem_u32(smem + L::kOffX + s * kPanelBytes), &tm.x,
@@ -260,73 +297,99 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const uint32_t wsm = smem_u32(smem + L::kOffW);
       const uint32_t xsm = smem_u32(smem + L::kOffX);
+      const uint32_t bsm = smem_u32(smem + L::kOffBias);
+      const uint32_t ones = tmem_base + L::kOnesCol;
       int s = 0;
       uint32_t ph = 0;
-      uint32_t ready_ph[2] = {0, 0};
-      bool first[2] = {true, true};
+      // per-buffer job cursor: local tile index (tiles j with j % NBUF == b) and layer
+      int jt[NBUF], jl[NBUF];
+      uint32_t ready_ph[NBUF];
+      bool first[NBUF];
+      for (int b = 0; b < NBUF; ++b) { jt[b] = b; jl[b] = 0; ready_ph[b] = 0; first[b] = true; }
+      int next_l0 = 0;  // local tile whose layer 0 consumes the x ring next (ring order)
+      uint64_t idle_since = 0;
+      int prefer = 0;
 #pragma unroll 1
-      for (int pair = blockIdx.x; ok && pair < num_tiles; pair += 2 * gridDim.x) {
+      while (ok) {
+        bool any_left = false, issued = false;
 #pragma unroll 1
-        for (int l = 0; ok && l < NL; ++l) {
-#pragma unroll 1
-          for (int b = 0; ok && b < 2; ++b) {
-            const int tile = pair + b * gridDim.x;
-            if (tile >= num_tiles) continue;
-            if (!first[b]) {
-              if (!mbar_wait(smem_u32(&act_ready[b]), ready_ph[b], wctx, kDevTimeoutMma)) { ok = false; break; }
-              ready_ph[b] ^= 1;
-            }
-            first[b] = false;
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + b * L::kBufCols;
-            if (l == 0) {
-              for (int p = 0; p < kPanels0; ++p) {
-                if (!mbar_wait(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
-                tc_fence_after();
-                const uint64_t adesc = make_sdesc_sw128(xsm + s * kPanelBytes, 16, 1024);
+        for (int bi = 0; bi < NBUF && !issued; ++bi) {
+          const int b = (prefer + bi) % NBUF;
+          const int tile = blockIdx.x + jt[b] * gridDim.x;
+          if (tile >= num_tiles) continue;
+          any_left = true;
+          const int l = jl[b];
+          // dependency: this buffer's previous epilogue step is done
+          if (!first[b] && !mbar_test_wait(smem_u32(&act_ready[b]), ready_ph[b])) continue;
+          // layer 0 takes x panels in ring order and needs the first panel present
+          if (l == 0 && (jt[b] != next_l0 || !mbar_test_wait(smem_u32(&x_full[s]), ph))) continue;
+          if (!first[b]) ready_ph[b] ^= 1;
+          first[b] = false;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + b * L::kBufCols;
+          const uint32_t bias_l = bsm + l * (N / 64) * 1024;
+          // acc = 1 x bias (initialises the accumulator)
+          mma_ts(d_tmem, ones, make_sdesc_sw128(bias_l, 1024, 1024), kIdesc, 0u);
+          if (l == 0) {
+            for (int p = 0; p < kPanels0; ++p) {
+              if (p > 0 && !mbar_wait(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t adesc = make_sdesc_sw128(xsm + s * kPanelBytes, 16, 1024);
 #pragma unroll
-                for (int k = 0; k < kPanel / 16; ++k) {
-                  const int kk = p * (kPanel / 16) + k;  // 16-row K step within W0
-                  const uint64_t bdesc = make_sdesc_sw128(wsm + kk * 2048, K0 * 128, 1024);
-                  mma_ss(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc, kIdesc,
-                         (p | k) != 0 ? 1u : 0u);
-                }
-                mma_commit(smem_u32(&x_empty[s]));
-                if (++s == kXS) { s = 0; ph ^= 1; }
+              for (int k = 0; k < kPanel / 16; ++k) {
+                const int kk = p * (kPanel / 16) + k;  // 16-row K step within W0
+                const uint64_t bdesc = make_sdesc_sw128(wsm + kk * 2048, K0 * 128, 1024);
+                mma_ss(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc, kIdesc, 1u);
               }
-              if (!ok) break;
-            } else {
-              const uint32_t wl = wsm + w_layer_offset(l, L::kW0Bytes, L::kWhBytes);
-              const uint32_t a_tmem = tmem_base + b * L::kBufCols + L::kActCol;
-#pragma unroll
-              for (int k = 0; k < N / 16; ++k) {
-                const uint64_t bdesc = make_sdesc_sw128(wl + k * 2048, N * 128, 1024);
-                mma_ts(d_tmem, a_tmem + k * 8, bdesc, kIdesc, k != 0 ? 1u : 0u);
-              }
+              mma_commit(smem_u32(&x_empty[s]));
+              if (++s == kXS) { s = 0; ph ^= 1; }
             }
-            mma_commit(smem_u32(&acc_full[b]));
+            next_l0 += 1;
+          } else {
+            const uint32_t wl = wsm + w_layer_offset(l, L::kW0Bytes, L::kWhBytes);
+            const uint32_t a_tmem = tmem_base + b * L::kBufCols + L::kActCol;
+#pragma unroll
+            for (int k = 0; k < N / 16; ++k) {
+              const uint64_t bdesc = make_sdesc_sw128(wl + k * 2048, N * 128, 1024);
+              mma_ts(d_tmem, a_tmem + k * 8, bdesc, kIdesc, 1u);
+            }
+          }
+          mma_commit(smem_u32(&acc_full[b]));
+          if (++jl[b] == NL) { jl[b] = 0; jt[b] += NBUF; }
+          issued = true;
+          prefer = (b + 1) % NBUF;
+        }
+        if (!any_left) break;
+        if (issued) {
+          idle_since = 0;
+        } else {
+          const uint64_t now = globaltimer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > args.timeout_ns || *abort_flag) {
+            if (!*abort_flag) { atomicCAS(args.status, 0, kDevTimeoutMma); *abort_flag = 1; }
+            ok = false;
           }
         }
       }
       // drain: every issued MMA has completed before TMEM can be released
       mma_commit(smem_u32(mma_done));
-      WaitCtx drain{args.status, abort_flag, args.timeout_ns};
-      volatile int zero = 0;
-      drain.abort_flag = &zero;  // drain even after an abort
+      volatile int no_abort = 0;
+      WaitCtx drain{args.status, &no_abort, args.timeout_ns};
       mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..9)
-    const int g = (warp - 2) >> 2;         // TMEM buffer served by this group
-    const int q = warp & 3;                // TMEM lane quarter accessible to this warp
+    // ---------------------------------------------------------------- epilogue
+    const int g = (warp - 2) >> 2;  // TMEM buffer served by this group
+    const int q = warp & 3;         // TMEM lane quarter accessible to this warp
     uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes;
     const uint32_t stg_u32 = smem_u32(stg);
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + g * L::kBufCols;
     uint32_t acc_ph = 0;
     bool ok = true;
 #pragma unroll 1
-    for (int tile = blockIdx.x + g * gridDim.x; ok && tile < num_tiles; tile += 2 * gridDim.x) {
+    for (int tile = blockIdx.x + g * gridDim.x; ok && tile < num_tiles; tile += NBUF * gridDim.x) {
 #pragma unroll 1
       for (int l = 0; l < NL; ++l) {
         if (!mbar_wait(smem_u32(&acc_full[g]), acc_ph, wctx, kDevTimeoutEpilogue)) { ok = false; break; }
@@ -336,16 +399,14 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int c = 0; c < N / 32; ++c) tmem_ld32(t_lane + c * 32, v[c]);
         tmem_wait_ld();
-        const uint32_t* bias2 = reinterpret_cast<const uint32_t*>(args.bias[l]);
-        const int act = static_cast<int>((ACTS >> (4 * l)) & 15u);
         if (l + 1 < NL) {
-          // hidden layer: bias + activation -> 16-bit activation in TMEM (next layer's A)
-          switch (act) {
-            case kActRelu: epi_hidden<T, N, kActRelu>(v, bias2, t_lane + L::kActCol); break;
-            case kActGeluTanh: epi_hidden<T, N, kActGeluTanh>(v, bias2, t_lane + L::kActCol); break;
-            case kActSilu: epi_hidden<T, N, kActSilu>(v, bias2, t_lane + L::kActCol); break;
-            case kActSigmoid: epi_hidden<T, N, kActSigmoid>(v, bias2, t_lane + L::kActCol); break;
-            default: epi_hidden<T, N, kActNone>(v, bias2, t_lane + L::kActCol); break;
+          // hidden layer: activation -> 16-bit activation in TMEM (next layer's A operand)
+          switch ((ACTS >> (4 * l)) & 15u) {
+            case kActRelu: epi_hidden<T, N, kActRelu>(v, t_lane + L::kActCol); break;
+            case kActGeluTanh: epi_hidden<T, N, kActGeluTanh>(v, t_lane + L::kActCol); break;
+            case kActSilu: epi_hidden<T, N, kActSilu>(v, t_lane + L::kActCol); break;
+            case kActSigmoid: epi_hidden<T, N, kActSigmoid>(v, t_lane + L::kActCol); break;
+            default: epi_hidden<T, N, kActNone>(v, t_lane + L::kActCol); break;
           }
           tmem_wait_st();
           tc_fence_before();
@@ -356,30 +417,19 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&act_ready[g]));
-          float y[N];
-          epi_bias<T, N>(v, bias2, y);
-          if constexpr (TAIL == kTailLayerNorm) {
-            row_layernorm<T, N>(y, args.gamma, args.beta, args.ln_eps);
-          } else {
-            switch (act) {
-              case kActRelu: apply_act_row<N, kActRelu>(y); break;
-              case kActGeluTanh: apply_act_row<N, kActGeluTanh>(y); break;
-              case kActSilu: apply_act_row<N, kActSilu>(y); break;
-              case kActSigmoid: apply_act_row<N, kActSigmoid>(y); break;
-              default: break;
-            }
-          }
-          // store: per 64-column chunk, swizzled staging (SW128) then a 32x64 TMA store
+          float mean = 0.f, rstd = 1.f;
+          if constexpr (TAIL == kTailLayerNorm) row_stats<N>(v, args.ln_eps, mean, rstd);
+          const float nmr = -mean * rstd;
           const int row0 = tile * kBM + q * 32;
 #pragma unroll
-          for (int h = 0; h < N / 64; ++h) {
+          for (int c = 0; c < N / 32; ++c) {
             if (lane == 0) bulk_wait_group_read<0>();
             __syncwarp();
-            stage_row_chunk64<T>(stg, lane, y + h * 64);
+            stage_chunk32<T, TAIL, kLastAct>(stg, lane, v[c], ln_g + c * 32, ln_b + c * 32, rstd, nmr);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0 && row0 < args.m) {
-              tma_store_2d(&tm.out, stg_u32, h * 64, row0);
+              tma_store_2d(&tm.out, stg_u32, c * 32, row0);
               bulk_commit_group();
             }
           }
