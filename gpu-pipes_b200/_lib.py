@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "gp_set_timeout_ns",
     "gp_set_fault_injection",
     "gp_launch_count",
+    "gp_set_kernel_variant",
 )
 
 
@@ -98,6 +99,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_set_timeout_ns.restype = _INT
     lib.gp_set_fault_injection.argtypes = [_INT]
     lib.gp_set_fault_injection.restype = _INT
+    lib.gp_set_kernel_variant.argtypes = [_INT]
+    lib.gp_set_kernel_variant.restype = _INT
     lib.gp_launch_count.argtypes = []
     lib.gp_launch_count.restype = ctypes.c_uint64
 
@@ -153,6 +156,10 @@ def set_timeout_ns(ns: int) -> None:
 
 def set_fault_injection(mode: int) -> None:
     check(lib().gp_set_fault_injection(int(mode)))
+
+
+def set_kernel_variant(v: int) -> None:
+    check(lib().gp_set_kernel_variant(int(v)))
 
 
 def launch_count() -> int:

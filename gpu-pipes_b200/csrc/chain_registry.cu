@@ -1,4 +1,6 @@
 // Table of compiled chains and the spec matcher.
+#include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -19,6 +21,10 @@ GP_DECLARE(launch_mgn_nl_f16_k256)
 GP_DECLARE(launch_mgn_nl_f16_k128)
 GP_DECLARE(launch_probe_1l_f16_k128)
 GP_DECLARE(launch_probe_2l_f16_k128)
+GP_DECLARE(launch_mgn_ln_f16_k384_single)
+GP_DECLARE(launch_mgn_ln_f16_k256_single)
+GP_DECLARE(launch_probe_1l_f16_k128_pair)
+GP_DECLARE(launch_probe_2l_f16_k128_pair)
 #undef GP_DECLARE
 
 #define R GP_ACT_RELU
@@ -38,22 +44,45 @@ static const ChainEntry kChains[] = {
     // single GEMM and two-GEMM probes (known-answer tests of the tcgen05 paths)
     {"probe_1l_f16_k128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128},
     {"probe_2l_f16_k128", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128},
+    // variant 1: alternative kernels for the same chains (selected with GP_KERNEL_VARIANT=1)
+    {"mgn_ln_f16_k384_single", GP_F16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k384_single, 1},
+    {"mgn_ln_f16_k256_single", GP_F16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k256_single, 1},
+    {"probe_1l_f16_k128_pair", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128_pair, 1},
+    {"probe_2l_f16_k128_pair", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_pair, 1},
 };
 #undef R
 #undef NO
 
-const ChainEntry* find_chain(const gp_mlp_spec& s) {
-  for (const ChainEntry& e : kChains) {
-    if (e.dtype != s.dtype || e.n_layers != s.n_layers || e.tail != s.tail) continue;
-    bool ok = true;
-    for (int l = 0; ok && l <= s.n_layers; ++l) ok = e.widths[l] == s.widths[l];
-    for (int l = 0; ok && l < s.n_layers; ++l) {
-      const bool last_normed = (l == s.n_layers - 1) && s.tail != GP_TAIL_NONE;
-      if (!last_normed) ok = e.act[l] == s.act[l];
-    }
-    if (ok) return &e;
+static std::atomic<int> g_variant{[] {
+  const char* e = std::getenv("GP_KERNEL_VARIANT");
+  return e != nullptr ? std::atoi(e) : 0;
+}()};
+
+static int wanted_variant() { return g_variant.load(std::memory_order_relaxed); }
+
+void set_kernel_variant(int v) { g_variant.store(v); }
+
+static bool matches(const ChainEntry& e, const gp_mlp_spec& s) {
+  if (e.dtype != s.dtype || e.n_layers != s.n_layers || e.tail != s.tail) return false;
+  for (int l = 0; l <= s.n_layers; ++l)
+    if (e.widths[l] != s.widths[l]) return false;
+  for (int l = 0; l < s.n_layers; ++l) {
+    const bool last_normed = (l == s.n_layers - 1) && s.tail != GP_TAIL_NONE;
+    if (!last_normed && e.act[l] != s.act[l]) return false;
   }
-  return nullptr;
+  return true;
+}
+
+// The entry of the requested variant (GP_KERNEL_VARIANT, default 0) if one exists, else the
+// first entry that matches.
+const ChainEntry* find_chain(const gp_mlp_spec& s) {
+  const ChainEntry* any = nullptr;
+  for (const ChainEntry& e : kChains) {
+    if (!matches(e, s)) continue;
+    if (e.variant == wanted_variant()) return &e;
+    if (any == nullptr) any = &e;
+  }
+  return any;
 }
 
 int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask) {

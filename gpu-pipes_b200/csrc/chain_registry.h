@@ -30,9 +30,11 @@ struct ChainEntry {
   int act[kMaxLayers];
   int tail;
   LaunchFn launch;
+  int variant = 0;  // 0 = default kernel for the chain; others selectable for A/B measurements
 };
 
 const ChainEntry* find_chain(const gp_mlp_spec& s);
+void set_kernel_variant(int v);
 
 // helpers implemented in gp_abi.cu
 int set_error(int code, const char* fmt, ...);

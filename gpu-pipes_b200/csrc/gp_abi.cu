@@ -314,4 +314,10 @@ int gp_set_fault_injection(int mode) {
 
 uint64_t gp_launch_count(void) { return g_launches.load(); }
 
+int gp_set_kernel_variant(int variant) {
+  if (variant < 0 || variant > 1) return set_error(GP_ERR_ARG, "kernel variant %d unknown", variant);
+  set_kernel_variant(variant);
+  return GP_OK;
+}
+
 }  // extern "C"

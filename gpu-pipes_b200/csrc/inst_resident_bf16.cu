@@ -6,7 +6,7 @@
 namespace gp {
 constexpr uint32_t kReluReluNone = GP_ACT_RELU | (GP_ACT_RELU << 4);
 
-int launch_mgn_ln_bf16_k384(const LaunchCtx& c) { return launch_resident<__nv_bfloat16, 384, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
-int launch_mgn_ln_bf16_k256(const LaunchCtx& c) { return launch_resident<__nv_bfloat16, 256, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
-int launch_mgn_ln_bf16_k128(const LaunchCtx& c) { return launch_resident<__nv_bfloat16, 128, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
+int launch_mgn_ln_bf16_k384(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 384, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
+int launch_mgn_ln_bf16_k256(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 256, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
+int launch_mgn_ln_bf16_k128(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 128, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
 }  // namespace gp

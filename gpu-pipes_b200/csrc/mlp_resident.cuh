@@ -40,17 +40,20 @@
 
 namespace gp {
 
-template <int K0_, int N_, int NL_, int NBUF_>
+template <int K0_, int N_, int NL_, int NBUF_, int CG_>
 struct ResidentLayout {
-  static constexpr int K0 = K0_, N = N_, NL = NL_, NBUF = NBUF_;
+  static constexpr int K0 = K0_, N = N_, NL = NL_, NBUF = NBUF_, CG = CG_;
   static_assert(K0 % kPanel == 0 && K0 >= kPanel, "K0 must be a multiple of 64");
   static_assert(N % kPanel == 0 && N >= 64 && N <= 128, "hidden width must be 64 or 128");
   static_assert(NL >= 1 && NL <= kMaxLayers, "layer count");
   static_assert(NBUF == 1 || NBUF == 2, "one or two tiles in flight");
-  static constexpr int kW0Bytes = K0 * N * 2;
-  static constexpr int kWhBytes = N * N * 2;
+  static_assert(CG == 1 || (CG == 2 && N == 128), "CTA pairs split N = 128 into two halves");
+  static constexpr int NC = N / CG;                // weight / bias columns held by this CTA
+  static constexpr int kUnitRows = kBM * CG;       // rows per work unit (one tile per CTA)
+  static constexpr int kW0Bytes = K0 * NC * 2;
+  static constexpr int kWhBytes = N * NC * 2;
   static constexpr int kWBytes = kW0Bytes + (NL - 1) * kWhBytes;
-  static constexpr int kBiasBytes = NL * (N / 64) * 1024 + 1024;  // + one trailing zero atom
+  static constexpr int kBiasBytes = NL * (NC / 64) * 1024 + 1024;  // + one trailing zero atom
   static constexpr int kNumEpiWarps = 4 * NBUF;
   static constexpr int kStageBytes = 32 * 64;  // per epilogue warp: 32 rows x 32 cols x 2 B
   static constexpr int kStgBytes = kNumEpiWarps * kStageBytes;
@@ -164,22 +167,28 @@ __device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint
   }
 }
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF>
-__global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
-    mlp_resident_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
-  using L = ResidentLayout<K0, N, NL, NBUF>;
+// Kernel body shared by the single-CTA (CG = 1) and CTA-pair (CG = 2) forms. In the pair form
+// the cluster's two CTAs each own 128 rows of a 256-row unit and half of every weight's columns;
+// the leader (rank 0) issues cta_group::2 MMAs (M = 256) that read both CTAs' shared memory and
+// write both CTAs' TMEM. Loads of both CTAs complete on the leader's barriers; MMA commits
+// arrive on both CTAs' barriers; both CTAs' epilogues release a buffer on the leader's barrier.
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG>
+__device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const ChainArgs& args) {
+  using L = ResidentLayout<K0, N, NL, NBUF, CG>;
   constexpr int kXS = L::kXStages;
   constexpr int kPanels0 = K0 / kPanel;
-  constexpr uint32_t kIdesc = make_idesc_f16(kBM, N, Elem<T>::kIsBf16, 0, 1);
+  constexpr int NC = L::NC;
+  constexpr bool kPair = CG == 2;
+  constexpr uint32_t kIdesc = make_idesc_f16(kBM * CG, N, Elem<T>::kIsBf16, 0, 1);
   constexpr int kLastAct = static_cast<int>((ACTS >> (4 * (NL - 1))) & 15u);
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* x_full = bars;         // [kXS]
+  uint64_t* x_full = bars;         // [kXS]   (leader's receive both CTAs' loads)
   uint64_t* x_empty = bars + 8;    // [kXS]
   uint64_t* w_full = bars + 16;    // [1]
   uint64_t* acc_full = bars + 17;  // [NBUF]
-  uint64_t* act_ready = bars + 19; // [NBUF]
+  uint64_t* act_ready = bars + 19; // [NBUF]  (leader's count both CTAs' epilogue warps)
   uint64_t* mma_done = bars + 21;  // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
@@ -188,11 +197,16 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int num_units = args.num_tiles;  // in units of kUnitRows rows
 
   // the swizzled operand layouts assume a 1024-byte aligned shared window
   if ((smem_u32(smem) & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
-    return;
+    return;  // uniform over the cluster: both CTAs have the same layout
   }
 
   if (threadIdx.x == 0) {
@@ -203,7 +217,7 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
     mbar_init(smem_u32(w_full), 1);
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&act_ready[b]), 4);
+      mbar_init(smem_u32(&act_ready[b]), 4 * CG);
     }
     mbar_init(smem_u32(mma_done), 1);
     *abort_flag = 0;
@@ -214,17 +228,23 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
     prefetch_tmap(&tm.out);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_holder), L::kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_holder), L::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), L::kTmemCols);
+      tmem_relinquish();
+    }
   }
-  // bias slices (row 0 of each 8-row x 128-byte atom; rows 1..7 and a trailing atom are zero)
-  // and the LayerNorm parameters in fp32
+  // bias slices (row 0 of each 8-row x 128-byte atom holds this CTA's NC bias values; rows 1..7
+  // and a trailing atom are zero) and the LayerNorm parameters in fp32
   for (int i = threadIdx.x; i < L::kBiasBytes / 16; i += blockDim.x) {
     const int atom = i >> 6, chunk = i & 63;  // 64 chunks of 16 B per atom
     uint4 val = make_uint4(0, 0, 0, 0);
-    const int l = atom / (N / 64), nb = atom % (N / 64);
+    const int l = atom / (NC / 64), nb = atom % (NC / 64);
     if (chunk < 8 && l < NL && args.bias[l] != nullptr) {
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(args.bias[l]) + (nb * 8 + chunk) * 4;
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(args.bias[l]) +
+                            (rank * NC + nb * 64) / 2 + chunk * 4;
       val = make_uint4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
     }
     *reinterpret_cast<uint4*>(smem + L::kOffBias + i * 16) = val;
@@ -249,40 +269,60 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
     tmem_wait_st();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // peer barriers initialised, ones and bias written in both CTAs
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
 
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
-  const int num_tiles = args.num_tiles;
+  // barrier addresses as seen by the loads / arrivals of this CTA (the leader's in a pair)
+  auto leader_bar = [&](const uint64_t* b) -> uint32_t {
+    return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
+  };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
       const uint64_t stream = l2_policy_evict_first();
-      mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes);
+      if (leader) mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes * CG);
+      const uint32_t wbar = leader_bar(w_full);
 #pragma unroll 1
       for (int l = 0; l < NL; ++l) {
         const int kl = l == 0 ? K0 : N;
         const uint32_t wbase =
             smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
         for (int kp = 0; kp < kl / kPanel; ++kp)
-          for (int nb = 0; nb < N / kPanel; ++nb)
-            tma_load_2d_hint(wbase + nb * (kl * 128) + kp * (kPanel * 128), &tm.w[l],
-                             smem_u32(w_full), nb * kPanel, kp * kPanel, keep);
+          for (int nb = 0; nb < NC / kPanel; ++nb) {
+            const uint32_t dst = wbase + nb * (kl * 128) + kp * (kPanel * 128);
+            const int c0 = static_cast<int>(rank) * NC + nb * kPanel;
+            if constexpr (kPair) {
+              tma_load_2d_pair(dst, &tm.w[l], wbar, c0, kp * kPanel, keep);
+            } else {
+              tma_load_2d_hint(dst, &tm.w[l], wbar, c0, kp * kPanel, keep);
+            }
+          }
       }
       int s = 0;
       uint32_t ph = 0;
 #pragma unroll 1
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int unit = unit0; unit < num_units; unit += units_step) {
+        const int row = unit * L::kUnitRows + static_cast<int>(rank) * kBM;
 #pragma unroll 1
         for (int p = 0; p < kPanels0; ++p) {
-          if (!mbar_wait(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer))
+          if (!mbar_wait<kPair>(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer))
             goto producer_done;
           if (!args.inject) {
-            mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
-            tma_load_2d_hint(smem_u32(smem + L::kOffX + s * kPanelBytes), &tm.x,
-                             smem_u32(&x_full[s]), p * kPanel, tile * kBM, stream);
+            const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
+            if constexpr (kPair) {
+              if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
+              tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[s]), p * kPanel, row, stream);
+            } else {
+              mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
+              tma_load_2d_hint(dst, &tm.x, smem_u32(&x_full[s]), p * kPanel, row, stream);
+            }
           }
           if (++s == kXS) { s = 0; ph ^= 1; }
         }
@@ -291,22 +331,35 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait(smem_u32(w_full), 0, wctx, kDevTimeoutWeights);
+    // ---------------------------------------------------------------- MMA issuer (pair leader)
+    if (lane == 0 && leader) {
+      bool ok = mbar_wait<kPair>(smem_u32(w_full), 0, wctx, kDevTimeoutWeights);
       tc_fence_after();
       const uint32_t wsm = smem_u32(smem + L::kOffW);
       const uint32_t xsm = smem_u32(smem + L::kOffX);
       const uint32_t bsm = smem_u32(smem + L::kOffBias);
       const uint32_t ones = tmem_base + L::kOnesCol;
+      auto mma_ss_any = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+        if constexpr (kPair) mma_ss_pair(d, a, b, kIdesc, acc); else mma_ss(d, a, b, kIdesc, acc);
+      };
+      auto mma_ts_any = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t acc) {
+        if constexpr (kPair) mma_ts_pair(d, a, b, kIdesc, acc); else mma_ts(d, a, b, kIdesc, acc);
+      };
+      auto commit_any = [&](uint64_t* bar) {
+        if constexpr (kPair) mma_commit_pair(smem_u32(bar), 0x3); else mma_commit(smem_u32(bar));
+      };
+      auto test_any = [&](uint64_t* bar, uint32_t parity) {
+        return kPair ? mbar_test_wait_cluster(smem_u32(bar), parity)
+                     : mbar_test_wait(smem_u32(bar), parity);
+      };
       int s = 0;
       uint32_t ph = 0;
-      // per-buffer job cursor: local tile index (tiles j with j % NBUF == b) and layer
+      // per-buffer job cursor: local unit index (units j with j % NBUF == b) and layer
       int jt[NBUF], jl[NBUF];
       uint32_t ready_ph[NBUF];
       bool first[NBUF];
       for (int b = 0; b < NBUF; ++b) { jt[b] = b; jl[b] = 0; ready_ph[b] = 0; first[b] = true; }
-      int next_l0 = 0;  // local tile whose layer 0 consumes the x ring next (ring order)
+      int next_l0 = 0;  // local unit whose layer 0 consumes the x ring next (ring order)
       uint64_t idle_since = 0;
       int prefer = 0;
 #pragma unroll 1
@@ -315,33 +368,33 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
 #pragma unroll 1
         for (int bi = 0; bi < NBUF && !issued; ++bi) {
           const int b = (prefer + bi) % NBUF;
-          const int tile = blockIdx.x + jt[b] * gridDim.x;
-          if (tile >= num_tiles) continue;
+          const int unit = unit0 + jt[b] * units_step;
+          if (unit >= num_units) continue;
           any_left = true;
           const int l = jl[b];
-          // dependency: this buffer's previous epilogue step is done
-          if (!first[b] && !mbar_test_wait(smem_u32(&act_ready[b]), ready_ph[b])) continue;
+          // dependency: this buffer's previous epilogue step is done (in both CTAs)
+          if (!first[b] && !test_any(&act_ready[b], ready_ph[b])) continue;
           // layer 0 takes x panels in ring order and needs the first panel present
-          if (l == 0 && (jt[b] != next_l0 || !mbar_test_wait(smem_u32(&x_full[s]), ph))) continue;
+          if (l == 0 && (jt[b] != next_l0 || !test_any(&x_full[s], ph))) continue;
           if (!first[b]) ready_ph[b] ^= 1;
           first[b] = false;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + b * L::kBufCols;
-          const uint32_t bias_l = bsm + l * (N / 64) * 1024;
+          const uint32_t bias_l = bsm + l * (NC / 64) * 1024;
           // acc = 1 x bias (initialises the accumulator)
-          mma_ts(d_tmem, ones, make_sdesc_sw128(bias_l, 1024, 1024), kIdesc, 0u);
+          mma_ts_any(d_tmem, ones, make_sdesc_sw128(bias_l, 1024, 1024), 0u);
           if (l == 0) {
             for (int p = 0; p < kPanels0; ++p) {
-              if (p > 0 && !mbar_wait(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+              if (p > 0 && !mbar_wait<kPair>(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
               tc_fence_after();
               const uint64_t adesc = make_sdesc_sw128(xsm + s * kPanelBytes, 16, 1024);
 #pragma unroll
               for (int k = 0; k < kPanel / 16; ++k) {
                 const int kk = p * (kPanel / 16) + k;  // 16-row K step within W0
                 const uint64_t bdesc = make_sdesc_sw128(wsm + kk * 2048, K0 * 128, 1024);
-                mma_ss(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc, kIdesc, 1u);
+                mma_ss_any(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc, 1u);
               }
-              mma_commit(smem_u32(&x_empty[s]));
+              commit_any(&x_empty[s]);
               if (++s == kXS) { s = 0; ph ^= 1; }
             }
             next_l0 += 1;
@@ -351,10 +404,10 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
 #pragma unroll
             for (int k = 0; k < N / 16; ++k) {
               const uint64_t bdesc = make_sdesc_sw128(wl + k * 2048, N * 128, 1024);
-              mma_ts(d_tmem, a_tmem + k * 8, bdesc, kIdesc, 1u);
+              mma_ts_any(d_tmem, a_tmem + k * 8, bdesc, 1u);
             }
           }
-          mma_commit(smem_u32(&acc_full[b]));
+          commit_any(&acc_full[b]);
           if (++jl[b] == NL) { jl[b] = 0; jt[b] += NBUF; }
           issued = true;
           prefer = (b + 1) % NBUF;
@@ -373,10 +426,12 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
         }
       }
       // drain: every issued MMA has completed before TMEM can be released
-      mma_commit(smem_u32(mma_done));
+      commit_any(mma_done);
+    }
+    if (lane == 0) {
       volatile int no_abort = 0;
       WaitCtx drain{args.status, &no_abort, args.timeout_ns};
-      mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
+      mbar_wait<kPair>(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -386,13 +441,14 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
     uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes;
     const uint32_t stg_u32 = smem_u32(stg);
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + g * L::kBufCols;
+    const uint32_t ready_bar[2] = {leader_bar(&act_ready[0]), leader_bar(&act_ready[NBUF - 1])};
     uint32_t acc_ph = 0;
     bool ok = true;
 #pragma unroll 1
-    for (int tile = blockIdx.x + g * gridDim.x; ok && tile < num_tiles; tile += NBUF * gridDim.x) {
+    for (int unit = unit0 + g * units_step; ok && unit < num_units; unit += NBUF * units_step) {
 #pragma unroll 1
       for (int l = 0; l < NL; ++l) {
-        if (!mbar_wait(smem_u32(&acc_full[g]), acc_ph, wctx, kDevTimeoutEpilogue)) { ok = false; break; }
+        if (!mbar_wait<kPair>(smem_u32(&acc_full[g]), acc_ph, wctx, kDevTimeoutEpilogue)) { ok = false; break; }
         acc_ph ^= 1;
         tc_fence_after();
         uint32_t v[N / 32][32];
@@ -411,16 +467,20 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&act_ready[g]));
+          if (lane == 0) {
+            if constexpr (kPair) mbar_arrive_cluster(ready_bar[g]); else mbar_arrive(smem_u32(&act_ready[g]));
+          }
         } else {
           // last layer: the accumulator is in registers; release the TMEM buffer first
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&act_ready[g]));
+          if (lane == 0) {
+            if constexpr (kPair) mbar_arrive_cluster(ready_bar[g]); else mbar_arrive(smem_u32(&act_ready[g]));
+          }
           float mean = 0.f, rstd = 1.f;
           if constexpr (TAIL == kTailLayerNorm) row_stats<N>(v, args.ln_eps, mean, rstd);
           const float nmr = -mean * rstd;
-          const int row0 = tile * kBM + q * 32;
+          const int row0 = unit * L::kUnitRows + static_cast<int>(rank) * kBM + q * 32;
 #pragma unroll
           for (int c = 0; c < N / 32; ++c) {
             if (lane == 0) bulk_wait_group_read<0>();
@@ -441,11 +501,27 @@ __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF>::kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // no CTA leaves while the pair's MMAs may still read its memory
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
+    if constexpr (kPair) tmem_dealloc_pair(tmem_base, L::kTmemCols); else tmem_dealloc(tmem_base, L::kTmemCols);
   }
+}
+
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF>
+__global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF, 1>::kThreads, 1)
+    mlp_resident_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 1>(tm, args);
+}
+
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(ResidentLayout<K0, N, NL, NBUF, 2>::kThreads, 1)
+    mlp_resident_pair_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 2>(tm, args);
 }
 
 }  // namespace gp

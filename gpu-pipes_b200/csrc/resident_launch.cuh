@@ -1,16 +1,21 @@
-// Host launcher for mlp_resident_kernel.
+// Host launchers for the weight-resident chain kernel (single CTA and CTA pair).
 #pragma once
+
+#include <cstring>
 
 #include "chain_registry.h"
 #include "mlp_resident.cuh"
 
 namespace gp {
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF = 2>
-int launch_resident(const LaunchCtx& c) {
-  using L = ResidentLayout<K0, N, NL, NBUF>;
-  const void* kern = reinterpret_cast<const void*>(&mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>);
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG>
+int launch_resident_cg(const LaunchCtx& c) {
+  using L = ResidentLayout<K0, N, NL, NBUF, CG>;
+  const void* kern =
+      CG == 2 ? reinterpret_cast<const void*>(&mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>)
+              : reinterpret_cast<const void*>(&mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>);
   static unsigned long long done_mask = 0;
+  static int max_clusters[64] = {0};
   int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
   if (rc != GP_OK) return rc;
   const int dt = c.spec->dtype;
@@ -21,9 +26,50 @@ int launch_resident(const LaunchCtx& c) {
   for (int l = 0; rc == GP_OK && l < NL; ++l)
     rc = make_tmap_2d(&tm.w[l], c.w[l], dt, l == 0 ? K0 : N, N, kPanel, kPanel, 128);
   if (rc != GP_OK) return rc;
-  const int grid = c.args.num_tiles < c.sm_count ? c.args.num_tiles : c.sm_count;
-  mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, c.args);
+  ChainArgs args = c.args;
+  args.num_tiles = static_cast<int>((c.m + L::kUnitRows - 1) / L::kUnitRows);
+  if constexpr (CG == 1) {
+    const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
+    mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  } else {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& mc = max_clusters[dev & 63];
+    if (mc == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (c.sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(L::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = L::kSmemBytes;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = c.sm_count / 2;
+      }
+      mc = n;
+    }
+    const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
+    mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>
+        <<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  }
   return GP_OK;
+}
+
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF = 2>
+int launch_resident(const LaunchCtx& c) {
+  return launch_resident_cg<T, K0, N, NL, ACTS, TAIL, NBUF, 1>(c);
+}
+
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF = 2>
+int launch_resident_pair(const LaunchCtx& c) {
+  return launch_resident_cg<T, K0, N, NL, ACTS, TAIL, NBUF, 2>(c);
 }
 
 }  // namespace gp

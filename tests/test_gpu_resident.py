@@ -18,6 +18,14 @@ pytestmark = pytest.mark.gpu
 NONE, RELU = L.ACT_NONE, L.ACT_RELU
 
 
+@pytest.fixture(params=[0, 1], ids=["pair", "single"])
+def variant(request):
+    """Run a test with the default (CTA-pair) kernels and with the single-CTA alternatives."""
+    L.set_kernel_variant(request.param)
+    yield request.param
+    L.set_kernel_variant(0)
+
+
 def _dev(ts, dev):
     return [t.to(dev) if t is not None else None for t in ts]
 
@@ -29,7 +37,7 @@ def _assert_close(out, ref, what):
 
 
 # ------------------------------------------------------------------ known answers (exact)
-def test_single_gemm_all_ones(cuda_dev):
+def test_single_gemm_all_ones(cuda_dev, variant):
     """misc_tests/gemm-val/blockgemm-val.cu:198-219 pattern: I = W = 1 -> every output = K."""
     x = torch.ones(256, 128, dtype=torch.float16, device=cuda_dev)
     w = torch.ones(128, 128, dtype=torch.float16, device=cuda_dev)
@@ -39,7 +47,7 @@ def test_single_gemm_all_ones(cuda_dev):
     assert torch.equal(out, torch.full_like(out, 128.0))
 
 
-def test_single_gemm_permutation(cuda_dev):
+def test_single_gemm_permutation(cuda_dev, variant):
     """x @ P for a permutation P is an exact column shuffle: checks the B-operand layout."""
     g = torch.Generator().manual_seed(5)
     x = torch.randn(384, 128, generator=g).half()
@@ -54,7 +62,7 @@ def test_single_gemm_permutation(cuda_dev):
     assert torch.equal(out.cpu(), expect)
 
 
-def test_two_layer_tmem_handoff_exact(cuda_dev):
+def test_two_layer_tmem_handoff_exact(cuda_dev, variant):
     """Layer 2 reads layer 1's output from TMEM (A operand in tensor memory). With W1 a
     permutation and W2 = 2*I the result is exact, so any packing error shows up."""
     g = torch.Generator().manual_seed(6)
@@ -130,7 +138,7 @@ def _run_workload(w, dev, x=None):
 
 
 @pytest.mark.parametrize("wname", ["mgn_edge", "mgn_node"])
-def test_config_full_size(cuda_dev, wname):
+def test_config_full_size(cuda_dev, wname, variant):
     w = W.WORKLOADS[wname]
     x, layers, ln, out = _run_workload(w, cuda_dev)
     ref = O.workload_forward(w, x, layers, ln)
@@ -139,7 +147,7 @@ def test_config_full_size(cuda_dev, wname):
 
 
 @pytest.mark.parametrize("m", [1, 2, 127, 128, 129, 255, 300, 1000, 65537])
-def test_ragged_rows(cuda_dev, m):
+def test_ragged_rows(cuda_dev, m, variant):
     w = W.MGN_EDGE.with_m(m)
     x, layers, ln, out = _run_workload(w, cuda_dev)
     _assert_close(out, O.workload_forward(w, x, layers, ln), f"m={m}")
@@ -228,7 +236,7 @@ def test_wrong_width_raises(cuda_dev):
         cuda_ext.mgn_fullmlp(x, w1, b, w, b, w, b, b, b)
 
 
-def test_timeout_is_reported_and_context_survives(cuda_dev):
+def test_timeout_is_reported_and_context_survives(cuda_dev, variant):
     """Fault injection on the host side: the producer never issues its loads, so every consumer
     wait runs out after 5 ms; the kernel exits cleanly, the status word says which role gave up,
     and the next launch on the same context is correct."""
