@@ -10,46 +10,50 @@ namespace gp {
 
 // launchers defined in the instance translation units
 #define GP_DECLARE(fn) int fn(const LaunchCtx&);
-GP_DECLARE(launch_mgn_ln_f16_k384)
-GP_DECLARE(launch_mgn_ln_f16_k256)
-GP_DECLARE(launch_mgn_ln_f16_k128)
-GP_DECLARE(launch_mgn_ln_bf16_k384)
-GP_DECLARE(launch_mgn_ln_bf16_k256)
-GP_DECLARE(launch_mgn_ln_bf16_k128)
-GP_DECLARE(launch_mgn_nl_f16_k384)
-GP_DECLARE(launch_mgn_nl_f16_k256)
-GP_DECLARE(launch_mgn_nl_f16_k128)
-GP_DECLARE(launch_probe_1l_f16_k128)
-GP_DECLARE(launch_probe_2l_f16_k128)
-GP_DECLARE(launch_mgn_ln_f16_k384_single)
-GP_DECLARE(launch_mgn_ln_f16_k256_single)
-GP_DECLARE(launch_probe_1l_f16_k128_pair)
-GP_DECLARE(launch_probe_2l_f16_k128_pair)
+#define GP_DECLARE2(n) GP_DECLARE(launch_##n##_pair) GP_DECLARE(launch_##n##_single)
+GP_DECLARE2(mgn_ln_f16_k384)
+GP_DECLARE2(mgn_ln_f16_k256)
+GP_DECLARE2(mgn_ln_f16_k128)
+GP_DECLARE2(mgn_nl_f16_k384)
+GP_DECLARE2(mgn_nl_f16_k256)
+GP_DECLARE2(mgn_nl_f16_k128)
+GP_DECLARE2(probe_1l_f16_k128)
+GP_DECLARE2(probe_2l_f16_k128)
+GP_DECLARE(launch_mgn_ln_bf16_k384_pair)
+GP_DECLARE(launch_mgn_ln_bf16_k256_single)
+GP_DECLARE(launch_mgn_ln_bf16_k128_single)
+#undef GP_DECLARE2
 #undef GP_DECLARE
 
 #define R GP_ACT_RELU
 #define NO GP_ACT_NONE
+#define MGN(K0) {K0, 128, 128, 128}, {R, R, NO}
+// Variant 0 is the default kernel of a chain; variant 1 the other form (A/B measurement, tests).
 static const ChainEntry kChains[] = {
-    // MeshGraphNet MLP + LayerNorm (mgn_fullmlp), fp16 and bf16
-    {"mgn_ln_f16_k384", GP_F16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k384},
-    {"mgn_ln_f16_k256", GP_F16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k256},
-    {"mgn_ln_f16_k128", GP_F16, 3, {128, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k128},
-    {"mgn_ln_bf16_k384", GP_BF16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k384},
-    {"mgn_ln_bf16_k256", GP_BF16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k256},
-    {"mgn_ln_bf16_k128", GP_BF16, 3, {128, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k128},
+    // MeshGraphNet MLP + LayerNorm (mgn_fullmlp): k0 = 384 edge, 256 node, 128
+    {"mgn_ln_f16_k384", GP_F16, 3, MGN(384), GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k384_pair, 0},
+    {"mgn_ln_f16_k384_single", GP_F16, 3, MGN(384), GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k384_single, 1},
+    {"mgn_ln_f16_k256", GP_F16, 3, MGN(256), GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k256_single, 0},
+    {"mgn_ln_f16_k256_pair", GP_F16, 3, MGN(256), GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k256_pair, 1},
+    {"mgn_ln_f16_k128", GP_F16, 3, MGN(128), GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k128_single, 0},
+    {"mgn_ln_f16_k128_pair", GP_F16, 3, MGN(128), GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k128_pair, 1},
+    {"mgn_ln_bf16_k384", GP_BF16, 3, MGN(384), GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k384_pair, 0},
+    {"mgn_ln_bf16_k256", GP_BF16, 3, MGN(256), GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k256_single, 0},
+    {"mgn_ln_bf16_k128", GP_BF16, 3, MGN(128), GP_TAIL_LAYERNORM, launch_mgn_ln_bf16_k128_single, 0},
     // same chain without LayerNorm (mgn_linears, test_mlp)
-    {"mgn_nl_f16_k384", GP_F16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_NONE, launch_mgn_nl_f16_k384},
-    {"mgn_nl_f16_k256", GP_F16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_NONE, launch_mgn_nl_f16_k256},
-    {"mgn_nl_f16_k128", GP_F16, 3, {128, 128, 128, 128}, {R, R, NO}, GP_TAIL_NONE, launch_mgn_nl_f16_k128},
+    {"mgn_nl_f16_k384", GP_F16, 3, MGN(384), GP_TAIL_NONE, launch_mgn_nl_f16_k384_pair, 0},
+    {"mgn_nl_f16_k384_single", GP_F16, 3, MGN(384), GP_TAIL_NONE, launch_mgn_nl_f16_k384_single, 1},
+    {"mgn_nl_f16_k256", GP_F16, 3, MGN(256), GP_TAIL_NONE, launch_mgn_nl_f16_k256_single, 0},
+    {"mgn_nl_f16_k256_pair", GP_F16, 3, MGN(256), GP_TAIL_NONE, launch_mgn_nl_f16_k256_pair, 1},
+    {"mgn_nl_f16_k128", GP_F16, 3, MGN(128), GP_TAIL_NONE, launch_mgn_nl_f16_k128_single, 0},
+    {"mgn_nl_f16_k128_pair", GP_F16, 3, MGN(128), GP_TAIL_NONE, launch_mgn_nl_f16_k128_pair, 1},
     // single GEMM and two-GEMM probes (known-answer tests of the tcgen05 paths)
-    {"probe_1l_f16_k128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128},
-    {"probe_2l_f16_k128", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128},
-    // variant 1: alternative kernels for the same chains (selected with GP_KERNEL_VARIANT=1)
-    {"mgn_ln_f16_k384_single", GP_F16, 3, {384, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k384_single, 1},
-    {"mgn_ln_f16_k256_single", GP_F16, 3, {256, 128, 128, 128}, {R, R, NO}, GP_TAIL_LAYERNORM, launch_mgn_ln_f16_k256_single, 1},
-    {"probe_1l_f16_k128_pair", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128_pair, 1},
-    {"probe_2l_f16_k128_pair", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_pair, 1},
+    {"probe_1l_f16_k128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128_pair, 0},
+    {"probe_1l_f16_k128_single", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128_single, 1},
+    {"probe_2l_f16_k128", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_pair, 0},
+    {"probe_2l_f16_k128_single", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_single, 1},
 };
+#undef MGN
 #undef R
 #undef NO
 

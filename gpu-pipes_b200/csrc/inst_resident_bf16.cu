@@ -1,4 +1,4 @@
-// bf16 instantiations of the weight-resident chain kernel.
+// bf16 instantiations of the weight-resident chain kernel (same defaults as the fp16 ones).
 #include <cstring>
 
 #include "resident_launch.cuh"
@@ -6,7 +6,7 @@
 namespace gp {
 constexpr uint32_t kReluReluNone = GP_ACT_RELU | (GP_ACT_RELU << 4);
 
-int launch_mgn_ln_bf16_k384(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 384, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
-int launch_mgn_ln_bf16_k256(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 256, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
-int launch_mgn_ln_bf16_k128(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 128, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
+int launch_mgn_ln_bf16_k384_pair(const LaunchCtx& c) { return launch_resident_pair<__nv_bfloat16, 384, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
+int launch_mgn_ln_bf16_k256_single(const LaunchCtx& c) { return launch_resident<__nv_bfloat16, 256, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
+int launch_mgn_ln_bf16_k128_single(const LaunchCtx& c) { return launch_resident<__nv_bfloat16, 128, 128, 3, kReluReluNone, kTailLayerNorm>(c); }
 }  // namespace gp

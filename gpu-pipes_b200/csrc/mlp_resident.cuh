@@ -55,10 +55,15 @@ struct ResidentLayout {
   static constexpr int kWBytes = kW0Bytes + (NL - 1) * kWhBytes;
   static constexpr int kBiasBytes = NL * (NC / 64) * 1024 + 1024;  // + one trailing zero atom
   static constexpr int kNumEpiWarps = 4 * NBUF;
-  static constexpr int kStageBytes = 32 * 64;  // per epilogue warp: 32 rows x 32 cols x 2 B
-  static constexpr int kStgBytes = kNumEpiWarps * kStageBytes;
   static constexpr int kLnBytes = 2 * N * 4;  // fp32 gamma, beta
   static constexpr int kBarBytes = 256;
+  // output staging per epilogue warp: 32 rows x 32 cols x 2 B, double-buffered when that still
+  // leaves at least four x stages
+  static constexpr int kStageBytes = 32 * 64;
+  static constexpr int kStgBufs =
+      (kSmemLimit - (kWBytes + kBiasBytes + 2 * kNumEpiWarps * kStageBytes + kLnBytes + kBarBytes)) /
+                  kPanelBytes >= 4 ? 2 : 1;
+  static constexpr int kStgBytes = kNumEpiWarps * kStageBytes * kStgBufs;
   static constexpr int kFixed = kWBytes + kBiasBytes + kStgBytes + kLnBytes + kBarBytes;
   static constexpr int kXStagesRaw = (kSmemLimit - kFixed) / kPanelBytes;
   static constexpr int kXStages = kXStagesRaw > 8 ? 8 : kXStagesRaw;
@@ -138,40 +143,54 @@ __device__ __forceinline__ uint32_t act_pack_f2(float2 y) {
   return act_pack<T, ACT>(y.x, y.y);
 }
 
-// Write 32 values of this thread's row (c32 = 32-column block) into a 32-row x 64-byte staging
-// tile with the TMA SWIZZLE_64B pattern (16-byte chunk j of row r lands at j ^ ((r >> 1) & 3)),
-// applying the tail: LayerNorm (mean/rstd/gamma/beta) or the activation.
+// Final values of one 32-column block of this thread's row, packed to 16 bits: LayerNorm
+// ((v - mean) * rstd * gamma + beta; gamma/beta skipped when they are the identity) or the
+// activation. All shared-memory loads of gamma/beta happen here, before any staging store.
 template <typename T, int TAIL, int ACT>
-__device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint32_t (&vc)[32],
-                                              const float* ln_g, const float* ln_b, float rstd,
-                                              float nmr) {
+__device__ __forceinline__ void finish_chunk32(const uint32_t (&vc)[32], const float* __restrict__ ln_g,
+                                               const float* __restrict__ ln_b, bool ln_ident,
+                                               float rstd, float nmr, uint32_t (&pk)[16]) {
+  if constexpr (TAIL == kTailLayerNorm) {
+    const float2 r2 = make_float2(rstd, rstd), n2 = make_float2(nmr, nmr);
+    if (ln_ident) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t pk[4];
+      for (int j = 0; j < 16; ++j) {
+        const float2 y = __ffma2_rn(make_float2(__uint_as_float(vc[2 * j]), __uint_as_float(vc[2 * j + 1])), r2, n2);
+        pk[j] = Elem<T>::pack(y.x, y.y);
+      }
+    } else {
+      float4 g[8], b[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int i = j * 8 + e * 2;  // column within the 32-block
-      float2 y = make_float2(__uint_as_float(vc[i]), __uint_as_float(vc[i + 1]));
-      if constexpr (TAIL == kTailLayerNorm) {
-        const float2 g = *reinterpret_cast<const float2*>(ln_g + i);
-        const float2 b = *reinterpret_cast<const float2*>(ln_b + i);
-        y = __ffma2_rn(y, make_float2(rstd, rstd), make_float2(nmr, nmr));  // (v - mean) * rstd
-        y = __ffma2_rn(y, g, b);
-        pk[e] = Elem<T>::pack(y.x, y.y);
-      } else {
-        pk[e] = act_pack_f2<T, ACT>(y);
+      for (int j = 0; j < 8; ++j) {
+        g[j] = reinterpret_cast<const float4*>(ln_g)[j];
+        b[j] = reinterpret_cast<const float4*>(ln_b)[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float2 y0 = __ffma2_rn(make_float2(__uint_as_float(vc[4 * j]), __uint_as_float(vc[4 * j + 1])), r2, n2);
+        float2 y1 = __ffma2_rn(make_float2(__uint_as_float(vc[4 * j + 2]), __uint_as_float(vc[4 * j + 3])), r2, n2);
+        y0 = __ffma2_rn(y0, make_float2(g[j].x, g[j].y), make_float2(b[j].x, b[j].y));
+        y1 = __ffma2_rn(y1, make_float2(g[j].z, g[j].w), make_float2(b[j].z, b[j].w));
+        pk[2 * j] = Elem<T>::pack(y0.x, y0.y);
+        pk[2 * j + 1] = Elem<T>::pack(y1.x, y1.y);
       }
     }
-    *reinterpret_cast<uint4*>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) =
-        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      pk[j] = act_pack<T, ACT>(__uint_as_float(vc[2 * j]), __uint_as_float(vc[2 * j + 1]));
   }
 }
 
-// Kernel body shared by the single-CTA (CG = 1) and CTA-pair (CG = 2) forms. In the pair form
-// the cluster's two CTAs each own 128 rows of a 256-row unit and half of every weight's columns;
-// the leader (rank 0) issues cta_group::2 MMAs (M = 256) that read both CTAs' shared memory and
-// write both CTAs' TMEM. Loads of both CTAs complete on the leader's barriers; MMA commits
-// arrive on both CTAs' barriers; both CTAs' epilogues release a buffer on the leader's barrier.
+// Write one packed 32-column block of this thread's row into a 32-row x 64-byte staging tile
+// with the TMA SWIZZLE_64B pattern (16-byte chunk j of row r lands at j ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) =
+        make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+}
+
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG>
 __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const ChainArgs& args) {
   using L = ResidentLayout<K0, N, NL, NBUF, CG>;
@@ -249,17 +268,20 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     }
     *reinterpret_cast<uint4*>(smem + L::kOffBias + i * 16) = val;
   }
+  int ident_local = 1;
   if constexpr (TAIL == kTailLayerNorm) {
     for (int i = threadIdx.x; i < N; i += blockDim.x) {
       const T* g = reinterpret_cast<const T*>(args.gamma);
       const T* b = reinterpret_cast<const T*>(args.beta);
       ln_g[i] = g != nullptr ? Elem<T>::to_f(g[i]) : 1.0f;
       ln_b[i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
+      ident_local &= (ln_g[i] == 1.0f && ln_b[i] == 0.0f) ? 1 : 0;
     }
   }
   fence_proxy_async_smem();
   tc_fence_before();
-  __syncthreads();
+  // gamma == 1 and beta == 0 everywhere: the LayerNorm affine step is the identity
+  const bool ln_ident = __syncthreads_and(ident_local) != 0;
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (warp >= 2 && warp < 6) {
@@ -314,7 +336,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
         for (int p = 0; p < kPanels0; ++p) {
           if (!mbar_wait<kPair>(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer))
             goto producer_done;
-          if (!args.inject) {
+          if (args.inject != 1) {
             const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
             if constexpr (kPair) {
               if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
@@ -438,7 +460,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     // ---------------------------------------------------------------- epilogue
     const int g = (warp - 2) >> 2;  // TMEM buffer served by this group
     const int q = warp & 3;         // TMEM lane quarter accessible to this warp
-    uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes;
+    uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes * L::kStgBufs;
     const uint32_t stg_u32 = smem_u32(stg);
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + g * L::kBufCols;
     const uint32_t ready_bar[2] = {leader_bar(&act_ready[0]), leader_bar(&act_ready[NBUF - 1])};
@@ -483,13 +505,20 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
           const int row0 = unit * L::kUnitRows + static_cast<int>(rank) * kBM + q * 32;
 #pragma unroll
           for (int c = 0; c < N / 32; ++c) {
-            if (lane == 0) bulk_wait_group_read<0>();
+            uint32_t pk[16];
+            finish_chunk32<T, TAIL, kLastAct>(v[c], ln_g + c * 32, ln_b + c * 32, ln_ident, rstd, nmr, pk);
+            const int sb = L::kStgBufs == 2 ? (c & 1) : 0;
+            if (lane == 0) {
+              if constexpr (L::kStgBufs == 2) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
+            }
             __syncwarp();
-            stage_chunk32<T, TAIL, kLastAct>(stg, lane, v[c], ln_g + c * 32, ln_b + c * 32, rstd, nmr);
+            stage_chunk32(stg + sb * L::kStageBytes, lane, pk);
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0 && row0 < args.m) {
-              tma_store_2d(&tm.out, stg_u32, c * 32, row0);
+            if (lane == 0) {
+              // every lane-0 store is a bulk group (even when clipped away) so the ring of
+              // outstanding groups stays in step with the staging buffers
+              if (row0 < args.m) tma_store_2d(&tm.out, stg_u32 + sb * L::kStageBytes, c * 32, row0);
               bulk_commit_group();
             }
           }

@@ -126,9 +126,10 @@ GP_API int gp_set_timeout_ns(uint64_t ns);
  * bounded waits run out (no GPU fault; the kernel exits with a timeout status). 0 = off. */
 GP_API int gp_set_fault_injection(int mode);
 
-/* Kernel choice where several are compiled for one chain: 0 = default (CTA-pair kernels for the
- * MeshGraphNet family), 1 = alternative (single-CTA kernels). Process-wide; for A/B measurement and
- * tests. The environment variable GP_KERNEL_VARIANT sets the initial value. */
+/* Kernel choice where several are compiled for one chain: 0 = default, 1 = the other form
+ * (the MeshGraphNet family has a single-CTA and a CTA-pair kernel; the default is the faster
+ * one measured for that input width). Process-wide; for A/B measurement and tests. The
+ * environment variable GP_KERNEL_VARIANT sets the initial value. No reference counterpart. */
 GP_API int gp_set_kernel_variant(int variant);
 
 /* Number of kernels this library has launched in this process (for launch-count claims). */

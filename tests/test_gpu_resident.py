@@ -18,9 +18,9 @@ pytestmark = pytest.mark.gpu
 NONE, RELU = L.ACT_NONE, L.ACT_RELU
 
 
-@pytest.fixture(params=[0, 1], ids=["pair", "single"])
+@pytest.fixture(params=[0, 1], ids=["default", "other"])
 def variant(request):
-    """Run a test with the default (CTA-pair) kernels and with the single-CTA alternatives."""
+    """Run a test with the default kernels and with the other form (single-CTA / CTA-pair)."""
     L.set_kernel_variant(request.param)
     yield request.param
     L.set_kernel_variant(0)
