@@ -46,6 +46,11 @@ EXPORTED_SYMBOLS = (
     "gp_mgn_fullmlp_out",
     "gp_mgn_linears_out",
     "gp_testmlp_out",
+    "gp_dlrm_botmlp_out",
+    "gp_gc_edges_out",
+    "gp_gc_nodes_out",
+    "gp_nerf_a_out",
+    "gp_nerf_out",
     "gp_last_error",
     "gp_device_status",
     "gp_set_timeout_ns",
@@ -71,6 +76,7 @@ class GpSpec(ctypes.Structure):
         ("tail", ctypes.c_int),
         ("dtype", ctypes.c_int),
         ("ln_eps", ctypes.c_float),
+        ("skip_layer", ctypes.c_int),
     ]
 
 
@@ -91,6 +97,14 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_mgn_linears_out.restype = _INT
     lib.gp_testmlp_out.argtypes = [_I64] + [_P] * 9
     lib.gp_testmlp_out.restype = _INT
+    lib.gp_dlrm_botmlp_out.argtypes = [_I64] + [_P] * 9
+    lib.gp_dlrm_botmlp_out.restype = _INT
+    for name in ("gp_gc_edges_out", "gp_gc_nodes_out"):
+        getattr(lib, name).argtypes = [_I64, _INT, _INT] + [_P] * 9
+        getattr(lib, name).restype = _INT
+    for name in ("gp_nerf_a_out", "gp_nerf_out"):
+        getattr(lib, name).argtypes = [_I64, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P]
+        getattr(lib, name).restype = _INT
     lib.gp_last_error.argtypes = []
     lib.gp_last_error.restype = ctypes.c_char_p
     lib.gp_device_status.argtypes = [_INT, _INT, ctypes.POINTER(_INT)]
@@ -128,7 +142,7 @@ def check(code: int) -> None:
         raise GpError(code, last_error())
 
 
-def make_spec(widths, acts, tail=TAIL_NONE, dtype=GP_F16, ln_eps=1e-5) -> GpSpec:
+def make_spec(widths, acts, tail=TAIL_NONE, dtype=GP_F16, ln_eps=1e-5, skip_layer=0) -> GpSpec:
     s = GpSpec()
     n = len(widths) - 1
     if n < 1 or n > GP_MAX_LAYERS:
@@ -141,6 +155,7 @@ def make_spec(widths, acts, tail=TAIL_NONE, dtype=GP_F16, ln_eps=1e-5) -> GpSpec
     s.tail = int(tail)
     s.dtype = int(dtype)
     s.ln_eps = float(ln_eps)
+    s.skip_layer = int(skip_layer)
     return s
 
 

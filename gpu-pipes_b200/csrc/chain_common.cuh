@@ -33,6 +33,9 @@ struct ChainArgs {
   const void* gamma;                  // [N_last] LayerNorm scale
   const void* beta;                   // [N_last] LayerNorm shift
   const void* resid;                  // residual rows [M, N_last] (kTailResidualLN)
+  void* out;                          // output rows [M, N_out]
+  const void* head_w;                 // narrow head [N_last, HEAD_N] (stream kernel), or null
+  const void* head_b;                 // narrow head bias [HEAD_N], or null
   float ln_eps;
   int* status;                        // device status word (0 = ok)
   unsigned long long timeout_ns;      // budget of every bounded wait

@@ -22,6 +22,13 @@ GP_DECLARE2(probe_2l_f16_k128)
 GP_DECLARE(launch_mgn_ln_bf16_k384_pair)
 GP_DECLARE(launch_mgn_ln_bf16_k256_single)
 GP_DECLARE(launch_mgn_ln_bf16_k128_single)
+GP_DECLARE(launch_dlrm_bot_f16)
+GP_DECLARE(launch_gc_silu_bf16_k1536)
+GP_DECLARE(launch_gc_relu_f16_k1536)
+GP_DECLARE(launch_gc_relu_bf16_k1536)
+GP_DECLARE(launch_gc_relu_f16_k1024)
+GP_DECLARE(launch_nerf_f16)
+GP_DECLARE(launch_nerf_trunk_f16)
 #undef GP_DECLARE2
 #undef GP_DECLARE
 
@@ -52,6 +59,16 @@ static const ChainEntry kChains[] = {
     {"probe_1l_f16_k128_single", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_NONE, launch_probe_1l_f16_k128_single, 1},
     {"probe_2l_f16_k128", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_pair, 0},
     {"probe_2l_f16_k128_single", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_single, 1},
+    // weight-streaming chains (wide layers)
+    {"dlrm_bot_f16", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16, 0},
+    {"gc_silu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {GP_ACT_SILU, NO}, GP_TAIL_LAYERNORM, launch_gc_silu_bf16_k1536, 0},
+    {"gc_relu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_bf16_k1536, 0},
+    {"gc_relu_f16_k1536", GP_F16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_f16_k1536, 0},
+    {"gc_relu_f16_k1024", GP_F16, 2, {1024, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_f16_k1024, 0},
+    {"nerf_f16", GP_F16, 9, {64, 256, 256, 256, 256, 256, 256, 256, 256, 4}, {R, R, R, R, R, R, R, R, NO},
+     GP_TAIL_NONE, launch_nerf_f16, 0, 5},
+    {"nerf_trunk_f16", GP_F16, 8, {64, 256, 256, 256, 256, 256, 256, 256, 256}, {R, R, R, R, R, R, R, R},
+     GP_TAIL_NONE, launch_nerf_trunk_f16, 0, 5},
 };
 #undef MGN
 #undef R
@@ -68,6 +85,7 @@ void set_kernel_variant(int v) { g_variant.store(v); }
 
 static bool matches(const ChainEntry& e, const gp_mlp_spec& s) {
   if (e.dtype != s.dtype || e.n_layers != s.n_layers || e.tail != s.tail) return false;
+  if (e.skip != s.skip_layer) return false;
   for (int l = 0; l <= s.n_layers; ++l)
     if (e.widths[l] != s.widths[l]) return false;
   for (int l = 0; l < s.n_layers; ++l) {

@@ -31,6 +31,7 @@ struct ChainEntry {
   int tail;
   LaunchFn launch;
   int variant = 0;  // 0 = default kernel for the chain; others selectable for A/B measurements
+  int skip = 0;     // skip-concat layer (gp_mlp_spec.skip_layer)
 };
 
 const ChainEntry* find_chain(const gp_mlp_spec& s);

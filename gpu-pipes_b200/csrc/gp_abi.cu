@@ -139,8 +139,12 @@ static int validate(const gp_mlp_spec* spec, int64_t m, const void* x, const voi
   if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
   if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
   for (int l = 0; l <= spec->n_layers; ++l)
-    if (spec->widths[l] <= 0 || spec->widths[l] % 8 != 0)
-      return set_error(GP_ERR_SHAPE, "width[%d] = %d must be a positive multiple of 8", l, spec->widths[l]);
+    if (spec->widths[l] <= 0)
+      return set_error(GP_ERR_SHAPE, "width[%d] = %d must be positive", l, spec->widths[l]);
+  if (spec->widths[0] % 8 != 0)
+    return set_error(GP_ERR_SHAPE, "input width %d must be a multiple of 8 (16-byte rows)", spec->widths[0]);
+  if (spec->skip_layer < 0 || spec->skip_layer >= spec->n_layers)
+    return set_error(GP_ERR_SHAPE, "skip_layer %d out of range [0, %d)", spec->skip_layer, spec->n_layers);
   if (x == nullptr || out == nullptr || w == nullptr)
     return set_error(GP_ERR_ARG, "x, w and out must not be NULL");
   if (!aligned(x, 16) || !aligned(out, 16))
@@ -213,6 +217,7 @@ int fused_mlp(const gp_mlp_spec* spec, int64_t m, const void* x, const void* con
   c.args.gamma = gamma;
   c.args.beta = beta;
   c.args.resid = x;
+  c.args.out = out;
   c.args.ln_eps = spec->ln_eps;
   c.args.status = st->status;
   c.args.timeout_ns = g_timeout_ns.load();
@@ -266,6 +271,77 @@ int gp_mgn_linears_out(int64_t m, int k0, const void* x, const void* w1, const v
   gp_mlp_spec s = mgn_spec(k0, GP_TAIL_NONE, GP_F16);
   const void* w[3] = {w1, w2, w3};
   const void* b[3] = {b1, b2, b3};
+  return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_dlrm_botmlp_out(int64_t m, const void* x, const void* w1, const void* b1, const void* w2,
+                       const void* b2, const void* w3, const void* b3, void* out, void* stream) {
+  gp_mlp_spec s{};
+  s.n_layers = 3;
+  const int wd[4] = {16, 512, 256, 128};
+  for (int i = 0; i < 4; ++i) s.widths[i] = wd[i];
+  for (int i = 0; i < 3; ++i) s.act[i] = GP_ACT_RELU;
+  s.tail = GP_TAIL_NONE;
+  s.dtype = GP_F16;
+  const void* w[3] = {w1, w2, w3};
+  const void* b[3] = {b1, b2, b3};
+  return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+static int gc_mlp(int64_t m, int k0, int dtype, int act, const void* x, const void* w0,
+                  const void* b0, const void* w1, const void* b1, const void* gamma,
+                  const void* beta, void* out, void* stream) {
+  gp_mlp_spec s{};
+  s.n_layers = 2;
+  s.widths[0] = k0;
+  s.widths[1] = s.widths[2] = 512;
+  s.act[0] = act;
+  s.act[1] = GP_ACT_NONE;
+  s.tail = GP_TAIL_LAYERNORM;
+  s.dtype = dtype;
+  s.ln_eps = 1e-5f;
+  const void* w[2] = {w0, w1};
+  const void* b[2] = {b0, b1};
+  return fused_mlp(&s, m, x, w, b, gamma, beta, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_gc_edges_out(int64_t m, int dtype, int act, const void* x, const void* w0, const void* b0,
+                    const void* w1, const void* b1, const void* gamma, const void* beta, void* out,
+                    void* stream) {
+  return gc_mlp(m, 1536, dtype, act, x, w0, b0, w1, b1, gamma, beta, out, stream);
+}
+
+int gp_gc_nodes_out(int64_t m, int dtype, int act, const void* x, const void* w0, const void* b0,
+                    const void* w1, const void* b1, const void* gamma, const void* beta, void* out,
+                    void* stream) {
+  return gc_mlp(m, 1024, dtype, act, x, w0, b0, w1, b1, gamma, beta, out, stream);
+}
+
+static gp_mlp_spec nerf_spec(bool head) {
+  gp_mlp_spec s{};
+  s.n_layers = head ? 9 : 8;
+  s.widths[0] = 64;
+  for (int i = 1; i <= 8; ++i) s.widths[i] = 256;
+  if (head) s.widths[9] = 4;
+  for (int i = 0; i < 8; ++i) s.act[i] = GP_ACT_RELU;
+  s.act[8] = GP_ACT_NONE;
+  s.tail = GP_TAIL_NONE;
+  s.dtype = GP_F16;
+  s.skip_layer = 5;
+  return s;
+}
+
+int gp_nerf_a_out(int64_t m, const void* x, const void* const* w, const void* const* b, void* out,
+                  void* stream) {
+  if (w == nullptr) return set_error(GP_ERR_ARG, "w is NULL");
+  gp_mlp_spec s = nerf_spec(false);
+  return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* const* b, void* out,
+                void* stream) {
+  if (w == nullptr) return set_error(GP_ERR_ARG, "w is NULL");
+  gp_mlp_spec s = nerf_spec(true);
   return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
 }
 

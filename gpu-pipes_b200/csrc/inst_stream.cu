@@ -1,0 +1,56 @@
+// Instantiations of the weight-streaming chain kernel (wide layers).
+#include <type_traits>
+
+#include "stream_launch.cuh"
+
+namespace gp {
+
+// DLRM bottom MLP (common/mlps.py:23-35 DlrmMlp([13, 512, 256, 128])), input padded 13 -> 16.
+struct ChainDlrmBot {
+  using T = __half;
+  static constexpr int NL = 3;
+  __host__ __device__ static constexpr int K(int l) { return l == 0 ? 16 : (l == 1 ? 512 : 256); }
+  __host__ __device__ static constexpr int N(int l) { return l == 0 ? 512 : (l == 1 ? 256 : 128); }
+  __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
+  static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+};
+
+// GraphCast-style edge / node MLP (apps/gc_edges/torch/model.py:4-14): K0 -> 512 act -> 512, LN.
+template <typename TT, int K0_, int ACT0>
+struct ChainGc {
+  using T = TT;
+  static constexpr int NL = 2;
+  __host__ __device__ static constexpr int K(int l) { return l == 0 ? K0_ : 512; }
+  __host__ __device__ static constexpr int N(int) { return 512; }
+  __host__ __device__ static constexpr int ACT(int l) { return l == 0 ? ACT0 : kActNone; }
+  static constexpr int SKIP = 0, TAIL = kTailLayerNorm, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = std::is_same<TT, __nv_bfloat16>::value;
+};
+
+// NeRF trunk without view directions (apps/nerf_full/torch/model.py:5-66, use_viewdirs=False):
+// 63(64) -> 256 x5 (ReLU), concat x -> 319(320) -> 256, 256 -> 256 x2 (ReLU), decode 256 -> 4.
+struct ChainNerf {
+  using T = __half;
+  static constexpr int NL = 8;
+  __host__ __device__ static constexpr int K(int l) { return l == 0 ? 64 : (l == 5 ? 320 : 256); }
+  __host__ __device__ static constexpr int N(int) { return 256; }
+  __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
+  static constexpr int SKIP = 5, TAIL = kTailHead, HEAD_N = 4, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+};
+
+// The same trunk without the head: layer 8's ReLU output is the result (apps/nerf_a).
+struct ChainNerfTrunk : ChainNerf {
+  static constexpr int TAIL = kTailNone, HEAD_N = 0;
+};
+
+int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot>(c); }
+int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>>(c); }
+int launch_gc_relu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActRelu>>(c); }
+int launch_gc_relu_f16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1536, kActRelu>>(c); }
+int launch_gc_relu_f16_k1024(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1024, kActRelu>>(c); }
+int launch_nerf_f16(const LaunchCtx& c) { return launch_stream<ChainNerf>(c); }
+int launch_nerf_trunk_f16(const LaunchCtx& c) { return launch_stream<ChainNerfTrunk>(c); }
+
+}  // namespace gp

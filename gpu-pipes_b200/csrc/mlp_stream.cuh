@@ -1,0 +1,482 @@
+// Fused MLP chain with weights streamed from L2 ("wide" chains: hidden layers up to 512 wide).
+//
+// Covers the reference apps whose weights do not fit in one SM's shared memory:
+//   dlrm_botmlp  apps/dlrm_botmlp/pipelined/dlrm_botmlp_pl.cuh:139-173  13(16)->512->256->128, ReLU
+//   gc_edges     apps/gc_edges/pipelined/gc_edges_pl.cuh:112-142        1536->512->512 + LN(512)
+//   gc_nodes     (same kernel family, K0 = 1024)
+//   nerf_a       apps/nerf_a/pipelined/nerf_a_pl.cuh:183-227            64->256 x5, [h || x] -> 256,
+//                                                                       256 x2, then a 256->4 head
+// The reference gives every layer (and the concat / LN) its own CTA and moves activation tiles
+// between them through L2 ring queues; the concat is a separate copy stage
+// (common/pipe_concat.cuh:47-74). Here one persistent CTA runs the whole chain for a 128-row tile:
+//
+//   warp 0      TMA producer: x tiles (a resident 64-column tile, or a ring of 64-column panels
+//               for wide inputs) and every layer's weights as 32-row x (<=256)-column stages
+//               through an mbarrier ring (L2-resident: every CTA streams the same weights).
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
+//   warps 2-5   epilogue; thread t owns row t of the tile (TMEM lane t).
+//
+// Activations never leave the SM: the epilogue of layer l writes bias + activation of the fp32
+// accumulator as 16-bit values straight into shared memory, in the K-major SWIZZLE_128B layout
+// the next layer's MMA reads as its A operand. The skip concat of NeRF is free: the A operand of
+// that layer is the activation panels followed by the resident x panel. Accumulators hold up to
+// 512 fp32 columns (N = 512 runs as two 256-wide MMAs per K step). Tails: LayerNorm in two passes
+// over TMEM (row statistics, then normalise), or a narrow head (N < 64, e.g. NeRF 256 -> 4,
+// DLRM 256 -> 1) computed on CUDA cores from the last hidden row held by the thread.
+#pragma once
+
+#include "chain_common.cuh"
+#include "gp_ptx.cuh"
+#include "mlp_resident.cuh"
+
+namespace gp {
+
+constexpr int kTailHead = 3;  // narrow output layer on CUDA cores (stream kernel only)
+
+// Chain description used as a template argument:
+//   using T;  NL (tensor-core layers); K(l), N(l), ACT(l); SKIP (layer whose A operand is
+//   [act || x], 0 = none); TAIL (kTailNone / kTailLayerNorm / kTailHead); HEAD_N, HEAD_ACT;
+//   HIDDEN_F16: with bf16 data, keep hidden activations in fp16 (11-bit mantissa instead of 8)
+//   and run layers >= 1 as fp16 x fp16 MMAs on fp16 copies of their weights (bf16 -> fp16 is
+//   exact for weights within fp16 range). Input, first layer and output stay bf16.
+template <class C>
+struct StreamLayout {
+  static constexpr int NL = C::NL;
+  static constexpr int K0 = C::K(0);
+  static constexpr bool kXRes = K0 <= kPanel;  // whole x tile resident (one 64-column panel)
+  static constexpr int kBK = 32;               // weight rows per B stage
+  __host__ __device__ static constexpr int maxN() {
+    int m = 0;
+    for (int l = 0; l < NL; ++l) m = C::N(l) > m ? C::N(l) : m;
+    return m;
+  }
+  __host__ __device__ static constexpr int actW() {  // widest activation that feeds a later layer
+    int m = 64;
+    for (int l = 0; l + 1 < NL; ++l) m = C::N(l) > m ? C::N(l) : m;
+    return m;
+  }
+  __host__ __device__ static constexpr int biasFloats() {
+    int s = 0;
+    for (int l = 0; l < NL; ++l) s += C::N(l);
+    return s;
+  }
+  __host__ __device__ static constexpr int biasOff(int l) {
+    int s = 0;
+    for (int i = 0; i < l; ++i) s += C::N(i);
+    return s;
+  }
+  static constexpr int kMaxN = maxN();
+  static_assert(kMaxN <= 512, "accumulators are at most 512 columns");
+  static constexpr int kNB = kMaxN < 256 ? kMaxN : 256;  // N columns per MMA / per B stage
+  static constexpr int kActBytes = kBM * actW() * 2;
+  static constexpr int kXBytes = kXRes ? 2 * kPanelBytes : 0;  // double-buffered resident x
+  static constexpr int kBStageBytes = kBK * kNB * 2;
+  static constexpr int kBiasBytes = ((biasFloats() * 4 + 1023) / 1024) * 1024;
+  static constexpr int kLnBytes = C::TAIL == kTailLayerNorm ? 2 * C::N(NL - 1) * 4 : 0;
+  static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * 16 * 4 + 64 * 4) : 0;
+  static constexpr int kStageBytes = 32 * 64;  // per epilogue warp output staging (32 x 32 x 2 B)
+  static constexpr int kStgBytes = C::TAIL == kTailHead ? 0 : 4 * kStageBytes;
+  static constexpr int kBarBytes = 512;
+  static constexpr int kFixed = kActBytes + kXBytes + kBiasBytes + kLnBytes + kHeadBytes +
+                                kStgBytes + kBarBytes + 1024;  // + alignment of the staging area
+  // ring of x panels (streamed x only), then as many B stages as fit (at most 8)
+  static constexpr int kXStages = kXRes ? 0 : 2;
+  static constexpr int kBStagesRaw = (kSmemLimit - kFixed - kXStages * kPanelBytes) / kBStageBytes;
+  static constexpr int kBStages = kBStagesRaw > 8 ? 8 : kBStagesRaw;
+  static_assert(kBStages >= 2, "shared memory budget");
+  static constexpr int kOffAct = 0;
+  static constexpr int kOffX = kOffAct + kActBytes;                     // resident x or x ring
+  static constexpr int kOffB = kOffX + (kXRes ? kXBytes : kXStages * kPanelBytes);
+  static constexpr int kOffBias = kOffB + kBStages * kBStageBytes;
+  static constexpr int kOffLn = kOffBias + kBiasBytes;
+  static constexpr int kOffHead = kOffLn + kLnBytes;
+  static constexpr int kOffStg = ((kOffHead + kHeadBytes + 1023) / 1024) * 1024;
+  static constexpr int kOffBar = ((kOffStg + kStgBytes + 15) / 16) * 16;
+  static constexpr int kSmemBytes = kOffBar + kBarBytes;
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+  static_assert(kOffX % 1024 == 0 && kOffB % 1024 == 0 && kOffStg % 512 == 0, "alignment");
+  static constexpr int kThreads = 192;
+};
+
+// Number of 16-wide K steps of layer l in 64-column panel p, and in its 32-row half h.
+template <class C>
+__host__ __device__ constexpr int ksteps_in(int l, int p, int h) {
+  const int total = C::K(l) / 16;
+  int first = p * 4 + h * 2;
+  int n = total - first;
+  return n <= 0 ? 0 : (n > 2 ? 2 : n);
+}
+
+template <class C>
+__global__ void __launch_bounds__(192, 1)
+    mlp_stream_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  using T = typename C::T;
+  using L = StreamLayout<C>;
+  constexpr int NL = C::NL;
+  constexpr int kBS = L::kBStages;
+  constexpr int kNB = L::kNB;
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* b_full = bars;          // [8]
+  uint64_t* b_empty = bars + 8;     // [8]
+  uint64_t* x_full = bars + 16;     // [2]  x ring slots or resident x buffers
+  uint64_t* x_empty = bars + 18;    // [2]
+  uint64_t* acc_full = bars + 20;
+  uint64_t* act_ready = bars + 21;
+  uint64_t* mma_done = bars + 22;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+  float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
+  float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
+  float* ln_b = ln_g + C::N(NL - 1);
+  float* head_w = reinterpret_cast<float*>(smem + L::kOffHead);  // [N_last][16] fp32
+  float* head_b = head_w + C::N(NL - 1) * 16;                    // [16]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 8; ++s) {
+      mbar_init(smem_u32(&b_full[s]), 1);
+      mbar_init(smem_u32(&b_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&x_full[s]), 1);
+      mbar_init(smem_u32(&x_empty[s]), 1);
+    }
+    mbar_init(smem_u32(acc_full), 1);
+    mbar_init(smem_u32(act_ready), 4);
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) prefetch_tmap(&tm.x);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  // fp32 biases, LayerNorm parameters and head weights
+  for (int l = 0; l < NL; ++l) {
+    const T* b = reinterpret_cast<const T*>(args.bias[l]);
+    for (int i = threadIdx.x; i < C::N(l); i += blockDim.x)
+      bias_s[L::biasOff(l) + i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
+  }
+  if constexpr (C::TAIL == kTailLayerNorm) {
+    const T* g = reinterpret_cast<const T*>(args.gamma);
+    const T* b = reinterpret_cast<const T*>(args.beta);
+    for (int i = threadIdx.x; i < C::N(NL - 1); i += blockDim.x) {
+      ln_g[i] = g != nullptr ? Elem<T>::to_f(g[i]) : 1.0f;
+      ln_b[i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
+    }
+  }
+  if constexpr (C::TAIL == kTailHead) {
+    // head weights [N_last, HEAD_N] (row-major, 16-bit) -> fp32 [N_last][16], zero padded
+    const T* hw = reinterpret_cast<const T*>(args.head_w);
+    const T* hb = reinterpret_cast<const T*>(args.head_b);
+    for (int i = threadIdx.x; i < C::N(NL - 1) * 16; i += blockDim.x) {
+      const int k = i / 16, o = i % 16;
+      head_w[i] = o < C::HEAD_N ? Elem<T>::to_f(hw[k * C::HEAD_N + o]) : 0.0f;
+    }
+    for (int i = threadIdx.x; i < 16; i += blockDim.x)
+      head_b[i] = (i < C::HEAD_N && hb != nullptr) ? Elem<T>::to_f(hb[i]) : 0.0f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
+  const int num_tiles = args.num_tiles;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();
+      const uint64_t stream = l2_policy_evict_first();
+      int bs = 0, xs = 0;
+      uint32_t bph = 0, xph = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if constexpr (L::kXRes) {
+          if (!mbar_wait(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
+          if (args.inject != 1) {
+            mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes);
+            tma_load_2d_hint(smem_u32(smem + L::kOffX + xs * kPanelBytes), &tm.x,
+                             smem_u32(&x_full[xs]), 0, tile * kBM, stream);
+          }
+          if (++xs == 2) { xs = 0; xph ^= 1; }
+        }
+#pragma unroll 1
+        for (int l = 0; ok && l < NL; ++l) {
+          const int panels = (C::K(l) + kPanel - 1) / kPanel;
+          const int nchunks = (C::N(l) + kNB - 1) / kNB;
+          const int nb_boxes = (C::N(l) < kNB ? C::N(l) : kNB) / 64;
+#pragma unroll 1
+          for (int p = 0; ok && p < panels; ++p) {
+            if (!L::kXRes && l == 0) {
+              if (!mbar_wait(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
+              if (args.inject != 1) {
+                mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes);
+                tma_load_2d_hint(smem_u32(smem + L::kOffX + xs * kPanelBytes), &tm.x,
+                                 smem_u32(&x_full[xs]), p * kPanel, tile * kBM, stream);
+              }
+              if (++xs == 2) { xs = 0; xph ^= 1; }
+            }
+#pragma unroll 1
+            for (int nc = 0; ok && nc < nchunks; ++nc)
+#pragma unroll 1
+              for (int h = 0; h < 2; ++h) {
+                if (ksteps_in<C>(l, p, h) == 0) continue;
+                if (!mbar_wait(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
+                mbar_arrive_expect_tx(smem_u32(&b_full[bs]), nb_boxes * L::kBK * 128);
+                const uint32_t dst = smem_u32(smem + L::kOffB + bs * L::kBStageBytes);
+                for (int nb = 0; nb < nb_boxes; ++nb)
+                  tma_load_2d_hint(dst + nb * (L::kBK * 128), &tm.w[l], smem_u32(&b_full[bs]),
+                                   nc * kNB + nb * 64, p * kPanel + h * L::kBK, keep);
+                if (++bs == kBS) { bs = 0; bph ^= 1; }
+              }
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t act_sm = smem_u32(smem + L::kOffAct);
+      const uint32_t x_sm = smem_u32(smem + L::kOffX);
+      const uint32_t b_sm = smem_u32(smem + L::kOffB);
+      int bs = 0, xs = 0;
+      uint32_t bph = 0, xph = 0, rph = 0;
+      bool first = true, ok = true;
+#pragma unroll 1
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int xcur = xs;  // resident x buffer of this tile
+#pragma unroll 1
+        for (int l = 0; ok && l < NL; ++l) {
+          if (!first) {
+            if (!mbar_wait(smem_u32(act_ready), rph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            rph ^= 1;
+          }
+          first = false;
+          tc_fence_after();
+          const int panels = (C::K(l) + kPanel - 1) / kPanel;
+          const int nchunks = (C::N(l) + kNB - 1) / kNB;
+          const int ncols = C::N(l) < kNB ? C::N(l) : kNB;
+          const int ab_bf16 = (l == 0 || !C::HIDDEN_F16) ? Elem<T>::kIsBf16 : 0;
+          const uint32_t idesc = make_idesc_f16(kBM, ncols, ab_bf16, 0, 1);
+#pragma unroll 1
+          for (int p = 0; ok && p < panels; ++p) {
+            uint32_t a_base;
+            const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1);
+            if (from_x) {
+              if constexpr (L::kXRes) {
+                if (l == 0) {
+                  if (!mbar_wait(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
+                  tc_fence_after();
+                }
+                a_base = x_sm + xcur * kPanelBytes;
+              } else {
+                if (!mbar_wait(smem_u32(&x_full[xs]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
+                tc_fence_after();
+                a_base = x_sm + xs * kPanelBytes;
+              }
+            } else {
+              a_base = act_sm + p * kPanelBytes;
+            }
+#pragma unroll 1
+            for (int nc = 0; ok && nc < nchunks; ++nc)
+#pragma unroll 1
+              for (int h = 0; h < 2; ++h) {
+                const int ks = ksteps_in<C>(l, p, h);
+                if (ks == 0) continue;
+                if (!mbar_wait(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t bst = b_sm + bs * L::kBStageBytes;
+                for (int k = 0; k < ks; ++k) {
+                  const int kin = h * 2 + k;  // 16-wide K step within the 64-column panel
+                  const uint64_t adesc = make_sdesc_sw128(a_base + kin * 32, 16, 1024);
+                  const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK * 128, 1024);
+                  mma_ss(tmem_base + nc * kNB, adesc, bdesc, idesc,
+                         (p == 0 && h == 0 && k == 0) ? 0u : 1u);
+                }
+                mma_commit(smem_u32(&b_empty[bs]));
+                if (++bs == kBS) { bs = 0; bph ^= 1; }
+              }
+            if (!L::kXRes && l == 0) {
+              mma_commit(smem_u32(&x_empty[xs]));
+              if (++xs == 2) { xs = 0; xph ^= 1; }
+            }
+          }
+          if constexpr (L::kXRes) {
+            const int last_x_layer = C::SKIP != 0 ? C::SKIP : 0;
+            if (l == last_x_layer) mma_commit(smem_u32(&x_empty[xcur]));
+          }
+          mma_commit(smem_u32(acc_full));
+        }
+        if constexpr (L::kXRes) {
+          if (++xs == 2) { xs = 0; xph ^= 1; }
+        }
+      }
+      mma_commit(smem_u32(mma_done));
+      volatile int no_abort = 0;
+      WaitCtx drain{args.status, &no_abort, args.timeout_ns};
+      mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // row within the tile
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes;
+    uint8_t* act = smem + L::kOffAct;
+    uint32_t acc_ph = 0;
+    bool ok = true;
+    auto release = [&]() {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(act_ready));
+    };
+#pragma unroll 1
+    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      const int64_t row = static_cast<int64_t>(tile) * kBM + r;
+      const int row0 = tile * kBM + q * 32;
+#pragma unroll 1
+      for (int l = 0; l < NL; ++l) {
+        if (!mbar_wait(smem_u32(acc_full), acc_ph, wctx, kDevTimeoutEpilogue)) { ok = false; break; }
+        acc_ph ^= 1;
+        tc_fence_after();
+        const float* bl = bias_s + L::biasOff(l);
+        const int act_id = C::ACT(l);
+        if (l + 1 < NL) {
+          // hidden layer: bias + activation -> 16-bit A operand of the next layer (K-major SW128)
+#pragma unroll 1
+          for (int c = 0; c < C::N(l) / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(t_lane + c * 32, v);
+            tmem_wait_ld();
+            uint8_t* line = act + (c >> 1) * kPanelBytes + r * 128;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = j * 8 + e * 2;
+                const float2 bb = *reinterpret_cast<const float2*>(bl + c * 32 + i);
+                const float y0 = apply_act(act_id, __uint_as_float(v[i]) + bb.x);
+                const float y1 = apply_act(act_id, __uint_as_float(v[i + 1]) + bb.y);
+                pk[e] = C::HIDDEN_F16 ? Elem<__half>::pack(y0, y1) : Elem<T>::pack(y0, y1);
+              }
+              const int chunk = (c & 1) * 4 + j;
+              *reinterpret_cast<uint4*>(line + ((chunk ^ (r & 7)) * 16)) =
+                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+          fence_proxy_async_smem();
+          release();
+        } else if constexpr (C::TAIL == kTailHead) {
+          // last tensor layer + activation, then the narrow head on CUDA cores
+          float o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = 0.0f;
+#pragma unroll 1
+          for (int c = 0; c < C::N(l) / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(t_lane + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int k = c * 32 + i;
+              const float y = apply_act(act_id, __uint_as_float(v[i]) + bl[k]);
+              const float4* w4 = reinterpret_cast<const float4*>(head_w + k * 16);
+#pragma unroll
+              for (int o4 = 0; o4 < (C::HEAD_N + 3) / 4; ++o4) {
+                const float4 w = w4[o4];
+                o[o4 * 4 + 0] = fmaf(y, w.x, o[o4 * 4 + 0]);
+                o[o4 * 4 + 1] = fmaf(y, w.y, o[o4 * 4 + 1]);
+                o[o4 * 4 + 2] = fmaf(y, w.z, o[o4 * 4 + 2]);
+                o[o4 * 4 + 3] = fmaf(y, w.w, o[o4 * 4 + 3]);
+              }
+            }
+          }
+          release();
+          if (row < args.m) {
+            T* dst = reinterpret_cast<T*>(args.out) + row * C::HEAD_N;
+#pragma unroll
+            for (int i = 0; i < C::HEAD_N; ++i) {
+              const float y = apply_act(C::HEAD_ACT, o[i] + head_b[i]);
+              if constexpr (Elem<T>::kIsBf16) dst[i] = __float2bfloat16_rn(y); else dst[i] = __float2half_rn(y);
+            }
+          }
+        } else {
+          // last layer: optional LayerNorm (statistics pass over TMEM), then store via staging
+          float mean = 0.f, rstd = 1.f;
+          if constexpr (C::TAIL == kTailLayerNorm) {
+            float s = 0.f, sq = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < C::N(l) / 32; ++c) {
+              uint32_t v[32];
+              tmem_ld32(t_lane + c * 32, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float y = __uint_as_float(v[i]) + bl[c * 32 + i];
+                s += y;
+                sq = fmaf(y, y, sq);
+              }
+            }
+            mean = s * (1.0f / C::N(l));
+            rstd = rsqrtf(fmaxf(sq * (1.0f / C::N(l)) - mean * mean, 0.0f) + args.ln_eps);
+          }
+#pragma unroll 1
+          for (int c = 0; c < C::N(l) / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(t_lane + c * 32, v);
+            tmem_wait_ld();
+            if (c + 1 == C::N(l) / 32) release();  // the accumulator is fully read
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float y0 = __uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i];
+              float y1 = __uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1];
+              if constexpr (C::TAIL == kTailLayerNorm) {
+                y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
+                y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
+              } else {
+                y0 = apply_act(act_id, y0);
+                y1 = apply_act(act_id, y1);
+              }
+              pk[i] = Elem<T>::pack(y0, y1);
+            }
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+            stage_chunk32(stg, lane, pk);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(stg), c * 32, row0);
+              bulk_commit_group();
+            }
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace gp

@@ -46,8 +46,11 @@ def _stream(t: torch.Tensor) -> ctypes.c_void_p:
 
 
 def fused_mlp_out(x, weights, biases, out, *, acts, tail=L.TAIL_NONE, gamma=None, beta=None,
-                  ln_eps=1e-5) -> None:
-    """Generic chain: out = tail(act_L(... act_1(x W_1 + b_1) ...)). Weights are [K, N]."""
+                  ln_eps=1e-5, skip_layer=0) -> None:
+    """Generic chain: out = tail(act_L(... act_1(x W_1 + b_1) ...)). Weights are [K, N].
+
+    skip_layer = s > 0: layer s reads [output of layer s-1 || x] and its weight is
+    [N_{s-1} + K0, N_s] (the NeRF skip connection)."""
     _check_input("x", x)
     dt = _DT.get(x.dtype)
     if dt is None:
@@ -62,11 +65,12 @@ def fused_mlp_out(x, weights, biases, out, *, acts, tail=L.TAIL_NONE, gamma=None
         raise RuntimeError("x and out must be 2-D")
     widths = [x.shape[1]] + [w.shape[1] for w in weights]
     for i, w in enumerate(weights):
-        if w.dim() != 2 or w.shape[0] != widths[i]:
-            raise RuntimeError(f"w{i + 1} has shape {tuple(w.shape)}, expected [{widths[i]}, N]")
+        k = widths[i] + (widths[0] if skip_layer and i == skip_layer else 0)
+        if w.dim() != 2 or w.shape[0] != k:
+            raise RuntimeError(f"w{i + 1} has shape {tuple(w.shape)}, expected [{k}, N]")
     if out.shape[0] != x.shape[0] or out.shape[1] != widths[-1]:
         raise RuntimeError(f"out has shape {tuple(out.shape)}, expected [{x.shape[0]}, {widths[-1]}]")
-    spec = L.make_spec(widths, acts, tail, dt, ln_eps)
+    spec = L.make_spec(widths, acts, tail, dt, ln_eps, skip_layer)
     n = len(weights)
     wp = (ctypes.c_void_p * n)(*[w.data_ptr() for w in weights])
     bp = (ctypes.c_void_p * n)(*[(b.data_ptr() if b is not None else None) for b in biases])
@@ -142,8 +146,65 @@ def testmlp(x, w1, b1, w2, b2, w3, b3) -> torch.Tensor:
     return out
 
 
+# ------------------------------------------------------------------------------------------------
+# DLRM bottom MLP (apps/dlrm_botmlp), GraphCast MLPs (apps/gc_edges, apps/gc_nodes), NeRF
+# ------------------------------------------------------------------------------------------------
+def _out_like(x, n):
+    return torch.zeros(x.shape[0], n, dtype=x.dtype, device=x.device)
+
+
+def dlrm_botmlp_out(x, w1, b1, w2, b2, w3, b3, out) -> None:
+    """x [M, 16] (13 features zero padded) -> 512 -> 256 -> 128, ReLU after every layer."""
+    fused_mlp_out(x, [w1, w2, w3], [b1, b2, b3], out, acts=[L.ACT_RELU] * 3)
+
+
+def dlrm_botmlp(x, w1, b1, w2, b2, w3, b3) -> torch.Tensor:
+    out = _out_like(x, 128)
+    dlrm_botmlp_out(x, w1, b1, w2, b2, w3, b3, out)
+    return out
+
+
+def gc_edges_out(x, w0, b0, w1, b1, ga, be, out, act=L.ACT_RELU) -> None:
+    """x [M, 1536] -> 512 (act; ReLU as in the reference, SiLU for GraphCast) -> 512, LayerNorm."""
+    fused_mlp_out(x, [w0, w1], [b0, b1], out, acts=[act, L.ACT_NONE], tail=L.TAIL_LAYERNORM,
+                  gamma=ga, beta=be, ln_eps=1e-5)
+
+
+def gc_edges(x, w0, b0, w1, b1, ga, be, act=L.ACT_RELU) -> torch.Tensor:
+    out = _out_like(x, 512)
+    gc_edges_out(x, w0, b0, w1, b1, ga, be, out, act=act)
+    return out
+
+
+gc_nodes_out = gc_edges_out  # x [M, 1024]; same chain shape after the first layer
+
+
+def gc_nodes(x, w0, b0, w1, b1, ga, be, act=L.ACT_RELU) -> torch.Tensor:
+    out = _out_like(x, 512)
+    gc_nodes_out(x, w0, b0, w1, b1, ga, be, out, act=act)
+    return out
+
+
+def nerf_a_out(x, w1, b1, w2, b2, w3, b3, w4, b4, w5, b5, w6, b6, w7, b7, w8, b8, out) -> None:
+    """NeRF trunk: x [M, 64] -> 256 (x5, ReLU), [h || x] -> 256 (w6 is [320, 256]), 256 x2."""
+    fused_mlp_out(x, [w1, w2, w3, w4, w5, w6, w7, w8], [b1, b2, b3, b4, b5, b6, b7, b8], out,
+                  acts=[L.ACT_RELU] * 8, skip_layer=5)
+
+
+def nerf_a(x, *wb) -> torch.Tensor:
+    out = _out_like(x, 256)
+    nerf_a_out(x, *wb, out)
+    return out
+
+
+def nerf_out(x, weights, biases, out) -> None:
+    """NeRF trunk + decode head 256 -> 4 (9 weights; the last one is [256, 4])."""
+    fused_mlp_out(x, list(weights), list(biases), out, acts=[L.ACT_RELU] * 8 + [L.ACT_NONE],
+                  skip_layer=5)
+
+
 def run_workload_out(w, x, weights, ln, out) -> None:
     """Run a workloads.Workload chain through the generic C entry point."""
     gamma, beta = ln if ln is not None else (None, None)
     fused_mlp_out(x, [p[0] for p in weights], [p[1] for p in weights], out, acts=w.acts,
-                  tail=w.tail, gamma=gamma, beta=beta, ln_eps=w.ln_eps)
+                  tail=w.tail, gamma=gamma, beta=beta, ln_eps=w.ln_eps, skip_layer=w.skip_layer)

@@ -46,6 +46,7 @@ class Workload:
     input_logical: int = 0        # logical input columns (rest zero padding)
     weight_init: str = "kaiming"  # kaiming (nn.Linear default) | normal002 | xavier
     bias_init: str = "default"    # default (nn.Linear) | zero
+    skip_layer: int = 0           # layer reading [previous output || x] (NeRF), 0 = none
     description: str = ""
 
     @property
@@ -84,7 +85,14 @@ class Workload:
         return b
 
     def spec(self) -> L.GpSpec:
-        return L.make_spec(self.widths, self.acts, self.tail, self.gp_dtype, self.ln_eps)
+        return L.make_spec(self.widths, self.acts, self.tail, self.gp_dtype, self.ln_eps,
+                           self.skip_layer)
+
+    @property
+    def bound(self) -> str:
+        """'hbm' or 'tensor': the slower of FLOPs at the bf16 peak and bytes at HBM bandwidth
+        (ridge of the measured peaks, about 253 FLOP/B)."""
+        return "tensor" if self.flop_per_row / self.bytes_per_row > 253 else "hbm"
 
     def with_m(self, m: int) -> "Workload":
         return Workload(**{**self.__dict__, "m": int(m)})
@@ -110,7 +118,33 @@ MGN_LINEARS = _mgn("mgn_linears", 1310720, 384, 0, tail=L.TAIL_NONE,
 TEST_MLP = _mgn("test_mlp", 1310720, 128, 0, tail=L.TAIL_NONE,
                 desc="apps/test_mlp: 128->128->128->128")
 
-WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP)}
+# DLRM bottom MLP (common/mlps.py:23-35 DlrmMlp([13, 512, 256, 128])): 13 dense features padded
+# to 16; Xavier-uniform weights (seed 3); ReLU after every layer.
+_R, _N = L.ACT_RELU, L.ACT_NONE
+DLRM_BOT = Workload(
+    name="dlrm_bot", m=262144, dtype=torch.float16, seed=3, input_kind="dlrm_dense",
+    input_logical=13, weight_init="xavier",
+    layers=(Layer(16, 512, _R, 13, 512), Layer(512, 256, _R, 512, 256), Layer(256, 128, _R, 256, 128)),
+    description="DLRM bottom MLP: 13(16)->512->256->128, ReLU, fp16")
+
+# GraphCast-style edge MLP (apps/gc_edges/torch/model.py with SiLU): bf16, seed 4.
+GC_EDGE = Workload(
+    name="gc_edge", m=1638400, dtype=torch.bfloat16, seed=4, tail=L.TAIL_LAYERNORM, ln_eps=1e-5,
+    input_logical=1536,
+    layers=(Layer(1536, 512, L.ACT_SILU, 1536, 512), Layer(512, 512, _N, 512, 512)),
+    description="GraphCast edge MLP: 1536->512 SiLU->512, LayerNorm(512), bf16")
+
+# NeRF MLP (apps/nerf_full/torch/model.py, use_viewdirs=False, out_ch=4): positional encoding of
+# xyz ~ U(-1, 1), 63 features padded to 64; skip concat of x into layer 5; 256 -> 4 head.
+NERF = Workload(
+    name="nerf", m=4194304, dtype=torch.float16, seed=4, input_kind="nerf_posenc", input_logical=63,
+    skip_layer=5,
+    layers=(Layer(64, 256, _R, 63, 256),) + tuple(Layer(256, 256, _R, 256, 256) for _ in range(4)) +
+           (Layer(320, 256, _R, 319, 256), Layer(256, 256, _R, 256, 256), Layer(256, 256, _R, 256, 256),
+            Layer(256, 4, _N, 256, 4)),
+    description="NeRF MLP: 63(64)->256 x5, [h||x] 319(320)->256, 256 x2, ReLU, 256->4 head, fp16")
+
+WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF)}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -166,6 +200,17 @@ def make_input_chunk(w: Workload, chunk: int, rows: int | None = None) -> torch.
     g = _gen(w.seed, 1, chunk)
     if w.input_kind == "normal":
         x = torch.randn(rows, w.k0, generator=g)
+    elif w.input_kind == "dlrm_dense":
+        # log1p of Exp(1) draws (DLRM's dense-feature transform)
+        x = torch.log1p(torch.empty(rows, w.k0).exponential_(1.0, generator=g))
+    elif w.input_kind == "nerf_posenc":
+        # gamma(p) = [p, sin(2^k pi p), cos(2^k pi p)]_{k=0..9} for xyz ~ U(-1, 1)
+        p = torch.rand(rows, 3, generator=g) * 2 - 1
+        feats = [p]
+        for k in range(10):
+            feats += [torch.sin((2.0 ** k) * math.pi * p), torch.cos((2.0 ** k) * math.pi * p)]
+        x = torch.zeros(rows, w.k0)
+        x[:, :63] = torch.cat(feats, dim=1)
     else:
         raise ValueError(w.input_kind)
     if w.input_logical < w.k0:

@@ -70,7 +70,9 @@ typedef enum gp_tail {
 } gp_tail;
 
 /* A layer chain. widths[0] is the stored (padded) input width K0; layer l maps widths[l] to
- * widths[l+1] and applies act[l] (the last layer's act is ignored when tail is a LayerNorm). */
+ * widths[l+1] and applies act[l] (the last layer's act is ignored when tail is a LayerNorm).
+ * skip_layer = s > 0 makes layer s read the concatenation [output of layer s-1 || x] (the NeRF
+ * skip connection); its weight is then [widths[s] + widths[0], widths[s+1]]. 0 = no skip. */
 typedef struct gp_mlp_spec {
   int n_layers;
   int widths[GP_MAX_LAYERS + 1];
@@ -78,6 +80,7 @@ typedef struct gp_mlp_spec {
   int tail;         /* gp_tail */
   int dtype;        /* gp_dtype */
   float ln_eps;
+  int skip_layer;
 } gp_mlp_spec;
 
 /* ---------------------------------------------------------------------------------------------
@@ -108,6 +111,40 @@ GP_API int gp_mgn_linears_out(int64_t m, int k0, const void* x,
 GP_API int gp_testmlp_out(int64_t m, const void* x,
                    const void* w1, const void* b1, const void* w2, const void* b2,
                    const void* w3, const void* b3, void* out, void* stream);
+
+/* DLRM bottom MLP, fp16: x [m, 16] (13 dense features, zero padded), 16 -> 512 -> 256 -> 128,
+ * ReLU after every layer. w1 is [16, 512] (rows 13..15 multiply the zero padding).
+ * Replaces dlrm_botmlp_out (apps/dlrm_botmlp/pipelined/dlrm_botmlp_pl_ext.cu:24-66). */
+GP_API int gp_dlrm_botmlp_out(int64_t m, const void* x,
+                       const void* w1, const void* b1, const void* w2, const void* b2,
+                       const void* w3, const void* b3, void* out, void* stream);
+
+/* GraphCast edge MLP: x [m, 1536] -> 512 (act) -> 512, LayerNorm(512, eps 1e-5).
+ * Replaces gc_edges_out (apps/gc_edges/pipelined/gc_edges_pl_ext.cu:24-57), which is fp16 with
+ * ReLU; dtype (GP_F16 / GP_BF16) and act (GP_ACT_RELU / GP_ACT_SILU) select the variant. */
+GP_API int gp_gc_edges_out(int64_t m, int dtype, int act, const void* x,
+                    const void* w0, const void* b0, const void* w1, const void* b1,
+                    const void* gamma, const void* beta, void* out, void* stream);
+
+/* GraphCast node MLP: as gp_gc_edges_out with x [m, 1024].
+ * Replaces gc_nodes_out (apps/gc_nodes/pipelined/gc_nodes_pl_ext.cu:24-57). */
+GP_API int gp_gc_nodes_out(int64_t m, int dtype, int act, const void* x,
+                    const void* w0, const void* b0, const void* w1, const void* b1,
+                    const void* gamma, const void* beta, void* out, void* stream);
+
+/* NeRF trunk, fp16: x [m, 64] (63 positional-encoding features, zero padded); layers 1-5
+ * 64 -> 256 -> ... -> 256 (ReLU), layer 6 reads [h || x] (w6 is [320, 256]), layers 7-8
+ * 256 -> 256 (ReLU); out [m, 256].
+ * Replaces nerf_a_out (apps/nerf_a/pipelined/nerf_a_pl_ext.cu:24-77); w[8], b[8] = layers 1..8. */
+GP_API int gp_nerf_a_out(int64_t m, const void* x, const void* const* w, const void* const* b,
+                  void* out, void* stream);
+
+/* NeRF MLP with its output head (apps/nerf_full/torch/model.py:5-66, use_viewdirs = False):
+ * the trunk of gp_nerf_a_out followed by decode 256 -> 4 (no activation); out [m, 4].
+ * w[9], b[9] = layers 1..8 and the head (w[8] is [256, 4]). No reference launch function (the
+ * reference's pipelined NeRF kernels stop at the trunk or add the view-direction heads). */
+GP_API int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* const* b,
+                void* out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Diagnostics and control (no reference counterpart: the reference has no error reporting).

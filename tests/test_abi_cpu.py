@@ -47,7 +47,13 @@ def test_rejects_bad_shapes():
     s.n_layers = 0
     assert _call(s) == L.GP_ERR_SHAPE
     s = mgn()
-    s.widths[2] = 100  # not a multiple of 8
+    s.widths[2] = 0
+    assert _call(s) == L.GP_ERR_SHAPE
+    s = mgn()
+    s.widths[0] = 100  # input rows must be a multiple of 16 bytes
+    assert _call(s) == L.GP_ERR_SHAPE
+    s = mgn()
+    s.skip_layer = 3  # past the last layer
     assert _call(s) == L.GP_ERR_SHAPE
     assert _call(mgn(), m=-1) == L.GP_ERR_ARG
     assert _call(mgn(), m=2**31) == L.GP_ERR_SHAPE
