@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "gp_gc_nodes_out",
     "gp_nerf_a_out",
     "gp_nerf_out",
+    "gp_gc_edges_bf16_noalloc_out",
     "gp_last_error",
     "gp_device_status",
     "gp_set_timeout_ns",
@@ -105,6 +106,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     for name in ("gp_nerf_a_out", "gp_nerf_out"):
         getattr(lib, name).argtypes = [_I64, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P]
         getattr(lib, name).restype = _INT
+    lib.gp_gc_edges_bf16_noalloc_out.argtypes = [_I64, _INT] + [_P] * 9
+    lib.gp_gc_edges_bf16_noalloc_out.restype = _INT
     lib.gp_last_error.argtypes = []
     lib.gp_last_error.restype = ctypes.c_char_p
     lib.gp_device_status.argtypes = [_INT, _INT, ctypes.POINTER(_INT)]

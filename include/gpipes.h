@@ -146,6 +146,18 @@ GP_API int gp_nerf_a_out(int64_t m, const void* x, const void* const* w, const v
 GP_API int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* const* b,
                 void* out, void* stream);
 
+/* GraphCast edge MLP in bf16 (as gp_gc_edges_out with dtype GP_BF16, act GP_ACT_RELU or
+ * GP_ACT_SILU) for callers that cannot allocate GPU memory during a call: frameworks that own
+ * every device allocation, or serving loops that must never enter an allocator. It allocates
+ * nothing; the fp16 copy of the second layer's weights goes to a fixed 1 MiB buffer compiled
+ * into the library (held by every GPU that loads it, until exit). The first call on a device
+ * looks that buffer up (cudaGetSymbolAddress) and should come before any stream capture. Calls
+ * share the buffer: calls that overlap on the GPU race and must be ordered. Device-side timeouts
+ * are not reported through gp_device_status. No counterpart in the reference. */
+GP_API int gp_gc_edges_bf16_noalloc_out(int64_t m, int act, const void* x,
+                                 const void* w0, const void* b0, const void* w1, const void* b1,
+                                 const void* gamma, const void* beta, void* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Diagnostics and control (no reference counterpart: the reference has no error reporting).
  * ------------------------------------------------------------------------------------------- */
