@@ -46,9 +46,10 @@ from gpu_pipes_b200 import _lib as L  # noqa: E402
 from gpu_pipes_b200 import workloads as W  # noqa: E402
 
 L2_BYTES = 126 * 2**20
-# DRAM bytes (read + write) per launch of the fused kernel from one ncu capture, per row,
-# keyed by workload (profiles/mlp_resident_mgn_node.md). None until measured.
-NCU_TRAFFIC_PER_ROW = {"mgn_node": None, "mgn_edge": None}
+# DRAM bytes (read + write) per row of one launch of the fused kernel, from ncu captures
+# (profiles/mlp_resident_mgn_node.md, profiles/mlp_stream_nerf_gc.md); traffic grows with rows.
+NCU_TRAFFIC_PER_ROW = {"mgn_node": 752.7e6 / 1048576, "nerf": 141.4e6 / 1048576,
+                       "gc_edge": 509.8e6 / 131072}
 
 
 def parse():

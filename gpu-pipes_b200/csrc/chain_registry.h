@@ -43,6 +43,15 @@ int set_error(int code, const char* fmt, ...);
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
                  uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
+// Per-device workspace for kernels that need global scratch (fp16 weight copies, intermediates
+// of multi-kernel chains). workspace_acquire returns a buffer of at least `bytes` whose earlier
+// users (on any stream) are ordered before `stream`; the buffer is allocated on first use and
+// grown (never shrunk) when a larger one is needed. The caller must call workspace_release on
+// the same stream after enqueuing its last user; between the two calls other host threads that
+// want the workspace of this device wait.
+int workspace_acquire(size_t bytes, cudaStream_t stream, void** ptr);
+void workspace_release(cudaStream_t stream);
+
 // Sets the dynamic shared memory attribute of `kern` once per device.
 int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask);
 

@@ -127,6 +127,62 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, u
   return GP_OK;
 }
 
+// ------------------------------------------------------------------------------------------------
+// per-device workspace
+// ------------------------------------------------------------------------------------------------
+struct Workspace {
+  std::mutex mu;
+  void* ptr = nullptr;
+  size_t size = 0;
+  cudaEvent_t last_use = nullptr;  // recorded after the latest user's launches
+};
+static Workspace g_ws[64];
+
+int workspace_acquire(size_t bytes, cudaStream_t stream, void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(GP_ERR_ARG, "device %d out of range", dev);
+  Workspace& w = g_ws[dev];
+  w.mu.lock();
+  if (w.last_use == nullptr) {
+    e = cudaEventCreateWithFlags(&w.last_use, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      w.mu.unlock();
+      return set_error(GP_ERR_CUDA, "workspace event: %s", cudaGetErrorString(e));
+    }
+  }
+  if (w.size < bytes) {
+    // growing: earlier users must be done with the old buffer
+    e = cudaEventSynchronize(w.last_use);
+    if (e == cudaSuccess && w.ptr != nullptr) e = cudaFree(w.ptr);
+    w.ptr = nullptr;
+    w.size = 0;
+    const size_t grown = ((bytes + (size_t(1) << 20) - 1) >> 20) << 20;
+    if (e == cudaSuccess) e = cudaMalloc(&w.ptr, grown);
+    if (e != cudaSuccess) {
+      w.mu.unlock();
+      return set_error(GP_ERR_CUDA, "workspace of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    w.size = grown;
+  }
+  e = cudaStreamWaitEvent(stream, w.last_use, 0);
+  if (e != cudaSuccess) {
+    w.mu.unlock();
+    return set_error(GP_ERR_CUDA, "workspace ordering: %s", cudaGetErrorString(e));
+  }
+  *ptr = w.ptr;
+  return GP_OK;
+}
+
+void workspace_release(cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  Workspace& w = g_ws[dev];
+  cudaEventRecord(w.last_use, stream);
+  w.mu.unlock();
+}
+
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 static int validate(const gp_mlp_spec* spec, int64_t m, const void* x, const void* const* w,

@@ -4,9 +4,9 @@
 // framework that owns every device allocation (a custom allocator or a fixed memory budget with
 // cudaMalloc forbidden), real-time or serving loops that must not enter the allocator, and
 // environments where the stream-ordered pool may not be used. The regular entry point
-// (gp_gc_edges_out with GP_BF16) obtains a short-lived buffer for the fp16 copies of the second
-// layer's weights with cudaMallocAsync on the caller's stream; this variant uses a fixed buffer
-// compiled into the library instead:
+// (gp_gc_edges_out with GP_BF16) keeps the fp16 copies of the second layer's weights in a
+// per-device workspace that it allocates with cudaMalloc on first use (and grows when needed);
+// this variant uses a fixed buffer compiled into the library instead:
 //
 //   * g_noalloc_scratch is a file-scope __device__ array of kNoAllocScratchBytes (1 MiB). Every
 //     GPU that loads libgpipes.so holds it until the process exits.

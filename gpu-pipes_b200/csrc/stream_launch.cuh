@@ -29,8 +29,7 @@ int launch_stream(const LaunchCtx& c) {
   rc = make_tmap_2d(&tm.x, c.x, dt, c.m, C::K(0), kPanel, kBM, 128);
   if (rc == GP_OK && C::TAIL != kTailHead)
     rc = make_tmap_2d(&tm.out, c.out, dt, c.m, C::N(C::NL - 1), 32, 32, 64);
-  // fp16 copies of the weights of layers >= 1 (HIDDEN_F16), in stream-ordered scratch that is
-  // released right after the launch on the same stream
+  // fp16 copies of the weights of layers >= 1 (HIDDEN_F16), in the per-device workspace
   void* scratch = nullptr;
   size_t offs[kMaxLayers] = {0};
   if constexpr (C::HIDDEN_F16) {
@@ -39,8 +38,8 @@ int launch_stream(const LaunchCtx& c) {
       offs[l] = total;
       total += ((static_cast<size_t>(C::K(l)) * C::N(l) * 2 + 255) / 256) * 256;
     }
-    cudaError_t e = cudaMallocAsync(&scratch, total, c.stream);
-    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "weight scratch: %s", cudaGetErrorString(e));
+    rc = workspace_acquire(total, c.stream, &scratch);
+    if (rc != GP_OK) return rc;
     for (int l = 1; l < C::NL; ++l) {
       const int64_t n = static_cast<int64_t>(C::K(l)) * C::N(l);
       bf16_to_f16_kernel<<<static_cast<int>((n + 1023) / 1024), 256, 0, c.stream>>>(
@@ -54,7 +53,7 @@ int launch_stream(const LaunchCtx& c) {
     rc = make_tmap_2d(&tm.w[l], wl, conv ? GP_F16 : dt, C::K(l), C::N(l), 64, L::kBK, 128);
   }
   if (rc != GP_OK) {
-    if (scratch != nullptr) cudaFreeAsync(scratch, c.stream);
+    if (scratch != nullptr) workspace_release(c.stream);
     return rc;
   }
   ChainArgs args = c.args;
@@ -64,10 +63,7 @@ int launch_stream(const LaunchCtx& c) {
   }
   const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
   mlp_stream_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
-  if (scratch != nullptr) {
-    cudaError_t e = cudaFreeAsync(scratch, c.stream);
-    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "weight scratch free: %s", cudaGetErrorString(e));
-  }
+  if (scratch != nullptr) workspace_release(c.stream);
   return GP_OK;
 }
 
