@@ -29,6 +29,8 @@ GP_DECLARE(launch_gc_relu_bf16_k1536)
 GP_DECLARE(launch_gc_relu_f16_k1024)
 GP_DECLARE(launch_nerf_f16)
 GP_DECLARE(launch_nerf_trunk_f16)
+GP_DECLARE(launch_bert_ffn_bf16)
+GP_DECLARE(launch_dlrm_top_f16)
 #undef GP_DECLARE2
 #undef GP_DECLARE
 
@@ -69,6 +71,11 @@ static const ChainEntry kChains[] = {
      GP_TAIL_NONE, launch_nerf_f16, 0, 5},
     {"nerf_trunk_f16", GP_F16, 8, {64, 256, 256, 256, 256, 256, 256, 256, 256}, {R, R, R, R, R, R, R, R},
      GP_TAIL_NONE, launch_nerf_trunk_f16, 0, 5},
+    // chains with activations too wide for one SM: per-layer GEMMs through L2-sized chunks
+    {"bert_ffn_bf16", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
+     launch_bert_ffn_bf16, 0},
+    {"dlrm_top_f16", GP_F16, 5, {480, 1024, 1024, 512, 256, 1}, {R, R, R, R, GP_ACT_SIGMOID},
+     GP_TAIL_NONE, launch_dlrm_top_f16, 0},
 };
 #undef MGN
 #undef R

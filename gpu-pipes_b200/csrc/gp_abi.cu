@@ -373,6 +373,38 @@ int gp_gc_nodes_out(int64_t m, int dtype, int act, const void* x, const void* w0
   return gc_mlp(m, 1024, dtype, act, x, w0, b0, w1, b1, gamma, beta, out, stream);
 }
 
+int gp_bert_ffn_out(int64_t m, const void* x, const void* w1, const void* b1, const void* w2,
+                    const void* b2, const void* gamma, const void* beta, float ln_eps, void* out,
+                    void* stream) {
+  gp_mlp_spec s{};
+  s.n_layers = 2;
+  s.widths[0] = 1024;
+  s.widths[1] = 4096;
+  s.widths[2] = 1024;
+  s.act[0] = GP_ACT_GELU_TANH;
+  s.act[1] = GP_ACT_NONE;
+  s.tail = GP_TAIL_RESIDUAL_LN;
+  s.dtype = GP_BF16;
+  s.ln_eps = ln_eps;
+  const void* w[2] = {w1, w2};
+  const void* b[2] = {b1, b2};
+  return fused_mlp(&s, m, x, w, b, gamma, beta, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_dlrm_topmlp_out(int64_t m, const void* x, const void* const* w, const void* const* b,
+                       void* out, void* stream) {
+  if (w == nullptr) return set_error(GP_ERR_ARG, "w is NULL");
+  gp_mlp_spec s{};
+  s.n_layers = 5;
+  const int wd[6] = {480, 1024, 1024, 512, 256, 1};
+  for (int i = 0; i < 6; ++i) s.widths[i] = wd[i];
+  for (int i = 0; i < 4; ++i) s.act[i] = GP_ACT_RELU;
+  s.act[4] = GP_ACT_SIGMOID;
+  s.tail = GP_TAIL_NONE;
+  s.dtype = GP_F16;
+  return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
 static gp_mlp_spec nerf_spec(bool head) {
   gp_mlp_spec s{};
   s.n_layers = head ? 9 : 8;

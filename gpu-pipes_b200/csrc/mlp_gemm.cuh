@@ -1,0 +1,287 @@
+// One wide layer as a tcgen05 GEMM with a fused epilogue, for chains whose activations are too
+// wide to stay in one SM (BERT-large FFN 1024 -> 4096 -> 1024, DLRM top 480 -> 1024 -> 1024 -> 512):
+//
+//   out[M, N] = epilogue(A[M, K] . W[K, N])   epilogue = + bias, activation, + residual,
+//                                             16-bit (TMA store) or fp32 (direct) output
+//
+// The reference runs these layers as pipeline stages connected by L2-resident queues
+// (apps/bert_ffn/pipelined/bert_ffn_pl.cuh:132-162, apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl.cuh:
+// 185-224). Here each layer is one persistent launch over 128 x 256 output tiles, and the host
+// runs a chain over row chunks sized so that every intermediate stays within L2: the hand-off
+// between layers goes through L2, as in the reference, rather than HBM.
+//
+//   warp 0     TMA producer: per 64-wide K step one A panel (128 x 64, K-major SW128) and one
+//              B stage (64 x 256, N-major SW128) into a 4-stage mbarrier ring
+//   warp 1     TMEM allocator + MMA issuer: 128 x 256 x 16 MMAs into one of two accumulators
+//   warps 2-5  epilogue of the previous tile (thread = row) while the next tile accumulates
+#pragma once
+
+#include "chain_common.cuh"
+#include "gp_ptx.cuh"
+#include "mlp_resident.cuh"
+
+namespace gp {
+
+struct GemmArgs {
+  int m, n, k;          // out [m, n] = A [m, k] . W [k, n]
+  int n_tiles;          // n / 256
+  int num_tiles;        // ceil(m / 128) * n_tiles
+  int act;              // Act applied after bias (+ residual)
+  int out_f32;          // 1: fp32 output written directly; 0: 16-bit output through TMA
+  int out_f16;          // 16-bit output type: 1 = fp16, 0 = bf16
+  const void* bias;     // [n] 16-bit (type `bias_bf16`), or null
+  int bias_bf16;
+  const void* resid;    // [m, n] 16-bit residual added before the activation, or null
+  int resid_bf16;
+  void* out;            // [m, n]
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+struct GemmLayout {
+  static constexpr int kBN = 256;
+  static constexpr int kStages = 4;
+  static constexpr int kABytes = kPanelBytes;           // 128 x 64 x 2
+  static constexpr int kBBytes = kPanel * kBN * 2;      // 64 x 256 x 2
+  static constexpr int kStageBytes = kABytes + kBBytes; // 48 KB
+  static constexpr int kStgBytes = 4 * 32 * 64;         // per epilogue warp: 32 x 32 x 2 B
+  static constexpr int kOffStg = kStages * kStageBytes;
+  static constexpr int kOffBar = kOffStg + kStgBytes;
+  static constexpr int kSmemBytes = kOffBar + 256;
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+};
+
+__device__ __forceinline__ float load16(const void* p, int64_t i, int is_bf16) {
+  const uint16_t bits = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
+  if (is_bf16) return __bfloat162float(__ushort_as_bfloat16(bits));
+  return __half2float(__ushort_as_half(bits));
+}
+
+__global__ void __launch_bounds__(192, 1)
+    mlp_gemm_kernel(const __grid_constant__ TensorMaps tm, const GemmArgs args, int ab_bf16) {
+  using L = GemmLayout;
+  constexpr int kS = L::kStages;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* full = bars;            // [4]
+  uint64_t* empty = bars + 4;       // [4]
+  uint64_t* acc_full = bars + 8;    // [2]
+  uint64_t* acc_empty = bars + 10;  // [2]
+  uint64_t* mma_done = bars + 12;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kS; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4);
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
+  const int kpanels = (args.k + kPanel - 1) / kPanel;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+#pragma unroll 1
+      for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x) {
+        const int mt = t / args.n_tiles, nt = t % args.n_tiles;
+        bool ok = true;
+#pragma unroll 1
+        for (int kp = 0; kp < kpanels; ++kp) {
+          if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
+          const uint32_t st = smem_u32(smem + s * L::kStageBytes);
+          mbar_arrive_expect_tx(smem_u32(&full[s]), L::kStageBytes);
+          tma_load_2d_hint(st, &tm.x, smem_u32(&full[s]), kp * kPanel, mt * kBM, keep);
+          for (int nb = 0; nb < L::kBN / 64; ++nb)
+            tma_load_2d_hint(st + L::kABytes + nb * (kPanel * 128), &tm.w[0], smem_u32(&full[s]),
+                             nt * L::kBN + nb * 64, kp * kPanel, keep);
+          if (++s == kS) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(kBM, L::kBN, ab_bf16, 0, 1);
+      int s = 0, it = 0;
+      uint32_t ph = 0, eph[2] = {0, 0};
+      bool ok = true;
+#pragma unroll 1
+      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x, ++it) {
+        const int b = it & 1;
+        if (it >= 2) {
+          if (!mbar_wait(smem_u32(&acc_empty[b]), eph[b], wctx, kDevTimeoutMma)) break;
+          eph[b] ^= 1;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + b * L::kBN;
+#pragma unroll 1
+        for (int kp = 0; kp < kpanels; ++kp) {
+          if (!mbar_wait(smem_u32(&full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * L::kStageBytes);
+          const uint64_t adesc = make_sdesc_sw128(st, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t bdesc = make_sdesc_sw128(st + L::kABytes + k * 2048, kPanel * 128, 1024);
+            mma_ss(d, adesc + static_cast<uint64_t>(k * 2), bdesc, idesc, (kp | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&empty[s]));
+          if (++s == kS) { s = 0; ph ^= 1; }
+        }
+        if (ok) mma_commit(smem_u32(&acc_full[b]));
+      }
+      mma_commit(smem_u32(mma_done));
+      volatile int no_abort = 0;
+      WaitCtx drain{args.status, &no_abort, args.timeout_ns};
+      mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    uint8_t* stg = smem + L::kOffStg + (warp - 2) * (32 * 64);
+    uint32_t aph[2] = {0, 0};
+    int it = 0;
+#pragma unroll 1
+    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++it) {
+      const int b = it & 1;
+      const int mt = t / args.n_tiles, nt = t % args.n_tiles;
+      if (!mbar_wait(smem_u32(&acc_full[b]), aph[b], wctx, kDevTimeoutEpilogue)) break;
+      aph[b] ^= 1;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(mt) * kBM + r;
+      const int row0 = mt * kBM + q * 32;
+      const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * L::kBN;
+#pragma unroll 1
+      for (int c = 0; c < L::kBN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_lane + c * 32, v);
+        tmem_wait_ld();
+        if (c + 1 == L::kBN / 32) {  // accumulator fully read: the MMA may reuse it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+        }
+        const int col0 = nt * L::kBN + c * 32;
+        float y[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float val = __uint_as_float(v[i]);
+          if (args.bias != nullptr) val += load16(args.bias, col0 + i, args.bias_bf16);
+          y[i] = val;
+        }
+        if (args.resid != nullptr && row < args.m) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            y[i] += load16(args.resid, row * args.n + col0 + i, args.resid_bf16);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) y[i] = apply_act(args.act, y[i]);
+        if (args.out_f32) {
+          if (row < args.m) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.out) + row * args.n + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+          }
+        } else {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = args.out_f16 ? Elem<__half>::pack(y[2 * i], y[2 * i + 1])
+                                 : Elem<__nv_bfloat16>::pack(y[2 * i], y[2 * i + 1]);
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+          stage_chunk32(stg, lane, pk);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(stg), col0, row0);
+            bulk_commit_group();
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// Row LayerNorm over fp32 rows of width N (multiple of 128): one warp per row, two passes in
+// registers (mean, then squared deviations), out = (y - mean) / sqrt(var + eps) * gamma + beta.
+template <int N>
+__global__ void __launch_bounds__(256)
+    row_layernorm_kernel(const float* __restrict__ y, const void* gamma, const void* beta, int g_bf16,
+                         float eps, int64_t m, void* out, int out_bf16) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= m) return;
+  constexpr int kPer = N / 128;  // float4 per lane
+  float4 v[kPer];
+  const float4* src = reinterpret_cast<const float4*>(y + row * N);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    v[i] = src[i * 32 + lane];
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.0f / N);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q += a * a + b * b + c * c + d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q * (1.0f / N) + eps);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int col = (i * 32 + lane) * 4;
+    float o4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    uint32_t pk[2];
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      float a = (o4[e] - mean) * rstd, b = (o4[e + 1] - mean) * rstd;
+      if (gamma != nullptr) { a *= load16(gamma, col + e, g_bf16); b *= load16(gamma, col + e + 1, g_bf16); }
+      if (beta != nullptr) { a += load16(beta, col + e, g_bf16); b += load16(beta, col + e + 1, g_bf16); }
+      pk[e / 2] = out_bf16 ? Elem<__nv_bfloat16>::pack(a, b) : Elem<__half>::pack(a, b);
+    }
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + row * N + col) = make_uint2(pk[0], pk[1]);
+  }
+}
+
+}  // namespace gp

@@ -9,7 +9,7 @@
 namespace gp {
 
 // bf16 -> fp16 copy of a weight matrix (exact for values within the fp16 range).
-__global__ void bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ src, __half* __restrict__ dst,
+static __global__ void bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ src, __half* __restrict__ dst,
                                    int64_t n) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)

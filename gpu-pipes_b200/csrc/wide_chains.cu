@@ -1,0 +1,163 @@
+// Host orchestration of the chains whose hidden activations are too wide for one SM:
+//   BERT-large FFN  ln(x + W2 gelu(W1 x + b1) + b2), 1024 -> 4096 -> 1024, bf16
+//                   (apps/bert_ffn/torch/model.py:4-15 at BERT-large widths, GELU(tanh))
+//   DLRM top MLP    480 -> 1024 -> 1024 -> 512 -> 256 -> 1, ReLU, sigmoid at the end, fp16
+//                   (common/mlps.py:23-35 DlrmMlp([479, 1024, 1024, 512, 256, 1], sigmoid_i=4))
+// Each chain runs over row chunks sized so every intermediate (in the per-device workspace) stays
+// within L2; each wide layer is one mlp_gemm_kernel launch; the tail (LayerNorm, or the last two
+// DLRM layers with the sigmoid head) is a row kernel / the weight-streaming chain kernel.
+#include <cstring>
+
+#include "chain_registry.h"
+#include "mlp_gemm.cuh"
+#include "stream_launch.cuh"
+
+namespace gp {
+namespace {
+
+constexpr int kGemmThreads = 192;
+
+int gemm_launch(cudaStream_t s, int sm_count, const void* a, int a_bf16, int64_t m, int k,
+                const void* w, int n, const void* bias, int bias_bf16, const void* resid,
+                int resid_bf16, int act, void* out, int out_kind /*0 bf16, 1 f16, 2 f32*/,
+                int* status, unsigned long long timeout_ns) {
+  static unsigned long long done_mask = 0;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(&mlp_gemm_kernel), GemmLayout::kSmemBytes,
+                            &done_mask);
+  if (rc != GP_OK) return rc;
+  if (n % GemmLayout::kBN != 0) return set_error(GP_ERR_UNSUPPORTED, "gemm layer width %d", n);
+  TensorMaps tm;
+  std::memset(&tm, 0, sizeof(tm));
+  const int adt = a_bf16 ? GP_BF16 : GP_F16;
+  rc = make_tmap_2d(&tm.x, a, adt, m, k, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.w[0], w, adt, k, n, 64, kPanel, 128);
+  if (rc == GP_OK && out_kind != 2)
+    rc = make_tmap_2d(&tm.out, out, out_kind == 0 ? GP_BF16 : GP_F16, m, n, 32, 32, 64);
+  if (rc != GP_OK) return rc;
+  GemmArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.m = static_cast<int>(m);
+  g.n = n;
+  g.k = k;
+  g.n_tiles = n / GemmLayout::kBN;
+  g.num_tiles = static_cast<int>((m + kBM - 1) / kBM) * g.n_tiles;
+  g.act = act;
+  g.out_f32 = out_kind == 2;
+  g.out_f16 = out_kind == 1;
+  g.bias = bias;
+  g.bias_bf16 = bias_bf16;
+  g.resid = resid;
+  g.resid_bf16 = resid_bf16;
+  g.out = out;
+  g.status = status;
+  g.timeout_ns = timeout_ns;
+  const int grid = g.num_tiles < sm_count ? g.num_tiles : sm_count;
+  mlp_gemm_kernel<<<grid, kGemmThreads, GemmLayout::kSmemBytes, s>>>(tm, g, a_bf16);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+}
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+// The last two DLRM top layers on the weight-streaming kernel: 512 -> 256 (ReLU) -> 1 (sigmoid).
+struct ChainDlrmTail {
+  using T = __half;
+  static constexpr int NL = 1;
+  __host__ __device__ static constexpr int K(int) { return 512; }
+  __host__ __device__ static constexpr int N(int) { return 256; }
+  __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
+  static constexpr int SKIP = 0, TAIL = kTailHead, HEAD_N = 1, HEAD_ACT = kActSigmoid;
+  static constexpr bool HIDDEN_F16 = false;
+};
+
+}  // namespace
+
+// BERT-large FFN (bf16): hidden activations kept in fp16 (as the other bf16 chains), the second
+// GEMM on an fp16 copy of W2, pre-LayerNorm rows in fp32.
+int launch_bert_ffn_bf16(const LaunchCtx& c) {
+  constexpr int H = 1024, F = 4096;
+  constexpr int64_t kChunk = 4096;  // h chunk 4096 x 4096 x 2 B = 32 MB
+  const int64_t chunk = c.m < kChunk ? c.m : kChunk;
+  const size_t w2_bytes = align256(size_t(F) * H * 2);
+  const size_t h_bytes = align256(size_t(chunk) * F * 2);
+  const size_t y_bytes = align256(size_t(chunk) * H * 4);
+  void* ws = nullptr;
+  int rc = workspace_acquire(w2_bytes + h_bytes + y_bytes, c.stream, &ws);
+  if (rc != GP_OK) return rc;
+  char* base = static_cast<char*>(ws);
+  void* w2h = base;
+  void* h = base + w2_bytes;
+  float* y = reinterpret_cast<float*>(base + w2_bytes + h_bytes);
+  const int64_t nw = int64_t(F) * H;
+  bf16_to_f16_kernel<<<static_cast<int>((nw + 1023) / 1024), 256, 0, c.stream>>>(
+      static_cast<const __nv_bfloat16*>(c.w[1]), static_cast<__half*>(w2h), nw);
+  const int* st = c.args.status;
+  for (int64_t r0 = 0; rc == GP_OK && r0 < c.m; r0 += chunk) {
+    const int64_t rows = (c.m - r0) < chunk ? (c.m - r0) : chunk;
+    const void* xr = static_cast<const char*>(c.x) + r0 * H * 2;
+    rc = gemm_launch(c.stream, c.sm_count, xr, 1, rows, H, c.w[0], F, c.args.bias[0], 1, nullptr, 0,
+                     kActGeluTanh, h, 1, const_cast<int*>(st), c.args.timeout_ns);
+    if (rc == GP_OK)
+      rc = gemm_launch(c.stream, c.sm_count, h, 0, rows, F, w2h, H, c.args.bias[1], 1, xr, 1,
+                       kActNone, y, 2, const_cast<int*>(st), c.args.timeout_ns);
+    if (rc == GP_OK) {
+      row_layernorm_kernel<H><<<static_cast<int>((rows + 7) / 8), 256, 0, c.stream>>>(
+          y, c.args.gamma, c.args.beta, 1, c.args.ln_eps, rows,
+          static_cast<char*>(c.out) + r0 * H * 2, 1);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "layernorm launch: %s", cudaGetErrorString(e));
+    }
+  }
+  workspace_release(c.stream);
+  return rc;
+}
+
+// DLRM top MLP (fp16): three wide layers on mlp_gemm_kernel, then 512 -> 256 -> 1 on the
+// streaming chain kernel.
+int launch_dlrm_top_f16(const LaunchCtx& c) {
+  constexpr int64_t kChunk = 16384;  // h1 + h2 + h3 = 80 MB
+  const int64_t chunk = c.m < kChunk ? c.m : kChunk;
+  const size_t h1_bytes = align256(size_t(chunk) * 1024 * 2);
+  const size_t h3_bytes = align256(size_t(chunk) * 512 * 2);
+  void* ws = nullptr;
+  int rc = workspace_acquire(2 * h1_bytes + h3_bytes, c.stream, &ws);
+  if (rc != GP_OK) return rc;
+  char* base = static_cast<char*>(ws);
+  void* h1 = base;
+  void* h2 = base + h1_bytes;
+  void* h3 = base + 2 * h1_bytes;
+  int* st = c.args.status;
+  const int k0 = c.spec->widths[0];
+  for (int64_t r0 = 0; rc == GP_OK && r0 < c.m; r0 += chunk) {
+    const int64_t rows = (c.m - r0) < chunk ? (c.m - r0) : chunk;
+    const void* xr = static_cast<const char*>(c.x) + r0 * k0 * 2;
+    rc = gemm_launch(c.stream, c.sm_count, xr, 0, rows, k0, c.w[0], 1024, c.args.bias[0], 0, nullptr,
+                     0, kActRelu, h1, 1, st, c.args.timeout_ns);
+    if (rc == GP_OK)
+      rc = gemm_launch(c.stream, c.sm_count, h1, 0, rows, 1024, c.w[1], 1024, c.args.bias[1], 0,
+                       nullptr, 0, kActRelu, h2, 1, st, c.args.timeout_ns);
+    if (rc == GP_OK)
+      rc = gemm_launch(c.stream, c.sm_count, h2, 0, rows, 1024, c.w[2], 512, c.args.bias[2], 0,
+                       nullptr, 0, kActRelu, h3, 1, st, c.args.timeout_ns);
+    if (rc == GP_OK) {
+      gp_mlp_spec tail_spec = *c.spec;
+      LaunchCtx t = c;
+      t.spec = &tail_spec;
+      t.m = rows;
+      t.x = h3;
+      t.out = static_cast<char*>(c.out) + r0 * 2;
+      t.w[0] = c.w[3];
+      t.w[1] = c.w[4];
+      t.args.bias[0] = c.args.bias[3];
+      t.args.bias[1] = c.args.bias[4];
+      t.args.m = rows;
+      t.args.num_tiles = static_cast<int>((rows + kBM - 1) / kBM);
+      t.args.out = t.out;
+      rc = launch_stream<ChainDlrmTail>(t);
+    }
+  }
+  workspace_release(c.stream);
+  return rc;
+}
+
+}  // namespace gp

@@ -203,6 +203,30 @@ def nerf_out(x, weights, biases, out) -> None:
                   skip_layer=5)
 
 
+def bert_ffn_out(x, w1, b1, w2, b2, ga, be, out, eps=1e-12) -> None:
+    """BERT-large FFN, bf16: out = LN(x + W2 gelu_tanh(W1 x + b1) + b2); x [M, 1024]."""
+    fused_mlp_out(x, [w1, w2], [b1, b2], out, acts=[L.ACT_GELU_TANH, L.ACT_NONE],
+                  tail=L.TAIL_RESIDUAL_LN, gamma=ga, beta=be, ln_eps=eps)
+
+
+def bert_ffn(x, w1, b1, w2, b2, ga, be, eps=1e-12) -> torch.Tensor:
+    out = _out_like(x, x.shape[1])
+    bert_ffn_out(x, w1, b1, w2, b2, ga, be, out, eps=eps)
+    return out
+
+
+def dlrm_topmlp_out(x, w1, b1, w2, b2, w3, b3, w4, b4, w5, b5, out) -> None:
+    """x [M, 480] -> 1024 -> 1024 -> 512 -> 256 (ReLU) -> 1 (sigmoid)."""
+    fused_mlp_out(x, [w1, w2, w3, w4, w5], [b1, b2, b3, b4, b5], out,
+                  acts=[L.ACT_RELU] * 4 + [L.ACT_SIGMOID])
+
+
+def dlrm_topmlp(x, *wb) -> torch.Tensor:
+    out = _out_like(x, 1)
+    dlrm_topmlp_out(x, *wb, out)
+    return out
+
+
 def run_workload_out(w, x, weights, ln, out) -> None:
     """Run a workloads.Workload chain through the generic C entry point."""
     gamma, beta = ln if ln is not None else (None, None)

@@ -78,6 +78,10 @@ class Workload:
         return 2 * (self.k0 + self.n_out)
 
     @property
+    def n_out_logical(self) -> int:
+        return self.layers[-1].n_logical
+
+    @property
     def weight_bytes(self) -> int:
         b = sum(2 * (l.k * l.n + l.n) for l in self.layers)
         if self.tail != L.TAIL_NONE:
@@ -144,7 +148,25 @@ NERF = Workload(
             Layer(256, 4, _N, 256, 4)),
     description="NeRF MLP: 63(64)->256 x5, [h||x] 319(320)->256, 256 x2, ReLU, 256->4 head, fp16")
 
-WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF)}
+# BERT-large FFN (apps/bert_ffn/torch/model.py at H=1024, ff=4096, GELU(tanh), LN eps 1e-12):
+# weights N(0, 0.02^2), zero biases, seed 2, bf16.
+BERT_FFN = Workload(
+    name="bert_ffn", m=16384, dtype=torch.bfloat16, seed=2, tail=L.TAIL_RESIDUAL_LN, ln_eps=1e-12,
+    input_logical=1024, weight_init="normal002", bias_init="zero",
+    layers=(Layer(1024, 4096, L.ACT_GELU_TANH, 1024, 4096), Layer(4096, 1024, _N, 4096, 1024)),
+    description="BERT-large FFN: 1024->4096 GELU->1024, +x, LayerNorm(1024, 1e-12), bf16")
+
+# DLRM top MLP (DlrmMlp([479, 1024, 1024, 512, 256, 1], sigmoid_i=4)): input 479 padded to 480
+# (the 128-wide bottom output concatenated with 351 interaction values); Xavier-uniform, seed 3.
+DLRM_TOP = Workload(
+    name="dlrm_top", m=262144, dtype=torch.float16, seed=3, input_logical=479, weight_init="xavier",
+    layers=(Layer(480, 1024, _R, 479, 1024), Layer(1024, 1024, _R, 1024, 1024),
+            Layer(1024, 512, _R, 1024, 512), Layer(512, 256, _R, 512, 256),
+            Layer(256, 1, L.ACT_SIGMOID, 256, 1)),
+    description="DLRM top MLP: 479(480)->1024->1024->512->256 ReLU ->1 sigmoid, fp16")
+
+WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF,
+                                 BERT_FFN, DLRM_TOP)}
 
 
 # ------------------------------------------------------------------------------------------------

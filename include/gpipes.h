@@ -132,6 +132,21 @@ GP_API int gp_gc_nodes_out(int64_t m, int dtype, int act, const void* x,
                     const void* w0, const void* b0, const void* w1, const void* b1,
                     const void* gamma, const void* beta, void* out, void* stream);
 
+/* BERT-large FFN with residual and LayerNorm, bf16: out = LN(x + W2 gelu_tanh(W1 x + b1) + b2),
+ * x [m, 1024], w1 [1024, 4096], w2 [4096, 1024], LN(1024, ln_eps) with gamma/beta.
+ * Replaces bert_ffn_out (apps/bert_ffn/pipelined/bert_ffn_pl_ext.cu:24-57), whose app is the
+ * 128 -> 512 (ReLU) -> 128 fp16 block; this entry point runs the BERT-large widths. */
+GP_API int gp_bert_ffn_out(int64_t m, const void* x, const void* w1, const void* b1,
+                    const void* w2, const void* b2, const void* gamma, const void* beta,
+                    float ln_eps, void* out, void* stream);
+
+/* DLRM top MLP, fp16: x [m, 480] (479 interaction features, zero padded) -> 1024 -> 1024 -> 512
+ * -> 256 (ReLU) -> 1 (sigmoid); w[5], b[5]; w1 is [480, 1024]; out [m, 1].
+ * Replaces dlrm_topmlp_out (apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl_ext.cu:24-71), which pads
+ * the output to 64 columns and applies ReLU instead of the model's sigmoid on the last layer. */
+GP_API int gp_dlrm_topmlp_out(int64_t m, const void* x, const void* const* w,
+                       const void* const* b, void* out, void* stream);
+
 /* NeRF trunk, fp16: x [m, 64] (63 positional-encoding features, zero padded); layers 1-5
  * 64 -> 256 -> ... -> 256 (ReLU), layer 6 reads [h || x] (w6 is [320, 256]), layers 7-8
  * 256 -> 256 (ReLU); out [m, 256].

@@ -1,0 +1,72 @@
+"""GPU parity of the wide chains (BERT-large FFN with residual + LayerNorm, DLRM top MLP with the
+sigmoid head) against the CPU oracle, through the C ABI. Row counts cross the chunk boundaries the
+host uses (4,096 rows for BERT, 16,384 for DLRM top); full-size runs are checked on row samples."""
+import pytest
+import torch
+
+from gpu_pipes_b200 import cuda_ext
+from gpu_pipes_b200 import workloads as W
+from oracle import mlp_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(w, dev):
+    x = W.make_input(w)
+    layers, ln = W.make_weights(w)
+    out = torch.empty(w.m, w.n_out, dtype=w.dtype, device=dev)
+    cuda_ext.run_workload_out(w, x.to(dev), [(a.to(dev), b.to(dev)) for a, b in layers],
+                              None if ln is None else tuple(t.to(dev) for t in ln), out)
+    torch.cuda.synchronize()
+    return x, layers, ln, out
+
+
+def _check(w, x, layers, ln, out, spans):
+    for r0, n in spans:
+        ref = O.workload_forward(w, x[r0:r0 + n], layers, ln)
+        r = O.compare(out[r0:r0 + n].float().cpu(), ref)
+        assert r["ok"], f"{w.name} rows {r0}+{n}: {r}"
+
+
+@pytest.mark.parametrize("m", [1, 129, 4096 + 77, 9000])
+def test_bert_ffn_ragged(cuda_dev, m):
+    w = W.BERT_FFN.with_m(m)
+    x, layers, ln, out = _run(w, cuda_dev)
+    _check(w, x, layers, ln, out, [(0, m)])
+
+
+def test_bert_ffn_full_size(cuda_dev):
+    w = W.BERT_FFN
+    x, layers, ln, out = _run(w, cuda_dev)
+    _check(w, x, layers, ln, out, [(0, 2048), (8192 - 1024, 2048), (w.m - 2048, 2048)])
+
+
+@pytest.mark.parametrize("m", [1, 255, 16384 + 5, 40000])
+def test_dlrm_top_ragged(cuda_dev, m):
+    w = W.DLRM_TOP.with_m(m)
+    x, layers, ln, out = _run(w, cuda_dev)
+    _check(w, x, layers, ln, out, [(0, m)])
+
+
+def test_dlrm_top_full_size(cuda_dev):
+    w = W.DLRM_TOP
+    x, layers, ln, out = _run(w, cuda_dev)
+    _check(w, x, layers, ln, out, [(0, 8192), (131072 - 4096, 8192), (w.m - 8192, 8192)])
+
+
+def test_named_entry_points(cuda_dev):
+    """cuda_ext.bert_ffn / cuda_ext.dlrm_topmlp (the reference's names) give the same rows."""
+    w = W.BERT_FFN.with_m(300)
+    x = W.make_input(w)
+    layers, ln = W.make_weights(w)
+    d = [t.to(cuda_dev) for p in layers for t in p]
+    out = cuda_ext.bert_ffn(x.to(cuda_dev), *d, *[t.to(cuda_dev) for t in ln], eps=1e-12)
+    torch.cuda.synchronize()
+    assert O.compare(out.float().cpu(), O.workload_forward(w, x, layers, ln))["ok"]
+    w = W.DLRM_TOP.with_m(300)
+    x = W.make_input(w)
+    layers, _ = W.make_weights(w)
+    d = [t.to(cuda_dev) for p in layers for t in p]
+    out = cuda_ext.dlrm_topmlp(x.to(cuda_dev), *d)
+    torch.cuda.synchronize()
+    assert O.compare(out.float().cpu(), O.workload_forward(w, x, layers, None))["ok"]
