@@ -14,6 +14,7 @@ struct ChainDlrmBot {
   __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
   static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 2;
 };
 
 // GraphCast-style edge / node MLP (apps/gc_edges/torch/model.py:4-14): K0 -> 512 act -> 512, LN.
@@ -26,6 +27,7 @@ struct ChainGc {
   __host__ __device__ static constexpr int ACT(int l) { return l == 0 ? ACT0 : kActNone; }
   static constexpr int SKIP = 0, TAIL = kTailLayerNorm, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = std::is_same<TT, __nv_bfloat16>::value;
+  static constexpr int HALVES = 2;
 };
 
 // NeRF trunk without view directions (apps/nerf_full/torch/model.py:5-66, use_viewdirs=False):
@@ -38,6 +40,7 @@ struct ChainNerf {
   __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
   static constexpr int SKIP = 5, TAIL = kTailHead, HEAD_N = 4, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 1;
 };
 
 // The same trunk without the head: layer 8's ReLU output is the result (apps/nerf_a).

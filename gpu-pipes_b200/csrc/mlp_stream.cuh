@@ -33,7 +33,9 @@ namespace gp {
 
 constexpr int kTailHead = 3;  // narrow output layer on CUDA cores (stream kernel only)
 
-// Chain description used as a template argument:
+// Chain description used as a template argument (HALVES: 2 = each layer's output is computed
+// and drained as two column halves so the epilogue of one overlaps the MMAs of the other;
+// 1 = one pass per layer):
 //   using T;  NL (tensor-core layers); K(l), N(l), ACT(l); SKIP (layer whose A operand is
 //   [act || x], 0 = none); TAIL (kTailNone / kTailLayerNorm / kTailHead); HEAD_N, HEAD_ACT;
 //   HIDDEN_F16: with bf16 data, keep hidden activations in fp16 (11-bit mantissa instead of 8)
@@ -67,7 +69,16 @@ struct StreamLayout {
   }
   static constexpr int kMaxN = maxN();
   static_assert(kMaxN <= 512, "accumulators are at most 512 columns");
-  static constexpr int kNB = kMaxN < 256 ? kMaxN : 256;  // N columns per MMA / per B stage
+  static constexpr int NH = C::HALVES;  // output halves per layer (1 or 2)
+  static_assert(NH == 1 || NH == 2, "one or two output halves");
+  static constexpr int kNB = kMaxN / NH;  // N columns per MMA / per B stage (one output half)
+  static_assert(kNB <= 256, "an output half is at most 256 columns");
+  __host__ __device__ static constexpr bool halvesOk() {
+    for (int l = 0; l < NL; ++l)
+      if (C::N(l) % (64 * C::HALVES) != 0) return false;
+    return true;
+  }
+  static_assert(halvesOk(), "every layer width must split into two halves of whole 64-column panels");
   static constexpr int kActBytes = kBM * actW() * 2;
   static constexpr int kXBytes = kXRes ? 2 * kPanelBytes : 0;  // double-buffered resident x
   static constexpr int kBStageBytes = kBK * kNB * 2;
@@ -115,6 +126,7 @@ __global__ void __launch_bounds__(192, 1)
   constexpr int NL = C::NL;
   constexpr int kBS = L::kBStages;
   constexpr int kNB = L::kNB;
+  constexpr int NH = L::NH;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
@@ -122,11 +134,11 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* b_empty = bars + 8;     // [8]
   uint64_t* x_full = bars + 16;     // [2]  x ring slots or resident x buffers
   uint64_t* x_empty = bars + 18;    // [2]
-  uint64_t* acc_full = bars + 20;
-  uint64_t* act_ready = bars + 21;
-  uint64_t* mma_done = bars + 22;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+  uint64_t* acc_full = bars + 20;   // [2] per output half
+  uint64_t* act_ready = bars + 22;  // [2] per output half
+  uint64_t* mma_done = bars + 24;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 26);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
   float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
   float* ln_b = ln_g + C::N(NL - 1);
@@ -149,8 +161,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(smem_u32(&x_full[s]), 1);
       mbar_init(smem_u32(&x_empty[s]), 1);
     }
-    mbar_init(smem_u32(acc_full), 1);
-    mbar_init(smem_u32(act_ready), 4);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(smem_u32(&acc_full[h]), 1);
+      mbar_init(smem_u32(&act_ready[h]), 4);
+    }
     mbar_init(smem_u32(mma_done), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -194,12 +208,26 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
+    // Stage order per layer mirrors the MMA issue order: K panel p outer for a streamed-x first
+    // layer (each x panel serves both output halves), output half outer otherwise.
     if (lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
       const uint64_t stream = l2_policy_evict_first();
       int bs = 0, xs = 0;
       uint32_t bph = 0, xph = 0;
       bool ok = true;
+      auto stage = [&](int l, int p, int hf, int kh) -> bool {
+        if (ksteps_in<C>(l, p, kh) == 0) return true;
+        if (!mbar_wait(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) return false;
+        const int hw = C::N(l) / NH;
+        mbar_arrive_expect_tx(smem_u32(&b_full[bs]), (hw / 64) * L::kBK * 128);
+        const uint32_t dst = smem_u32(smem + L::kOffB + bs * L::kBStageBytes);
+        for (int nb = 0; nb < hw / 64; ++nb)
+          tma_load_2d_hint(dst + nb * (L::kBK * 128), &tm.w[l], smem_u32(&b_full[bs]),
+                           hf * hw + nb * 64, p * kPanel + kh * L::kBK, keep);
+        if (++bs == kBS) { bs = 0; bph ^= 1; }
+        return true;
+      };
 #pragma unroll 1
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         if constexpr (L::kXRes) {
@@ -214,11 +242,9 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
         for (int l = 0; ok && l < NL; ++l) {
           const int panels = (C::K(l) + kPanel - 1) / kPanel;
-          const int nchunks = (C::N(l) + kNB - 1) / kNB;
-          const int nb_boxes = (C::N(l) < kNB ? C::N(l) : kNB) / 64;
+          if (!L::kXRes && l == 0) {
 #pragma unroll 1
-          for (int p = 0; ok && p < panels; ++p) {
-            if (!L::kXRes && l == 0) {
+            for (int p = 0; ok && p < panels; ++p) {
               if (!mbar_wait(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
               if (args.inject != 1) {
                 mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes);
@@ -226,20 +252,15 @@ __global__ void __launch_bounds__(192, 1)
                                  smem_u32(&x_full[xs]), p * kPanel, tile * kBM, stream);
               }
               if (++xs == 2) { xs = 0; xph ^= 1; }
+              for (int hf = 0; ok && hf < NH; ++hf)
+                for (int kh = 0; ok && kh < 2; ++kh) ok = stage(l, p, hf, kh);
             }
+          } else {
 #pragma unroll 1
-            for (int nc = 0; ok && nc < nchunks; ++nc)
+            for (int hf = 0; ok && hf < NH; ++hf)
 #pragma unroll 1
-              for (int h = 0; h < 2; ++h) {
-                if (ksteps_in<C>(l, p, h) == 0) continue;
-                if (!mbar_wait(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
-                mbar_arrive_expect_tx(smem_u32(&b_full[bs]), nb_boxes * L::kBK * 128);
-                const uint32_t dst = smem_u32(smem + L::kOffB + bs * L::kBStageBytes);
-                for (int nb = 0; nb < nb_boxes; ++nb)
-                  tma_load_2d_hint(dst + nb * (L::kBK * 128), &tm.w[l], smem_u32(&b_full[bs]),
-                                   nc * kNB + nb * 64, p * kPanel + h * L::kBK, keep);
-                if (++bs == kBS) { bs = 0; bph ^= 1; }
-              }
+              for (int p = 0; ok && p < panels; ++p)
+                for (int kh = 0; ok && kh < 2; ++kh) ok = stage(l, p, hf, kh);
           }
         }
       }
@@ -247,77 +268,109 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
+    // Each layer's output is computed as two column halves with their own commit (acc_full[h]),
+    // so the epilogue of half 0 overlaps the MMAs of half 1, and the next layer's first K half
+    // (activation panels of half 0) starts as soon as act_ready[0] says they are written.
     if (lane == 0) {
       const uint32_t act_sm = smem_u32(smem + L::kOffAct);
       const uint32_t x_sm = smem_u32(smem + L::kOffX);
       const uint32_t b_sm = smem_u32(smem + L::kOffB);
       int bs = 0, xs = 0;
-      uint32_t bph = 0, xph = 0, rph = 0;
+      uint32_t bph = 0, xph = 0, rph[2] = {0, 0};
       bool first = true, ok = true;
 #pragma unroll 1
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         const int xcur = xs;  // resident x buffer of this tile
 #pragma unroll 1
         for (int l = 0; ok && l < NL; ++l) {
-          if (!first) {
-            if (!mbar_wait(smem_u32(act_ready), rph, wctx, kDevTimeoutMma)) { ok = false; break; }
-            rph ^= 1;
-          }
+          bool have[2] = {first, first};
           first = false;
-          tc_fence_after();
+          auto need = [&](int h) -> bool {  // previous epilogue half h is done
+            if (have[h]) return true;
+            if (!mbar_wait(smem_u32(&act_ready[h]), rph[h], wctx, kDevTimeoutMma)) return false;
+            rph[h] ^= 1;
+            have[h] = true;
+            tc_fence_after();
+            return true;
+          };
+          if (!need(0)) { ok = false; break; }
+          // a layer wider than the previous one (the last layer of the previous tile for l = 0)
+          // writes columns the previous epilogue's second half may still be reading
+          const int n_prev = l == 0 ? C::N(NL - 1) : C::N(l - 1);
+          if (NH == 2 && C::N(l) > n_prev && !need(1)) { ok = false; break; }
           const int panels = (C::K(l) + kPanel - 1) / kPanel;
-          const int nchunks = (C::N(l) + kNB - 1) / kNB;
-          const int ncols = C::N(l) < kNB ? C::N(l) : kNB;
+          const int hw = C::N(l) / NH;
+          // activation panels at or beyond hi_p were written by the previous epilogue's half 1
+          const int hi_p = (l == 0 || NH == 1) ? panels + 1 : C::N(l - 1) / 128;
           const int ab_bf16 = (l == 0 || !C::HIDDEN_F16) ? Elem<T>::kIsBf16 : 0;
-          const uint32_t idesc = make_idesc_f16(kBM, ncols, ab_bf16, 0, 1);
-#pragma unroll 1
-          for (int p = 0; ok && p < panels; ++p) {
-            uint32_t a_base;
+          const uint32_t idesc = make_idesc_f16(kBM, hw, ab_bf16, 0, 1);
+          const bool p_outer = !L::kXRes && l == 0;
+          // A operand of panel p (waits for x where needed); 0 on timeout
+          auto a_panel = [&](int p) -> uint32_t {
             const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1);
-            if (from_x) {
-              if constexpr (L::kXRes) {
-                if (l == 0) {
-                  if (!mbar_wait(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
-                  tc_fence_after();
-                }
-                a_base = x_sm + xcur * kPanelBytes;
-              } else {
-                if (!mbar_wait(smem_u32(&x_full[xs]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
-                tc_fence_after();
-                a_base = x_sm + xs * kPanelBytes;
-              }
+            if (!from_x) return act_sm + p * kPanelBytes;
+            if constexpr (L::kXRes) {
+              return x_sm + xcur * kPanelBytes;
             } else {
-              a_base = act_sm + p * kPanelBytes;
+              if (!mbar_wait(smem_u32(&x_full[xs]), xph, wctx, kDevTimeoutMma)) return 0u;
+              tc_fence_after();
+              return x_sm + xs * kPanelBytes;
             }
-#pragma unroll 1
-            for (int nc = 0; ok && nc < nchunks; ++nc)
-#pragma unroll 1
-              for (int h = 0; h < 2; ++h) {
-                const int ks = ksteps_in<C>(l, p, h);
-                if (ks == 0) continue;
-                if (!mbar_wait(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t bst = b_sm + bs * L::kBStageBytes;
-                for (int k = 0; k < ks; ++k) {
-                  const int kin = h * 2 + k;  // 16-wide K step within the 64-column panel
-                  const uint64_t adesc = make_sdesc_sw128(a_base + kin * 32, 16, 1024);
-                  const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK * 128, 1024);
-                  mma_ss(tmem_base + nc * kNB, adesc, bdesc, idesc,
-                         (p == 0 && h == 0 && k == 0) ? 0u : 1u);
-                }
-                mma_commit(smem_u32(&b_empty[bs]));
-                if (++bs == kBS) { bs = 0; bph ^= 1; }
+          };
+          auto issue = [&](uint32_t a_base, int p, int hf) -> bool {
+            for (int kh = 0; kh < 2; ++kh) {
+              const int ks = ksteps_in<C>(l, p, kh);
+              if (ks == 0) continue;
+              if (!mbar_wait(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) return false;
+              tc_fence_after();
+              const uint32_t bst = b_sm + bs * L::kBStageBytes;
+              for (int k = 0; k < ks; ++k) {
+                const int kin = kh * 2 + k;  // 16-wide K step within the 64-column panel
+                const uint64_t adesc = make_sdesc_sw128(a_base + kin * 32, 16, 1024);
+                const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK * 128, 1024);
+                mma_ss(tmem_base + hf * hw, adesc, bdesc, idesc, (p == 0 && kh == 0 && k == 0) ? 0u : 1u);
               }
-            if (!L::kXRes && l == 0) {
+              mma_commit(smem_u32(&b_empty[bs]));
+              if (++bs == kBS) { bs = 0; bph ^= 1; }
+            }
+            return true;
+          };
+          if (L::kXRes && l == 0) {
+            if (!mbar_wait(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            tc_fence_after();
+          }
+          if (p_outer) {
+            if (NH == 2 && !need(1)) { ok = false; break; }
+#pragma unroll 1
+            for (int p = 0; ok && p < panels; ++p) {
+              const uint32_t a = a_panel(p);
+              if (a == 0u) { ok = false; break; }
+              ok = issue(a, p, 0) && (NH == 1 || issue(a, p, 1));
               mma_commit(smem_u32(&x_empty[xs]));
               if (++xs == 2) { xs = 0; xph ^= 1; }
             }
+            if (!ok) break;
+            mma_commit(smem_u32(&acc_full[0]));
+            if (NH == 2) mma_commit(smem_u32(&acc_full[1]));
+          } else {
+#pragma unroll 1
+            for (int hf = 0; ok && hf < NH; ++hf) {
+              if (hf == 1 && !need(1)) { ok = false; break; }
+#pragma unroll 1
+              for (int p = 0; ok && p < panels; ++p) {
+                if (p >= hi_p && !need(1)) { ok = false; break; }
+                const uint32_t a = a_panel(p);
+                if (a == 0u) { ok = false; break; }
+                ok = issue(a, p, hf);
+              }
+              if (ok) mma_commit(smem_u32(&acc_full[hf]));
+            }
+            if (!ok) break;
           }
           if constexpr (L::kXRes) {
             const int last_x_layer = C::SKIP != 0 ? C::SKIP : 0;
             if (l == last_x_layer) mma_commit(smem_u32(&x_empty[xcur]));
           }
-          mma_commit(smem_u32(acc_full));
         }
         if constexpr (L::kXRes) {
           if (++xs == 2) { xs = 0; xph ^= 1; }
@@ -336,76 +389,93 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes;
     uint8_t* act = smem + L::kOffAct;
-    uint32_t acc_ph = 0;
+    uint32_t acc_ph[2] = {0, 0};
     bool ok = true;
-    auto release = [&]() {
+    auto wait_acc = [&](int h) -> bool {
+      if (!mbar_wait(smem_u32(&acc_full[h]), acc_ph[h], wctx, kDevTimeoutEpilogue)) return false;
+      acc_ph[h] ^= 1;
+      tc_fence_after();
+      return true;
+    };
+    auto release = [&](int h) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(act_ready));
+      if (lane == 0) mbar_arrive(smem_u32(&act_ready[h]));
     };
 #pragma unroll 1
     for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
       const int64_t row = static_cast<int64_t>(tile) * kBM + r;
       const int row0 = tile * kBM + q * 32;
 #pragma unroll 1
-      for (int l = 0; l < NL; ++l) {
-        if (!mbar_wait(smem_u32(acc_full), acc_ph, wctx, kDevTimeoutEpilogue)) { ok = false; break; }
-        acc_ph ^= 1;
-        tc_fence_after();
+      for (int l = 0; ok && l < NL; ++l) {
         const float* bl = bias_s + L::biasOff(l);
         const int act_id = C::ACT(l);
+        const int hc = C::N(l) / 32 / NH;  // 32-column chunks per half
         if (l + 1 < NL) {
           // hidden layer: bias + activation -> 16-bit A operand of the next layer (K-major SW128)
+          // Layers >= 1 read their A operand from this same activation buffer: the second half's
+          // MMAs of layer l still read layer l-1's activations, so writing layer l's activations
+          // waits for both halves (the next layer still starts as soon as half 0 is written).
+          if (NH == 2 && l >= 1 && !(wait_acc(0) && wait_acc(1))) { ok = false; break; }
 #pragma unroll 1
-          for (int c = 0; c < C::N(l) / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(t_lane + c * 32, v);
-            tmem_wait_ld();
-            uint8_t* line = act + (c >> 1) * kPanelBytes + r * 128;
+          for (int hf = 0; hf < NH; ++hf) {
+            if ((NH == 1 || l == 0) && !wait_acc(hf)) { ok = false; break; }
+#pragma unroll 1
+            for (int c = hf * hc; c < (hf + 1) * hc; ++c) {
+              uint32_t v[32];
+              tmem_ld32(t_lane + c * 32, v);
+              tmem_wait_ld();
+              uint8_t* line = act + (c >> 1) * kPanelBytes + r * 128;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint32_t pk[4];
+              for (int j = 0; j < 4; ++j) {
+                uint32_t pk[4];
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int i = j * 8 + e * 2;
-                const float2 bb = *reinterpret_cast<const float2*>(bl + c * 32 + i);
-                const float y0 = apply_act(act_id, __uint_as_float(v[i]) + bb.x);
-                const float y1 = apply_act(act_id, __uint_as_float(v[i + 1]) + bb.y);
-                pk[e] = C::HIDDEN_F16 ? Elem<__half>::pack(y0, y1) : Elem<T>::pack(y0, y1);
+                for (int e = 0; e < 4; ++e) {
+                  const int i = j * 8 + e * 2;
+                  const float2 bb = *reinterpret_cast<const float2*>(bl + c * 32 + i);
+                  const float y0 = apply_act(act_id, __uint_as_float(v[i]) + bb.x);
+                  const float y1 = apply_act(act_id, __uint_as_float(v[i + 1]) + bb.y);
+                  pk[e] = C::HIDDEN_F16 ? Elem<__half>::pack(y0, y1) : Elem<T>::pack(y0, y1);
+                }
+                const int chunk = (c & 1) * 4 + j;
+                *reinterpret_cast<uint4*>(line + ((chunk ^ (r & 7)) * 16)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
               }
-              const int chunk = (c & 1) * 4 + j;
-              *reinterpret_cast<uint4*>(line + ((chunk ^ (r & 7)) * 16)) =
-                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
+            fence_proxy_async_smem();
+            release(hf);
           }
-          fence_proxy_async_smem();
-          release();
         } else if constexpr (C::TAIL == kTailHead) {
           // last tensor layer + activation, then the narrow head on CUDA cores
           float o[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) o[i] = 0.0f;
 #pragma unroll 1
-          for (int c = 0; c < C::N(l) / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(t_lane + c * 32, v);
-            tmem_wait_ld();
+          for (int hf = 0; hf < NH; ++hf) {
+            if (!wait_acc(hf)) { ok = false; break; }
+#pragma unroll 1
+            for (int c = hf * hc; c < (hf + 1) * hc; ++c) {
+              uint32_t v[32];
+              tmem_ld32(t_lane + c * 32, v);
+              tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int k = c * 32 + i;
-              const float y = apply_act(act_id, __uint_as_float(v[i]) + bl[k]);
-              const float4* w4 = reinterpret_cast<const float4*>(head_w + k * 16);
+              for (int i = 0; i < 32; ++i) {
+                const int k = c * 32 + i;
+                const float y = apply_act(act_id, __uint_as_float(v[i]) + bl[k]);
+                const float4* w4 = reinterpret_cast<const float4*>(head_w + k * 16);
 #pragma unroll
-              for (int o4 = 0; o4 < (C::HEAD_N + 3) / 4; ++o4) {
-                const float4 w = w4[o4];
-                o[o4 * 4 + 0] = fmaf(y, w.x, o[o4 * 4 + 0]);
-                o[o4 * 4 + 1] = fmaf(y, w.y, o[o4 * 4 + 1]);
-                o[o4 * 4 + 2] = fmaf(y, w.z, o[o4 * 4 + 2]);
-                o[o4 * 4 + 3] = fmaf(y, w.w, o[o4 * 4 + 3]);
+                for (int o4 = 0; o4 < (C::HEAD_N + 3) / 4; ++o4) {
+                  const float4 w = w4[o4];
+                  o[o4 * 4 + 0] = fmaf(y, w.x, o[o4 * 4 + 0]);
+                  o[o4 * 4 + 1] = fmaf(y, w.y, o[o4 * 4 + 1]);
+                  o[o4 * 4 + 2] = fmaf(y, w.z, o[o4 * 4 + 2]);
+                  o[o4 * 4 + 3] = fmaf(y, w.w, o[o4 * 4 + 3]);
+                }
               }
             }
+            release(hf);
           }
-          release();
+          if (!ok) break;
           if (row < args.m) {
             T* dst = reinterpret_cast<T*>(args.out) + row * C::HEAD_N;
 #pragma unroll
@@ -418,6 +488,7 @@ __global__ void __launch_bounds__(192, 1)
           // last layer: optional LayerNorm (statistics pass over TMEM), then store via staging
           float mean = 0.f, rstd = 1.f;
           if constexpr (C::TAIL == kTailLayerNorm) {
+            if (!wait_acc(0) || (NH == 2 && !wait_acc(1))) { ok = false; break; }
             float s = 0.f, sq = 0.f;
 #pragma unroll 1
             for (int c = 0; c < C::N(l) / 32; ++c) {
@@ -436,10 +507,14 @@ __global__ void __launch_bounds__(192, 1)
           }
 #pragma unroll 1
           for (int c = 0; c < C::N(l) / 32; ++c) {
+            const int hf = c / hc;
+            if constexpr (C::TAIL != kTailLayerNorm) {
+              if (c % hc == 0 && !wait_acc(hf)) { ok = false; break; }
+            }
             uint32_t v[32];
             tmem_ld32(t_lane + c * 32, v);
             tmem_wait_ld();
-            if (c + 1 == C::N(l) / 32) release();  // the accumulator is fully read
+            if (c % hc == hc - 1) release(hf);  // this half of the accumulator is read
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -470,7 +545,6 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -50,6 +50,7 @@ struct ChainGcNoAlloc {
   __host__ __device__ static constexpr int ACT(int l) { return l == 0 ? ACT0 : kActNone; }
   static constexpr int SKIP = 0, TAIL = kTailLayerNorm, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = true;
+  static constexpr int HALVES = 2;
 };
 
 __global__ void noalloc_bf16_to_f16(const __nv_bfloat16* __restrict__ src, __half* __restrict__ dst,

@@ -68,6 +68,7 @@ struct ChainDlrmTail {
   __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
   static constexpr int SKIP = 0, TAIL = kTailHead, HEAD_N = 1, HEAD_ACT = kActSigmoid;
   static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 1;
 };
 
 }  // namespace
