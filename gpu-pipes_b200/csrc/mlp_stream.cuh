@@ -14,7 +14,11 @@
 //               for wide inputs) and every layer's weights as 32-row x (<=256)-column stages
 //               through an mbarrier ring (L2-resident: every CTA streams the same weights).
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2-5   epilogue; thread t owns row t of the tile (TMEM lane t).
+//   warps 2-9   epilogue, two warps per TMEM lane quarter: thread t of a quarter's pair owns row
+//               t of the tile (TMEM lane t); warp group 0 drains the even 32-column accumulator
+//               chunks, group 1 the odd ones, so two warps per scheduler hide each other's
+//               TMEM-load and math latency. Row sums for the LayerNorm and the head's partial
+//               dot products are combined through shared memory.
 //
 // Activations never leave the SM: the epilogue of layer l writes bias + activation of the fp32
 // accumulator as 16-bit values straight into shared memory, in the K-major SWIZZLE_128B layout
@@ -85,11 +89,19 @@ struct StreamLayout {
   static constexpr int kBiasBytes = ((biasFloats() * 4 + 1023) / 1024) * 1024;
   static constexpr int kLnBytes = C::TAIL == kTailLayerNorm ? 2 * C::N(NL - 1) * 4 : 0;
   static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * 16 * 4 + 64 * 4) : 0;
+  static constexpr int kEpiWarps = 8;
   static constexpr int kStageBytes = 32 * 64;  // per epilogue warp output staging (32 x 32 x 2 B)
-  static constexpr int kStgBytes = C::TAIL == kTailHead ? 0 : 4 * kStageBytes;
+  // LayerNorm tails stage their output in the activation buffer (free once the last layer's MMAs
+  // are complete; two 2 KB buffers per warp in its own lane quarter of panels 0 and 1)
+  static constexpr bool kStgInAct = C::TAIL == kTailLayerNorm && actW() >= 2 * kPanel;
+  static constexpr int kStgBytes = (C::TAIL == kTailHead || kStgInAct) ? 0 : kEpiWarps * kStageBytes;
+  // cross-group exchange: LayerNorm (sum, sum of squares) or head partial sums, per row
+  static constexpr int kHeadPad = ((C::HEAD_N + 3) / 4) * 4;
+  static constexpr int kXchgBytes =
+      C::TAIL == kTailHead ? kBM * kHeadPad * 4 : (C::TAIL == kTailLayerNorm ? 2 * kBM * 8 : 0);
   static constexpr int kBarBytes = 512;
   static constexpr int kFixed = kActBytes + kXBytes + kBiasBytes + kLnBytes + kHeadBytes +
-                                kStgBytes + kBarBytes + 1024;  // + alignment of the staging area
+                                kXchgBytes + kStgBytes + kBarBytes + 1024;  // + alignment of the staging area
   // ring of x panels (streamed x only), then as many B stages as fit (at most 8)
   static constexpr int kXStages = kXRes ? 0 : 2;
   static constexpr int kBStagesRaw = (kSmemLimit - kFixed - kXStages * kPanelBytes) / kBStageBytes;
@@ -101,12 +113,14 @@ struct StreamLayout {
   static constexpr int kOffBias = kOffB + kBStages * kBStageBytes;
   static constexpr int kOffLn = kOffBias + kBiasBytes;
   static constexpr int kOffHead = kOffLn + kLnBytes;
-  static constexpr int kOffStg = ((kOffHead + kHeadBytes + 1023) / 1024) * 1024;
+  static constexpr int kOffXchg = kOffHead + kHeadBytes;
+  static constexpr int kOffStg = ((kOffXchg + kXchgBytes + 1023) / 1024) * 1024;
   static constexpr int kOffBar = ((kOffStg + kStgBytes + 15) / 16) * 16;
   static constexpr int kSmemBytes = kOffBar + kBarBytes;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kOffX % 1024 == 0 && kOffB % 1024 == 0 && kOffStg % 512 == 0, "alignment");
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static_assert(kThreads == 320, "launch bounds of mlp_stream_kernel");
 };
 
 // Number of 16-wide K steps of layer l in 64-column panel p, and in its 32-row half h.
@@ -119,7 +133,7 @@ __host__ __device__ constexpr int ksteps_in(int l, int p, int h) {
 }
 
 template <class C>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     mlp_stream_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
   using T = typename C::T;
   using L = StreamLayout<C>;
@@ -139,6 +153,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* mma_done = bars + 24;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 26);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
+  uint64_t* pair_bar = bars + 28;   // [4] the two epilogue warps of each TMEM lane quarter
   float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
   float* ln_b = ln_g + C::N(NL - 1);
@@ -163,9 +178,10 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(smem_u32(&acc_full[h]), 1);
-      mbar_init(smem_u32(&act_ready[h]), 4);
+      mbar_init(smem_u32(&act_ready[h]), L::kEpiWarps);
     }
     mbar_init(smem_u32(mma_done), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&pair_bar[i]), 64);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -383,12 +399,18 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
-    const int q = warp & 3;
-    const int r = q * 32 + lane;  // row within the tile
+    // ---------------------------------------------------------------- epilogue (warps 2..9)
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int eg = (warp - 2) >> 2;   // chunk group: even (0) or odd (1) 32-column chunks
+    const int r = q * 32 + lane;      // row within the tile
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStageBytes;
     uint8_t* act = smem + L::kOffAct;
+    // output staging: two buffers per warp inside the activation buffer (LayerNorm tails) or one
+    // dedicated buffer per warp
+    uint8_t* stg = L::kStgInAct ? act + q * 4096 + eg * 2048
+                                : smem + L::kOffStg + (warp - 2) * L::kStageBytes;
+    float* xchg = reinterpret_cast<float*>(smem + L::kOffXchg);
+    int sb = 0;
     uint32_t acc_ph[2] = {0, 0};
     bool ok = true;
     auto wait_acc = [&](int h) -> bool {
@@ -402,6 +424,30 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&act_ready[h]));
     };
+    // barrier of the two warps of this lane quarter (bounded, like every wait here)
+    uint32_t pph = 0;
+    auto pair_sync = [&]() -> bool {
+      mbar_arrive(smem_u32(&pair_bar[q]));
+      const bool r = mbar_wait(smem_u32(&pair_bar[q]), pph, wctx, kDevTimeoutEpilogue);
+      pph ^= 1;
+      return r;
+    };
+    // stage 32 packed columns of this warp's 32 rows and store them with one TMA box
+    auto store_chunk = [&](int c, int row0, const uint32_t (&pk)[16]) {
+      uint8_t* s = L::kStgInAct ? stg + sb * kPanelBytes : stg;
+      if (lane == 0) {
+        if constexpr (L::kStgInAct) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
+      }
+      __syncwarp();
+      stage_chunk32(s, lane, pk);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(s), c * 32, row0);
+        bulk_commit_group();
+      }
+      if constexpr (L::kStgInAct) sb ^= 1;
+    };
 #pragma unroll 1
     for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
       const int64_t row = static_cast<int64_t>(tile) * kBM + r;
@@ -410,7 +456,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int l = 0; ok && l < NL; ++l) {
         const float* bl = bias_s + L::biasOff(l);
         const int act_id = C::ACT(l);
-        const int hc = C::N(l) / 32 / NH;  // 32-column chunks per half
+        const int hc = C::N(l) / 32 / NH;  // 32-column chunks per half (even)
         if (l + 1 < NL) {
           // hidden layer: bias + activation -> 16-bit A operand of the next layer (K-major SW128)
           // Layers >= 1 read their A operand from this same activation buffer: the second half's
@@ -421,7 +467,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int hf = 0; hf < NH; ++hf) {
             if ((NH == 1 || l == 0) && !wait_acc(hf)) { ok = false; break; }
 #pragma unroll 1
-            for (int c = hf * hc; c < (hf + 1) * hc; ++c) {
+            for (int c = hf * hc + eg; c < (hf + 1) * hc; c += 2) {
               uint32_t v[32];
               tmem_ld32(t_lane + c * 32, v);
               tmem_wait_ld();
@@ -446,15 +492,17 @@ __global__ void __launch_bounds__(192, 1)
             release(hf);
           }
         } else if constexpr (C::TAIL == kTailHead) {
-          // last tensor layer + activation, then the narrow head on CUDA cores
-          float o[16];
+          // last tensor layer + activation, then the narrow head on CUDA cores: each group forms
+          // the partial dot products of its chunks, group 1 hands them to group 0
+          constexpr int HP = L::kHeadPad;
+          float o[HP];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = 0.0f;
+          for (int i = 0; i < HP; ++i) o[i] = 0.0f;
 #pragma unroll 1
           for (int hf = 0; hf < NH; ++hf) {
             if (!wait_acc(hf)) { ok = false; break; }
 #pragma unroll 1
-            for (int c = hf * hc; c < (hf + 1) * hc; ++c) {
+            for (int c = hf * hc + eg; c < (hf + 1) * hc; c += 2) {
               uint32_t v[32];
               tmem_ld32(t_lane + c * 32, v);
               tmem_wait_ld();
@@ -464,7 +512,7 @@ __global__ void __launch_bounds__(192, 1)
                 const float y = apply_act(act_id, __uint_as_float(v[i]) + bl[k]);
                 const float4* w4 = reinterpret_cast<const float4*>(head_w + k * 16);
 #pragma unroll
-                for (int o4 = 0; o4 < (C::HEAD_N + 3) / 4; ++o4) {
+                for (int o4 = 0; o4 < HP / 4; ++o4) {
                   const float4 w = w4[o4];
                   o[o4 * 4 + 0] = fmaf(y, w.x, o[o4 * 4 + 0]);
                   o[o4 * 4 + 1] = fmaf(y, w.y, o[o4 * 4 + 1]);
@@ -476,14 +524,32 @@ __global__ void __launch_bounds__(192, 1)
             release(hf);
           }
           if (!ok) break;
-          if (row < args.m) {
-            T* dst = reinterpret_cast<T*>(args.out) + row * C::HEAD_N;
+          float4* xo = reinterpret_cast<float4*>(xchg + r * HP);
+          if (eg == 1) {
 #pragma unroll
-            for (int i = 0; i < C::HEAD_N; ++i) {
-              const float y = apply_act(C::HEAD_ACT, o[i] + head_b[i]);
-              if constexpr (Elem<T>::kIsBf16) dst[i] = __float2bfloat16_rn(y); else dst[i] = __float2half_rn(y);
+            for (int o4 = 0; o4 < HP / 4; ++o4)
+              xo[o4] = make_float4(o[o4 * 4], o[o4 * 4 + 1], o[o4 * 4 + 2], o[o4 * 4 + 3]);
+          }
+          if (!pair_sync()) { ok = false; break; }
+          if (eg == 0) {
+#pragma unroll
+            for (int o4 = 0; o4 < HP / 4; ++o4) {
+              const float4 p = xo[o4];
+              o[o4 * 4 + 0] += p.x;
+              o[o4 * 4 + 1] += p.y;
+              o[o4 * 4 + 2] += p.z;
+              o[o4 * 4 + 3] += p.w;
+            }
+            if (row < args.m) {
+              T* dst = reinterpret_cast<T*>(args.out) + row * C::HEAD_N;
+#pragma unroll
+              for (int i = 0; i < C::HEAD_N; ++i) {
+                const float y = apply_act(C::HEAD_ACT, o[i] + head_b[i]);
+                if constexpr (Elem<T>::kIsBf16) dst[i] = __float2bfloat16_rn(y); else dst[i] = __float2half_rn(y);
+              }
             }
           }
+          if (!pair_sync()) { ok = false; break; }  // the exchange slots are free again
         } else {
           // last layer: optional LayerNorm (statistics pass over TMEM), then store via staging
           float mean = 0.f, rstd = 1.f;
@@ -491,7 +557,7 @@ __global__ void __launch_bounds__(192, 1)
             if (!wait_acc(0) || (NH == 2 && !wait_acc(1))) { ok = false; break; }
             float s = 0.f, sq = 0.f;
 #pragma unroll 1
-            for (int c = 0; c < C::N(l) / 32; ++c) {
+            for (int c = eg; c < C::N(l) / 32; c += 2) {
               uint32_t v[32];
               tmem_ld32(t_lane + c * 32, v);
               tmem_wait_ld();
@@ -502,42 +568,50 @@ __global__ void __launch_bounds__(192, 1)
                 sq = fmaf(y, y, sq);
               }
             }
+            float2* xs = reinterpret_cast<float2*>(xchg);
+            xs[eg * kBM + r] = make_float2(s, sq);
+            if (!pair_sync()) { ok = false; break; }
+            const float2 other = xs[(eg ^ 1) * kBM + r];
+            if (!pair_sync()) { ok = false; break; }  // the exchange slots are free again
+            s += other.x;
+            sq += other.y;
             mean = s * (1.0f / C::N(l));
             rstd = rsqrtf(fmaxf(sq * (1.0f / C::N(l)) - mean * mean, 0.0f) + args.ln_eps);
           }
 #pragma unroll 1
-          for (int c = 0; c < C::N(l) / 32; ++c) {
-            const int hf = c / hc;
+          for (int hf = 0; hf < NH; ++hf) {
             if constexpr (C::TAIL != kTailLayerNorm) {
-              if (c % hc == 0 && !wait_acc(hf)) { ok = false; break; }
+              if (!wait_acc(hf)) { ok = false; break; }
             }
-            uint32_t v[32];
-            tmem_ld32(t_lane + c * 32, v);
-            tmem_wait_ld();
-            if (c % hc == hc - 1) release(hf);  // this half of the accumulator is read
-            uint32_t pk[16];
+#pragma unroll 1
+            for (int c = hf * hc + eg; c < (hf + 1) * hc; c += 2) {
+              uint32_t v[32];
+              tmem_ld32(t_lane + c * 32, v);
+              tmem_wait_ld();
+              if (c + 2 >= (hf + 1) * hc) release(hf);  // this warp's part of the half is read
+              uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float y0 = __uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i];
-              float y1 = __uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1];
-              if constexpr (C::TAIL == kTailLayerNorm) {
-                y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
-                y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
-              } else {
-                y0 = apply_act(act_id, y0);
-                y1 = apply_act(act_id, y1);
+              for (int i = 0; i < 16; ++i) {
+                float y0 = __uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i];
+                float y1 = __uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1];
+                if constexpr (C::TAIL == kTailLayerNorm) {
+                  y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
+                  y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
+                } else {
+                  y0 = apply_act(act_id, y0);
+                  y1 = apply_act(act_id, y1);
+                }
+                pk[i] = Elem<T>::pack(y0, y1);
               }
-              pk[i] = Elem<T>::pack(y0, y1);
+              store_chunk(c, row0, pk);
             }
+          }
+          if constexpr (L::kStgInAct) {
+            // the next tile's hidden epilogue rewrites this lane quarter of the activation
+            // buffer: both warps' stores must have read their staging first
             if (lane == 0) bulk_wait_group_read<0>();
             __syncwarp();
-            stage_chunk32(stg, lane, pk);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(stg), c * 32, row0);
-              bulk_commit_group();
-            }
+            if (!pair_sync()) { ok = false; break; }
           }
         }
       }
