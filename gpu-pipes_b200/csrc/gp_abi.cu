@@ -127,6 +127,27 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, u
   return GP_OK;
 }
 
+// Weight matrix [rows = K, cols = N] (row-major, 16-bit) as a 3-D map {64, K, N / 64} with the
+// 64-column blocks 128 bytes apart; box {64, box_rows, box_blocks}, SWIZZLE_128B.
+int make_tmap_w3d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                  uint32_t box_rows, uint32_t box_blocks) {
+  if (cols % 64 != 0)
+    return set_error(GP_ERR_SHAPE, "weight width %llu is not a multiple of 64", (unsigned long long)cols);
+  const CUtensorMapDataType dt =
+      dtype == GP_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {cols * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, box_blocks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(GP_ERR_DRIVER, "cuTensorMapEncodeTiled (3-D) failed (%d) rows=%llu cols=%llu", (int)r,
+                     (unsigned long long)rows, (unsigned long long)cols);
+  return GP_OK;
+}
+
 // ------------------------------------------------------------------------------------------------
 // per-device workspace
 // ------------------------------------------------------------------------------------------------

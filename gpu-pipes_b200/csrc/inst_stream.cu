@@ -49,10 +49,10 @@ struct ChainNerfTrunk : ChainNerf {
 };
 
 int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot>(c); }
-int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>>(c); }
-int launch_gc_relu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActRelu>>(c); }
-int launch_gc_relu_f16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1536, kActRelu>>(c); }
-int launch_gc_relu_f16_k1024(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1024, kActRelu>>(c); }
+int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>, 2>(c); }
+int launch_gc_relu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActRelu>, 2>(c); }
+int launch_gc_relu_f16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1536, kActRelu>, 2>(c); }
+int launch_gc_relu_f16_k1024(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1024, kActRelu>, 2>(c); }
 int launch_nerf_f16(const LaunchCtx& c) { return launch_stream<ChainNerf>(c); }
 int launch_nerf_trunk_f16(const LaunchCtx& c) { return launch_stream<ChainNerfTrunk>(c); }
 

@@ -45,12 +45,11 @@ constexpr int kTailHead = 3;  // narrow output layer on CUDA cores (stream kerne
 //   HIDDEN_F16: with bf16 data, keep hidden activations in fp16 (11-bit mantissa instead of 8)
 //   and run layers >= 1 as fp16 x fp16 MMAs on fp16 copies of their weights (bf16 -> fp16 is
 //   exact for weights within fp16 range). Input, first layer and output stay bf16.
-template <class C>
+template <class C, int CG = 1>
 struct StreamLayout {
   static constexpr int NL = C::NL;
   static constexpr int K0 = C::K(0);
   static constexpr bool kXRes = K0 <= kPanel;  // whole x tile resident (one 64-column panel)
-  static constexpr int kBK = 32;               // weight rows per B stage
   __host__ __device__ static constexpr int maxN() {
     int m = 0;
     for (int l = 0; l < NL; ++l) m = C::N(l) > m ? C::N(l) : m;
@@ -85,7 +84,12 @@ struct StreamLayout {
   static_assert(halvesOk(), "every layer width must split into two halves of whole 64-column panels");
   static constexpr int kActBytes = kBM * actW() * 2;
   static constexpr int kXBytes = kXRes ? 2 * kPanelBytes : 0;  // double-buffered resident x
-  static constexpr int kBStageBytes = kBK * kNB * 2;
+  __host__ __device__ static constexpr bool pairOk() {
+    for (int l = 0; l < NL; ++l)
+      if ((C::N(l) / NH) % 128 != 0) return false;
+    return true;
+  }
+  static_assert(CG == 1 || (CG == 2 && pairOk()), "CTA pairs need output halves of 128-column multiples");
   static constexpr int kBiasBytes = ((biasFloats() * 4 + 1023) / 1024) * 1024;
   static constexpr int kLnBytes = C::TAIL == kTailLayerNorm ? 2 * C::N(NL - 1) * 4 : 0;
   static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * 16 * 4 + 64 * 4) : 0;
@@ -102,8 +106,15 @@ struct StreamLayout {
   static constexpr int kBarBytes = 512;
   static constexpr int kFixed = kActBytes + kXBytes + kBiasBytes + kLnBytes + kHeadBytes +
                                 kXchgBytes + kStgBytes + kBarBytes + 1024;  // + alignment of the staging area
-  // ring of x panels (streamed x only), then as many B stages as fit (at most 8)
+  // ring of x panels (streamed x only), then as many B stages as fit (at most 8). A stage holds
+  // kBK weight rows of one output half (a CTA pair runs 256-row MMAs and each CTA stages half of
+  // the columns) and arrives as ONE 3-D TMA request: TMA cost is largely per request, so 64-row
+  // stages are used whenever three of them fit, 32-row stages otherwise.
   static constexpr int kXStages = kXRes ? 0 : 2;
+  static constexpr int kRingBytes = kSmemLimit - kFixed - kXStages * kPanelBytes;
+  static constexpr int kBK = kRingBytes / (64 * kNB * 2 / CG) >= 3 ? 64 : 32;  // weight rows per stage
+  static constexpr int kSub = kPanel / kBK;                                     // stages per K panel
+  static constexpr int kBStageBytes = kBK * kNB * 2 / CG;
   static constexpr int kBStagesRaw = (kSmemLimit - kFixed - kXStages * kPanelBytes) / kBStageBytes;
   static constexpr int kBStages = kBStagesRaw > 8 ? 8 : kBStagesRaw;
   static_assert(kBStages >= 2, "shared memory budget");
@@ -123,20 +134,20 @@ struct StreamLayout {
   static_assert(kThreads == 320, "launch bounds of mlp_stream_kernel");
 };
 
-// Number of 16-wide K steps of layer l in 64-column panel p, and in its 32-row half h.
-template <class C>
+// Number of 16-wide K steps of layer l in 64-column panel p, and in its BK-row part h.
+template <class C, int BK>
 __host__ __device__ constexpr int ksteps_in(int l, int p, int h) {
   const int total = C::K(l) / 16;
-  int first = p * 4 + h * 2;
+  int first = p * 4 + h * (BK / 16);
   int n = total - first;
-  return n <= 0 ? 0 : (n > 2 ? 2 : n);
+  return n <= 0 ? 0 : (n > BK / 16 ? BK / 16 : n);
 }
 
-template <class C>
-__global__ void __launch_bounds__(320, 1)
-    mlp_stream_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+template <class C, int CG>
+__device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const ChainArgs& args) {
   using T = typename C::T;
-  using L = StreamLayout<C>;
+  using L = StreamLayout<C, CG>;
+  constexpr bool kPair = CG == 2;
   constexpr int NL = C::NL;
   constexpr int kBS = L::kBStages;
   constexpr int kNB = L::kNB;
@@ -162,6 +173,11 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  // work unit: kBM rows per CTA (one tile, or the pair's two tiles of a 256-row unit)
+  const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if ((smem_u32(smem) & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
@@ -178,7 +194,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(smem_u32(&acc_full[h]), 1);
-      mbar_init(smem_u32(&act_ready[h]), L::kEpiWarps);
+      mbar_init(smem_u32(&act_ready[h]), L::kEpiWarps * CG);
     }
     mbar_init(smem_u32(mma_done), 1);
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&pair_bar[i]), 64);
@@ -187,8 +203,13 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (warp == 0 && lane == 0) prefetch_tmap(&tm.x);
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_holder), 512);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_holder), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), 512);
+      tmem_relinquish();
+    }
   }
   // fp32 biases, LayerNorm parameters and head weights
   for (int l = 0; l < NL; ++l) {
@@ -216,11 +237,19 @@ __global__ void __launch_bounds__(320, 1)
       head_b[i] = (i < C::HEAD_N && hb != nullptr) ? Elem<T>::to_f(hb[i]) : 0.0f;
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrival
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
-  const int num_tiles = args.num_tiles;
+  const int num_units = args.num_tiles;  // in units of kBM * CG rows
+  // barrier address as seen by the loads / arrivals of this CTA (the leader's in a pair)
+  auto leader_bar = [&](const uint64_t* b) -> uint32_t {
+    return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
+  };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -233,26 +262,40 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t bph = 0, xph = 0;
       bool ok = true;
       auto stage = [&](int l, int p, int hf, int kh) -> bool {
-        if (ksteps_in<C>(l, p, kh) == 0) return true;
-        if (!mbar_wait(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) return false;
+        if (ksteps_in<C, L::kBK>(l, p, kh) == 0) return true;
+        if (!mbar_wait<kPair>(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) return false;
         const int hw = C::N(l) / NH;
-        mbar_arrive_expect_tx(smem_u32(&b_full[bs]), (hw / 64) * L::kBK * 128);
+        const int hwc = hw / CG;  // columns staged by this CTA
+        if (leader) mbar_arrive_expect_tx(smem_u32(&b_full[bs]), (hwc / 64) * L::kBK * 128 * CG);
         const uint32_t dst = smem_u32(smem + L::kOffB + bs * L::kBStageBytes);
-        for (int nb = 0; nb < hw / 64; ++nb)
-          tma_load_2d_hint(dst + nb * (L::kBK * 128), &tm.w[l], smem_u32(&b_full[bs]),
-                           hf * hw + nb * 64, p * kPanel + kh * L::kBK, keep);
+        const uint32_t fb = leader_bar(&b_full[bs]);
+        // one request: kBK rows x (hwc / 64) column blocks, block after block in shared memory
+        const int blk = (hf * hw + static_cast<int>(rank) * hwc) / 64;
+        const int row = p * kPanel + kh * L::kBK;
+        if constexpr (kPair) {
+          tma_load_3d_pair(dst, &tm.w[l], fb, 0, row, blk, keep);
+        } else {
+          tma_load_3d_hint(dst, &tm.w[l], fb, 0, row, blk, keep);
+        }
         if (++bs == kBS) { bs = 0; bph ^= 1; }
         return true;
       };
+      // one 64-column x panel of this CTA's rows into x slot xs
+      auto load_x = [&](int p, int row) {
+        if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes * CG);
+        const uint32_t dst = smem_u32(smem + L::kOffX + xs * kPanelBytes);
+        if constexpr (kPair) {
+          tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[xs]), p * kPanel, row, stream);
+        } else {
+          tma_load_2d_hint(dst, &tm.x, smem_u32(&x_full[xs]), p * kPanel, row, stream);
+        }
+      };
 #pragma unroll 1
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int unit = unit0; ok && unit < num_units; unit += units_step) {
+        const int row_base = unit * kBM * CG + static_cast<int>(rank) * kBM;
         if constexpr (L::kXRes) {
-          if (!mbar_wait(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
-          if (args.inject != 1) {
-            mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes);
-            tma_load_2d_hint(smem_u32(smem + L::kOffX + xs * kPanelBytes), &tm.x,
-                             smem_u32(&x_full[xs]), 0, tile * kBM, stream);
-          }
+          if (!mbar_wait<kPair>(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
+          if (args.inject != 1) load_x(0, row_base);
           if (++xs == 2) { xs = 0; xph ^= 1; }
         }
 #pragma unroll 1
@@ -261,22 +304,18 @@ __global__ void __launch_bounds__(320, 1)
           if (!L::kXRes && l == 0) {
 #pragma unroll 1
             for (int p = 0; ok && p < panels; ++p) {
-              if (!mbar_wait(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
-              if (args.inject != 1) {
-                mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes);
-                tma_load_2d_hint(smem_u32(smem + L::kOffX + xs * kPanelBytes), &tm.x,
-                                 smem_u32(&x_full[xs]), p * kPanel, tile * kBM, stream);
-              }
+              if (!mbar_wait<kPair>(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
+              if (args.inject != 1) load_x(p, row_base);
               if (++xs == 2) { xs = 0; xph ^= 1; }
               for (int hf = 0; ok && hf < NH; ++hf)
-                for (int kh = 0; ok && kh < 2; ++kh) ok = stage(l, p, hf, kh);
+                for (int kh = 0; ok && kh < L::kSub; ++kh) ok = stage(l, p, hf, kh);
             }
           } else {
 #pragma unroll 1
             for (int hf = 0; ok && hf < NH; ++hf)
 #pragma unroll 1
               for (int p = 0; ok && p < panels; ++p)
-                for (int kh = 0; ok && kh < 2; ++kh) ok = stage(l, p, hf, kh);
+                for (int kh = 0; ok && kh < L::kSub; ++kh) ok = stage(l, p, hf, kh);
           }
         }
       }
@@ -287,7 +326,12 @@ __global__ void __launch_bounds__(320, 1)
     // Each layer's output is computed as two column halves with their own commit (acc_full[h]),
     // so the epilogue of half 0 overlaps the MMAs of half 1, and the next layer's first K half
     // (activation panels of half 0) starts as soon as act_ready[0] says they are written.
-    if (lane == 0) {
+    // In a CTA pair only the leader issues: 256-row MMAs over both CTAs' A operands and weight
+    // halves, commits multicast to the barriers of both CTAs.
+    auto commit_any = [&](uint64_t* bar) {
+      if constexpr (kPair) mma_commit_pair(smem_u32(bar), 0x3); else mma_commit(smem_u32(bar));
+    };
+    if (lane == 0 && leader) {
       const uint32_t act_sm = smem_u32(smem + L::kOffAct);
       const uint32_t x_sm = smem_u32(smem + L::kOffX);
       const uint32_t b_sm = smem_u32(smem + L::kOffB);
@@ -295,15 +339,15 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t bph = 0, xph = 0, rph[2] = {0, 0};
       bool first = true, ok = true;
 #pragma unroll 1
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int xcur = xs;  // resident x buffer of this tile
+      for (int unit = unit0; ok && unit < num_units; unit += units_step) {
+        const int xcur = xs;  // resident x buffer of this unit
 #pragma unroll 1
         for (int l = 0; ok && l < NL; ++l) {
           bool have[2] = {first, first};
           first = false;
           auto need = [&](int h) -> bool {  // previous epilogue half h is done
             if (have[h]) return true;
-            if (!mbar_wait(smem_u32(&act_ready[h]), rph[h], wctx, kDevTimeoutMma)) return false;
+            if (!mbar_wait<kPair>(smem_u32(&act_ready[h]), rph[h], wctx, kDevTimeoutMma)) return false;
             rph[h] ^= 1;
             have[h] = true;
             tc_fence_after();
@@ -319,7 +363,7 @@ __global__ void __launch_bounds__(320, 1)
           // activation panels at or beyond hi_p were written by the previous epilogue's half 1
           const int hi_p = (l == 0 || NH == 1) ? panels + 1 : C::N(l - 1) / 128;
           const int ab_bf16 = (l == 0 || !C::HIDDEN_F16) ? Elem<T>::kIsBf16 : 0;
-          const uint32_t idesc = make_idesc_f16(kBM, hw, ab_bf16, 0, 1);
+          const uint32_t idesc = make_idesc_f16(kBM * CG, hw, ab_bf16, 0, 1);
           const bool p_outer = !L::kXRes && l == 0;
           // A operand of panel p (waits for x where needed); 0 on timeout
           auto a_panel = [&](int p) -> uint32_t {
@@ -328,31 +372,36 @@ __global__ void __launch_bounds__(320, 1)
             if constexpr (L::kXRes) {
               return x_sm + xcur * kPanelBytes;
             } else {
-              if (!mbar_wait(smem_u32(&x_full[xs]), xph, wctx, kDevTimeoutMma)) return 0u;
+              if (!mbar_wait<kPair>(smem_u32(&x_full[xs]), xph, wctx, kDevTimeoutMma)) return 0u;
               tc_fence_after();
               return x_sm + xs * kPanelBytes;
             }
           };
           auto issue = [&](uint32_t a_base, int p, int hf) -> bool {
-            for (int kh = 0; kh < 2; ++kh) {
-              const int ks = ksteps_in<C>(l, p, kh);
+            for (int kh = 0; kh < L::kSub; ++kh) {
+              const int ks = ksteps_in<C, L::kBK>(l, p, kh);
               if (ks == 0) continue;
-              if (!mbar_wait(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) return false;
+              if (!mbar_wait<kPair>(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) return false;
               tc_fence_after();
               const uint32_t bst = b_sm + bs * L::kBStageBytes;
               for (int k = 0; k < ks; ++k) {
-                const int kin = kh * 2 + k;  // 16-wide K step within the 64-column panel
+                const int kin = kh * (L::kBK / 16) + k;  // 16-wide K step within the 64-column panel
                 const uint64_t adesc = make_sdesc_sw128(a_base + kin * 32, 16, 1024);
                 const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK * 128, 1024);
-                mma_ss(tmem_base + hf * hw, adesc, bdesc, idesc, (p == 0 && kh == 0 && k == 0) ? 0u : 1u);
+                const uint32_t acc = (p == 0 && kh == 0 && k == 0) ? 0u : 1u;
+                if constexpr (kPair) {
+                  mma_ss_pair(tmem_base + hf * hw, adesc, bdesc, idesc, acc);
+                } else {
+                  mma_ss(tmem_base + hf * hw, adesc, bdesc, idesc, acc);
+                }
               }
-              mma_commit(smem_u32(&b_empty[bs]));
+              commit_any(&b_empty[bs]);
               if (++bs == kBS) { bs = 0; bph ^= 1; }
             }
             return true;
           };
           if (L::kXRes && l == 0) {
-            if (!mbar_wait(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            if (!mbar_wait<kPair>(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
             tc_fence_after();
           }
           if (p_outer) {
@@ -362,12 +411,12 @@ __global__ void __launch_bounds__(320, 1)
               const uint32_t a = a_panel(p);
               if (a == 0u) { ok = false; break; }
               ok = issue(a, p, 0) && (NH == 1 || issue(a, p, 1));
-              mma_commit(smem_u32(&x_empty[xs]));
+              commit_any(&x_empty[xs]);
               if (++xs == 2) { xs = 0; xph ^= 1; }
             }
             if (!ok) break;
-            mma_commit(smem_u32(&acc_full[0]));
-            if (NH == 2) mma_commit(smem_u32(&acc_full[1]));
+            commit_any(&acc_full[0]);
+            if (NH == 2) commit_any(&acc_full[1]);
           } else {
 #pragma unroll 1
             for (int hf = 0; ok && hf < NH; ++hf) {
@@ -379,23 +428,26 @@ __global__ void __launch_bounds__(320, 1)
                 if (a == 0u) { ok = false; break; }
                 ok = issue(a, p, hf);
               }
-              if (ok) mma_commit(smem_u32(&acc_full[hf]));
+              if (ok) commit_any(&acc_full[hf]);
             }
             if (!ok) break;
           }
           if constexpr (L::kXRes) {
             const int last_x_layer = C::SKIP != 0 ? C::SKIP : 0;
-            if (l == last_x_layer) mma_commit(smem_u32(&x_empty[xcur]));
+            if (l == last_x_layer) commit_any(&x_empty[xcur]);
           }
         }
         if constexpr (L::kXRes) {
           if (++xs == 2) { xs = 0; xph ^= 1; }
         }
       }
-      mma_commit(smem_u32(mma_done));
+      // drain: every issued MMA has completed before TMEM can be released
+      commit_any(mma_done);
+    }
+    if (lane == 0) {
       volatile int no_abort = 0;
       WaitCtx drain{args.status, &no_abort, args.timeout_ns};
-      mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
+      mbar_wait<kPair>(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -414,7 +466,7 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t acc_ph[2] = {0, 0};
     bool ok = true;
     auto wait_acc = [&](int h) -> bool {
-      if (!mbar_wait(smem_u32(&acc_full[h]), acc_ph[h], wctx, kDevTimeoutEpilogue)) return false;
+      if (!mbar_wait<kPair>(smem_u32(&acc_full[h]), acc_ph[h], wctx, kDevTimeoutEpilogue)) return false;
       acc_ph[h] ^= 1;
       tc_fence_after();
       return true;
@@ -422,7 +474,9 @@ __global__ void __launch_bounds__(320, 1)
     auto release = [&](int h) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&act_ready[h]));
+      if (lane == 0) {
+        if constexpr (kPair) mbar_arrive_cluster(leader_bar(&act_ready[h])); else mbar_arrive(smem_u32(&act_ready[h]));
+      }
     };
     // barrier of the two warps of this lane quarter (bounded, like every wait here)
     uint32_t pph = 0;
@@ -449,9 +503,10 @@ __global__ void __launch_bounds__(320, 1)
       if constexpr (L::kStgInAct) sb ^= 1;
     };
 #pragma unroll 1
-    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-      const int64_t row = static_cast<int64_t>(tile) * kBM + r;
-      const int row0 = tile * kBM + q * 32;
+    for (int unit = unit0; ok && unit < num_units; unit += units_step) {
+      const int row_base = unit * kBM * CG + static_cast<int>(rank) * kBM;
+      const int64_t row = static_cast<int64_t>(row_base) + r;
+      const int row0 = row_base + q * 32;
 #pragma unroll 1
       for (int l = 0; ok && l < NL; ++l) {
         const float* bl = bias_s + L::biasOff(l);
@@ -620,11 +675,28 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // no CTA leaves while the pair's MMAs may still read its memory
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if constexpr (kPair) tmem_dealloc_pair(tmem_base, 512); else tmem_dealloc(tmem_base, 512);
   }
+}
+
+template <class C>
+__global__ void __launch_bounds__(320, 1)
+    mlp_stream_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  mlp_stream_body<C, 1>(tm, args);
+}
+
+// CTA-pair form: two CTAs of a cluster share each weight stage (half of its columns each).
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    mlp_stream_pair_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  mlp_stream_body<C, 2>(tm, args);
 }
 
 }  // namespace gp

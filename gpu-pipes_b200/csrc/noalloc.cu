@@ -115,6 +115,19 @@ int na_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t
   return r == CUDA_SUCCESS ? GP_OK : set_error(GP_ERR_DRIVER, "cuTensorMapEncodeTiled failed (%d)", (int)r);
 }
 
+// weight [rows, cols] as {64, rows, cols / 64} (block stride 128 B), box {64, box_rows, box_blocks}
+int na_tmap_w3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t rows, uint64_t cols,
+                uint32_t box_rows, uint32_t box_blocks) {
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {cols * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, box_blocks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_na_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GP_OK : set_error(GP_ERR_DRIVER, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+}
+
 template <int ACT0>
 int na_launch(NoAllocDevice& d, int64_t m, const void* x, const void* w0, const void* b0,
               const void* w1, const void* b1, const void* gamma, const void* beta, void* out,
@@ -137,11 +150,11 @@ int na_launch(NoAllocDevice& d, int64_t m, const void* x, const void* w0, const 
   if (rc == GP_OK)
     rc = na_tmap(&tm.out, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, m, C::N(1), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc == GP_OK)
-    rc = na_tmap(&tm.w[0], w0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C::K(0), C::N(0), 64, Lay::kBK,
-                 CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = na_tmap_w3d(&tm.w[0], w0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C::K(0), C::N(0), Lay::kBK,
+                     C::N(0) / Lay::NH / 64);
   if (rc == GP_OK)
-    rc = na_tmap(&tm.w[1], d.scratch, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, C::K(1), C::N(1), 64, Lay::kBK,
-                 CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = na_tmap_w3d(&tm.w[1], d.scratch, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, C::K(1), C::N(1), Lay::kBK,
+                     C::N(1) / Lay::NH / 64);
   if (rc != GP_OK) return rc;
   ChainArgs args;
   std::memset(&args, 0, sizeof(args));

@@ -1,4 +1,5 @@
-// Host launcher for mlp_stream_kernel.
+// Host launcher for mlp_stream_kernel (one CTA per 128-row tile) and mlp_stream_pair_kernel
+// (CTA pairs over 256-row units, each CTA staging half of every weight stage).
 #pragma once
 
 #include <cstring>
@@ -16,11 +17,17 @@ static __global__ void bf16_to_f16_kernel(const __nv_bfloat16* __restrict__ src,
     dst[i] = __float2half_rn(__bfloat162float(src[i]));
 }
 
-template <class C>
+template <class C, int CG = 1>
 int launch_stream(const LaunchCtx& c) {
-  using L = StreamLayout<C>;
-  const void* kern = reinterpret_cast<const void*>(&mlp_stream_kernel<C>);
+  using L = StreamLayout<C, CG>;
+  const void* kern = nullptr;
+  if constexpr (CG == 2) {
+    kern = reinterpret_cast<const void*>(&mlp_stream_pair_kernel<C>);
+  } else {
+    kern = reinterpret_cast<const void*>(&mlp_stream_kernel<C>);
+  }
   static unsigned long long done_mask = 0;
+  static int max_clusters[64] = {0};
   int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
   if (rc != GP_OK) return rc;
   const int dt = c.spec->dtype;
@@ -50,7 +57,9 @@ int launch_stream(const LaunchCtx& c) {
   for (int l = 0; rc == GP_OK && l < C::NL; ++l) {
     const bool conv = C::HIDDEN_F16 && l > 0;
     const void* wl = conv ? static_cast<const void*>(static_cast<char*>(scratch) + offs[l]) : c.w[l];
-    rc = make_tmap_2d(&tm.w[l], wl, conv ? GP_F16 : dt, C::K(l), C::N(l), 64, L::kBK, 128);
+    // one stage = kBK rows of this CTA's columns of one output half
+    rc = make_tmap_w3d(&tm.w[l], wl, conv ? GP_F16 : dt, C::K(l), C::N(l), L::kBK,
+                       C::N(l) / L::NH / CG / 64);
   }
   if (rc != GP_OK) {
     if (scratch != nullptr) workspace_release(c.stream);
@@ -61,8 +70,37 @@ int launch_stream(const LaunchCtx& c) {
     args.head_w = c.w[C::NL];
     args.head_b = c.args.bias[C::NL];
   }
-  const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-  mlp_stream_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  args.num_tiles = static_cast<int>((c.m + kBM * CG - 1) / (kBM * CG));
+  if constexpr (CG == 1) {
+    const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
+    mlp_stream_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  } else {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& mc = max_clusters[dev & 63];
+    if (mc == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (c.sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(L::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = L::kSmemBytes;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = c.sm_count / 2;
+      }
+      mc = n;
+    }
+    const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
+    mlp_stream_pair_kernel<C><<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  }
   if (scratch != nullptr) workspace_release(c.stream);
   return GP_OK;
 }
