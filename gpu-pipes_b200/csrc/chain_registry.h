@@ -42,6 +42,8 @@ int set_error(int code, const char* fmt, ...);
 // swizzle_bytes: 128, 64, 32 or 0 (none)
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
                  uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
+int make_tmap_2d_f32(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                     uint32_t box_rows, int swizzle_bytes);
 int make_tmap_w3d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
                   uint32_t box_rows, uint32_t box_blocks);
 

@@ -127,6 +127,23 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, u
   return GP_OK;
 }
 
+// fp32 matrix [rows, cols] (row-major) with box {box_cols, box_rows}
+int make_tmap_2d_f32(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                     uint32_t box_rows, int swizzle_bytes) {
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(GP_ERR_DRIVER, "cuTensorMapEncodeTiled (fp32) failed (%d) rows=%llu cols=%llu", (int)r,
+                     (unsigned long long)rows, (unsigned long long)cols);
+  return GP_OK;
+}
+
 // Weight matrix [rows = K, cols = N] (row-major, 16-bit) as a 3-D map {64, K, N / 64} with the
 // 64-column blocks 128 bytes apart; box {64, box_rows, box_blocks}, SWIZZLE_128B.
 int make_tmap_w3d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,

@@ -11,9 +11,11 @@
 // between layers goes through L2, as in the reference, rather than HBM.
 //
 //   warp 0     TMA producer: per 64-wide K step one A panel (128 x 64, K-major SW128) and one
-//              B stage (64 x 256, N-major SW128) into a 4-stage mbarrier ring
+//              B stage (64 x 256, N-major SW128, one 3-D request) into a 3-stage mbarrier ring
 //   warp 1     TMEM allocator + MMA issuer: 128 x 256 x 16 MMAs into one of two accumulators
-//   warps 2-5  epilogue of the previous tile (thread = row) while the next tile accumulates
+//   warps 2-9  epilogue of the previous tile while the next tile accumulates: two warps per
+//              TMEM lane quarter (thread = row), even / odd 32-column chunks; bias from shared
+//              memory, 16-bit residual by vector loads, output through TMA stores
 #pragma once
 
 #include "chain_common.cuh"
@@ -40,15 +42,21 @@ struct GemmArgs {
 
 struct GemmLayout {
   static constexpr int kBN = 256;
-  static constexpr int kStages = 4;
+  static constexpr int kStages = 3;
   static constexpr int kABytes = kPanelBytes;           // 128 x 64 x 2
   static constexpr int kBBytes = kPanel * kBN * 2;      // 64 x 256 x 2
   static constexpr int kStageBytes = kABytes + kBBytes; // 48 KB
-  static constexpr int kStgBytes = 4 * 32 * 64;         // per epilogue warp: 32 x 32 x 2 B
-  static constexpr int kOffStg = kStages * kStageBytes;
-  static constexpr int kOffBar = kOffStg + kStgBytes;
+  static constexpr int kMaxN = 4096;                    // widest layer (bias staged in fp32)
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kStgWarpBytes = 4096;            // two 32 x 32 x 2 B buffers or one x 4 B
+  static constexpr int kOffBias = kStages * kStageBytes;
+  static constexpr int kOffStg = kOffBias + kMaxN * 4;
+  static constexpr int kOffBar = kOffStg + kEpiWarps * kStgWarpBytes;
   static constexpr int kSmemBytes = kOffBar + 256;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+  static_assert(kOffStg % 1024 == 0, "staging alignment (SWIZZLE_128B fp32 tiles)");
+  static_assert(kThreads == 320, "launch bounds of mlp_gemm_kernel");
 };
 
 __device__ __forceinline__ float load16(const void* p, int64_t i, int is_bf16) {
@@ -57,19 +65,45 @@ __device__ __forceinline__ float load16(const void* p, int64_t i, int is_bf16) {
   return __half2float(__ushort_as_half(bits));
 }
 
-__global__ void __launch_bounds__(192, 1)
+// GELU, tanh form 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))) (Hendrycks & Gimpel), with the
+// hardware tanh approximation (tanh.approx.f32, max relative error about 2^-11, below the 16-bit
+// rounding of the stored activation).
+__device__ __forceinline__ float gelu_tanh_fast(float v) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * v * (1.0f + t);
+}
+
+template <int ACT>
+__device__ __forceinline__ float gemm_act(float v) {
+  if constexpr (ACT == kActRelu) return fmaxf(v, 0.0f);
+  else if constexpr (ACT == kActGeluTanh) return gelu_tanh_fast(v);
+  else if constexpr (ACT == kActNone) return v;
+  else return apply_act(ACT, v);
+}
+
+__device__ __forceinline__ float2 unpack16x2(uint32_t w, int is_bf16) {
+  if (is_bf16) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// ACT: activation after bias (+ residual). OUT_F32: fp32 output (else 16-bit, `out_f16`).
+template <int ACT, bool OUT_F32>
+__global__ void __launch_bounds__(320, 1)
     mlp_gemm_kernel(const __grid_constant__ TensorMaps tm, const GemmArgs args, int ab_bf16) {
   using L = GemmLayout;
   constexpr int kS = L::kStages;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* full = bars;            // [4]
-  uint64_t* empty = bars + 4;       // [4]
+  uint64_t* full = bars;            // [kS]
+  uint64_t* empty = bars + 4;       // [kS]
   uint64_t* acc_full = bars + 8;    // [2]
   uint64_t* acc_empty = bars + 10;  // [2]
   uint64_t* mma_done = bars + 12;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if ((smem_u32(smem) & 1023u) != 0) {
@@ -83,7 +117,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), 4);
+      mbar_init(smem_u32(&acc_empty[b]), L::kEpiWarps);
     }
     mbar_init(smem_u32(mma_done), 1);
     *abort_flag = 0;
@@ -93,6 +127,8 @@ __global__ void __launch_bounds__(192, 1)
     tmem_alloc(smem_u32(tmem_holder), 512);
     tmem_relinquish();
   }
+  for (int i = threadIdx.x; i < args.n; i += blockDim.x)
+    bias_s[i] = args.bias != nullptr ? load16(args.bias, i, args.bias_bf16) : 0.0f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -115,9 +151,9 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t st = smem_u32(smem + s * L::kStageBytes);
           mbar_arrive_expect_tx(smem_u32(&full[s]), L::kStageBytes);
           tma_load_2d_hint(st, &tm.x, smem_u32(&full[s]), kp * kPanel, mt * kBM, keep);
-          for (int nb = 0; nb < L::kBN / 64; ++nb)
-            tma_load_2d_hint(st + L::kABytes + nb * (kPanel * 128), &tm.w[0], smem_u32(&full[s]),
-                             nt * L::kBN + nb * 64, kp * kPanel, keep);
+          // the whole 64 x 256 B stage (four 64-column blocks) as one 3-D request
+          tma_load_3d_hint(st + L::kABytes, &tm.w[0], smem_u32(&full[s]), 0, kp * kPanel,
+                           nt * (L::kBN / 64), keep);
           if (++s == kS) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -162,9 +198,12 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
+    // epilogue: two warps per TMEM lane quarter, even / odd 32-column chunks
     const int q = warp & 3;
+    const int eg = (warp - 2) >> 2;
     const int r = q * 32 + lane;
-    uint8_t* stg = smem + L::kOffStg + (warp - 2) * (32 * 64);
+    uint8_t* stg = smem + L::kOffStg + (warp - 2) * L::kStgWarpBytes;
+    int sb = 0;
     uint32_t aph[2] = {0, 0};
     int it = 0;
 #pragma unroll 1
@@ -178,11 +217,11 @@ __global__ void __launch_bounds__(192, 1)
       const int row0 = mt * kBM + q * 32;
       const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * L::kBN;
 #pragma unroll 1
-      for (int c = 0; c < L::kBN / 32; ++c) {
+      for (int c = eg; c < L::kBN / 32; c += 2) {
         uint32_t v[32];
         tmem_ld32(t_lane + c * 32, v);
         tmem_wait_ld();
-        if (c + 1 == L::kBN / 32) {  // accumulator fully read: the MMA may reuse it
+        if (c + 2 >= L::kBN / 32) {  // this warp's part of the accumulator is read
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
@@ -190,24 +229,37 @@ __global__ void __launch_bounds__(192, 1)
         const int col0 = nt * L::kBN + c * 32;
         float y[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float val = __uint_as_float(v[i]);
-          if (args.bias != nullptr) val += load16(args.bias, col0 + i, args.bias_bf16);
-          y[i] = val;
-        }
+        for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(v[i]) + bias_s[col0 + i];
         if (args.resid != nullptr && row < args.m) {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              static_cast<const uint16_t*>(args.resid) + row * args.n + col0);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            y[i] += load16(args.resid, row * args.n + col0 + i, args.resid_bf16);
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w = __ldg(src + j);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = unpack16x2(ws[e], args.resid_bf16);
+              y[j * 8 + e * 2] += f.x;
+              y[j * 8 + e * 2 + 1] += f.y;
+            }
+          }
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) y[i] = apply_act(args.act, y[i]);
-        if (args.out_f32) {
-          if (row < args.m) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(args.out) + row * args.n + col0);
+        for (int i = 0; i < 32; ++i) y[i] = gemm_act<ACT>(y[i]);
+        if constexpr (OUT_F32) {
+          // 32 x 32 fp32 tile, 128-byte rows in the SWIZZLE_128B layout of the output map
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(stg), col0, row0);
+            bulk_commit_group();
           }
         } else {
           uint32_t pk[16];
@@ -215,15 +267,17 @@ __global__ void __launch_bounds__(192, 1)
           for (int i = 0; i < 16; ++i)
             pk[i] = args.out_f16 ? Elem<__half>::pack(y[2 * i], y[2 * i + 1])
                                  : Elem<__nv_bfloat16>::pack(y[2 * i], y[2 * i + 1]);
-          if (lane == 0) bulk_wait_group_read<0>();
+          uint8_t* s = stg + sb * 2048;
+          if (lane == 0) bulk_wait_group_read<1>();  // the store that last read buffer sb is done
           __syncwarp();
-          stage_chunk32(stg, lane, pk);
+          stage_chunk32(s, lane, pk);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(stg), col0, row0);
+            if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(s), col0, row0);
             bulk_commit_group();
           }
+          sb ^= 1;
         }
       }
     }

@@ -15,24 +15,32 @@
 namespace gp {
 namespace {
 
-constexpr int kGemmThreads = 192;
+template <int ACT, bool OUT_F32>
+int gemm_launch_t(cudaStream_t s, int grid, const TensorMaps& tm, const GemmArgs& g, int a_bf16) {
+  static unsigned long long done_mask = 0;
+  const void* kern = reinterpret_cast<const void*>(&mlp_gemm_kernel<ACT, OUT_F32>);
+  int rc = ensure_smem_attr(kern, GemmLayout::kSmemBytes, &done_mask);
+  if (rc != GP_OK) return rc;
+  mlp_gemm_kernel<ACT, OUT_F32><<<grid, GemmLayout::kThreads, GemmLayout::kSmemBytes, s>>>(tm, g, a_bf16);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+}
 
 int gemm_launch(cudaStream_t s, int sm_count, const void* a, int a_bf16, int64_t m, int k,
                 const void* w, int n, const void* bias, int bias_bf16, const void* resid,
                 int resid_bf16, int act, void* out, int out_kind /*0 bf16, 1 f16, 2 f32*/,
                 int* status, unsigned long long timeout_ns) {
-  static unsigned long long done_mask = 0;
-  int rc = ensure_smem_attr(reinterpret_cast<const void*>(&mlp_gemm_kernel), GemmLayout::kSmemBytes,
-                            &done_mask);
-  if (rc != GP_OK) return rc;
-  if (n % GemmLayout::kBN != 0) return set_error(GP_ERR_UNSUPPORTED, "gemm layer width %d", n);
+  if (n % GemmLayout::kBN != 0 || n > GemmLayout::kMaxN)
+    return set_error(GP_ERR_UNSUPPORTED, "gemm layer width %d", n);
   TensorMaps tm;
   std::memset(&tm, 0, sizeof(tm));
   const int adt = a_bf16 ? GP_BF16 : GP_F16;
-  rc = make_tmap_2d(&tm.x, a, adt, m, k, kPanel, kBM, 128);
-  if (rc == GP_OK) rc = make_tmap_2d(&tm.w[0], w, adt, k, n, 64, kPanel, 128);
-  if (rc == GP_OK && out_kind != 2)
-    rc = make_tmap_2d(&tm.out, out, out_kind == 0 ? GP_BF16 : GP_F16, m, n, 32, 32, 64);
+  int rc = make_tmap_2d(&tm.x, a, adt, m, k, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], w, adt, k, n, kPanel, GemmLayout::kBN / 64);
+  if (rc == GP_OK) {
+    rc = out_kind == 2 ? make_tmap_2d_f32(&tm.out, out, m, n, 32, 32, 128)
+                       : make_tmap_2d(&tm.out, out, out_kind == 0 ? GP_BF16 : GP_F16, m, n, 32, 32, 64);
+  }
   if (rc != GP_OK) return rc;
   GemmArgs g;
   std::memset(&g, 0, sizeof(g));
@@ -52,9 +60,16 @@ int gemm_launch(cudaStream_t s, int sm_count, const void* a, int a_bf16, int64_t
   g.status = status;
   g.timeout_ns = timeout_ns;
   const int grid = g.num_tiles < sm_count ? g.num_tiles : sm_count;
-  mlp_gemm_kernel<<<grid, kGemmThreads, GemmLayout::kSmemBytes, s>>>(tm, g, a_bf16);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+  const bool f32 = out_kind == 2;
+  switch (act) {
+    case kActNone: return f32 ? gemm_launch_t<kActNone, true>(s, grid, tm, g, a_bf16)
+                              : gemm_launch_t<kActNone, false>(s, grid, tm, g, a_bf16);
+    case kActRelu: return f32 ? gemm_launch_t<kActRelu, true>(s, grid, tm, g, a_bf16)
+                              : gemm_launch_t<kActRelu, false>(s, grid, tm, g, a_bf16);
+    case kActGeluTanh: return f32 ? gemm_launch_t<kActGeluTanh, true>(s, grid, tm, g, a_bf16)
+                                  : gemm_launch_t<kActGeluTanh, false>(s, grid, tm, g, a_bf16);
+    default: return set_error(GP_ERR_UNSUPPORTED, "gemm activation %d", act);
+  }
 }
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
