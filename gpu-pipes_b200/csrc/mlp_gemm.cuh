@@ -2,17 +2,20 @@
 // wide to stay in one SM (BERT-large FFN 1024 -> 4096 -> 1024, DLRM top 480 -> 1024 -> 1024 -> 512):
 //
 //   out[M, N] = epilogue(A[M, K] . W[K, N])   epilogue = + bias, activation, + residual,
-//                                             16-bit (TMA store) or fp32 (direct) output
+//                                             16-bit or fp32 output through TMA stores
 //
 // The reference runs these layers as pipeline stages connected by L2-resident queues
 // (apps/bert_ffn/pipelined/bert_ffn_pl.cuh:132-162, apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl.cuh:
-// 185-224). Here each layer is one persistent launch over 128 x 256 output tiles, and the host
-// runs a chain over row chunks sized so that every intermediate stays within L2: the hand-off
-// between layers goes through L2, as in the reference, rather than HBM.
+// 185-224). Here each layer is one persistent launch over 256 x 256 output tiles, one per CTA
+// pair (cta_group::2: the leader issues 256-row MMAs over both CTAs' operands; each CTA loads its
+// own 128 A rows and half of the B columns), and the host runs a chain over row chunks sized so
+// that every intermediate stays within L2: the hand-off between layers goes through L2, as in the
+// reference, rather than HBM.
 //
 //   warp 0     TMA producer: per 64-wide K step one A panel (128 x 64, K-major SW128) and one
-//              B stage (64 x 256, N-major SW128, one 3-D request) into a 3-stage mbarrier ring
-//   warp 1     TMEM allocator + MMA issuer: 128 x 256 x 16 MMAs into one of two accumulators
+//              B stage (64 x 128 per CTA, N-major SW128, one 3-D request) into an mbarrier ring
+//   warp 1     TMEM allocator + MMA issuer (pair leader): 256 x 256 x 16 MMAs into one of two
+//              accumulators
 //   warps 2-9  epilogue of the previous tile while the next tile accumulates: two warps per
 //              TMEM lane quarter (thread = row), even / odd 32-column chunks; bias from shared
 //              memory, 16-bit residual by vector loads, output through TMA stores
@@ -40,12 +43,15 @@ struct GemmArgs {
   unsigned long long timeout_ns;
 };
 
-struct GemmLayout {
+// CG = 1: 128 x 256 output tiles per CTA. CG = 2: 256 x 256 tiles per CTA pair (cta_group::2
+// MMAs issued by the leader), each CTA loading its own 128 A rows and half of the B columns.
+template <int CG>
+struct GemmLayoutT {
   static constexpr int kBN = 256;
-  static constexpr int kStages = 3;
-  static constexpr int kABytes = kPanelBytes;           // 128 x 64 x 2
-  static constexpr int kBBytes = kPanel * kBN * 2;      // 64 x 256 x 2
-  static constexpr int kStageBytes = kABytes + kBBytes; // 48 KB
+  static constexpr int kStages = CG == 2 ? 4 : 3;
+  static constexpr int kABytes = kPanelBytes;             // 128 x 64 x 2
+  static constexpr int kBBytes = kPanel * kBN * 2 / CG;   // 64 x 256 (/ 2) x 2
+  static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB, or 32 KB per CTA of a pair
   static constexpr int kMaxN = 4096;                    // widest layer (bias staged in fp32)
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
@@ -58,6 +64,7 @@ struct GemmLayout {
   static_assert(kOffStg % 1024 == 0, "staging alignment (SWIZZLE_128B fp32 tiles)");
   static_assert(kThreads == 320, "launch bounds of mlp_gemm_kernel");
 };
+using GemmLayout = GemmLayoutT<1>;
 
 __device__ __forceinline__ float load16(const void* p, int64_t i, int is_bf16) {
   const uint16_t bits = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
@@ -89,11 +96,12 @@ __device__ __forceinline__ float2 unpack16x2(uint32_t w, int is_bf16) {
 }
 
 // ACT: activation after bias (+ residual). OUT_F32: fp32 output (else 16-bit, `out_f16`).
-template <int ACT, bool OUT_F32>
-__global__ void __launch_bounds__(320, 1)
-    mlp_gemm_kernel(const __grid_constant__ TensorMaps tm, const GemmArgs args, int ab_bf16) {
-  using L = GemmLayout;
+// args.num_tiles counts units of (128 * CG) x 256 output elements.
+template <int ACT, bool OUT_F32, int CG>
+__device__ __forceinline__ void mlp_gemm_body(const TensorMaps& tm, const GemmArgs& args, int ab_bf16) {
+  using L = GemmLayoutT<CG>;
   constexpr int kS = L::kStages;
+  constexpr bool kPair = CG == 2;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* full = bars;            // [kS]
@@ -105,6 +113,10 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
   float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if ((smem_u32(smem) & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
@@ -117,21 +129,37 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), L::kEpiWarps);
+      mbar_init(smem_u32(&acc_empty[b]), L::kEpiWarps * CG);
     }
     mbar_init(smem_u32(mma_done), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_holder), 512);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_holder), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), 512);
+      tmem_relinquish();
+    }
   }
   for (int i = threadIdx.x; i < args.n; i += blockDim.x)
     bias_s[i] = args.bias != nullptr ? load16(args.bias, i, args.bias_bf16) : 0.0f;
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrival
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
+  // barrier address as seen by the loads / arrivals of this CTA (the leader's in a pair)
+  auto leader_bar = [&](const uint64_t* b) -> uint32_t {
+    return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
+  };
+  auto commit_any = [&](uint64_t* bar) {
+    if constexpr (kPair) mma_commit_pair(smem_u32(bar), 0x3); else mma_commit(smem_u32(bar));
+  };
   const uint32_t tmem_base = *tmem_holder;
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
   const int kpanels = (args.k + kPanel - 1) / kPanel;
@@ -142,18 +170,25 @@ __global__ void __launch_bounds__(320, 1)
       int s = 0;
       uint32_t ph = 0;
 #pragma unroll 1
-      for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x) {
+      for (int t = unit0; t < args.num_tiles; t += units_step) {
         const int mt = t / args.n_tiles, nt = t % args.n_tiles;
+        const int arow = (mt * CG + static_cast<int>(rank)) * kBM;
+        const int bblk = nt * (L::kBN / 64) + static_cast<int>(rank) * (L::kBN / 64 / CG);
         bool ok = true;
 #pragma unroll 1
         for (int kp = 0; kp < kpanels; ++kp) {
-          if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
+          if (!mbar_wait<kPair>(smem_u32(&empty[s]), ph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
           const uint32_t st = smem_u32(smem + s * L::kStageBytes);
-          mbar_arrive_expect_tx(smem_u32(&full[s]), L::kStageBytes);
-          tma_load_2d_hint(st, &tm.x, smem_u32(&full[s]), kp * kPanel, mt * kBM, keep);
-          // the whole 64 x 256 B stage (four 64-column blocks) as one 3-D request
-          tma_load_3d_hint(st + L::kABytes, &tm.w[0], smem_u32(&full[s]), 0, kp * kPanel,
-                           nt * (L::kBN / 64), keep);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&full[s]), L::kStageBytes * CG);
+          const uint32_t fb = leader_bar(&full[s]);
+          // A: this CTA's 128 rows; B: its 64-column blocks of the tile as one 3-D request
+          if constexpr (kPair) {
+            tma_load_2d_pair(st, &tm.x, fb, kp * kPanel, arow, keep);
+            tma_load_3d_pair(st + L::kABytes, &tm.w[0], fb, 0, kp * kPanel, bblk, keep);
+          } else {
+            tma_load_2d_hint(st, &tm.x, fb, kp * kPanel, arow, keep);
+            tma_load_3d_hint(st + L::kABytes, &tm.w[0], fb, 0, kp * kPanel, bblk, keep);
+          }
           if (++s == kS) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -161,40 +196,48 @@ __global__ void __launch_bounds__(320, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(kBM, L::kBN, ab_bf16, 0, 1);
+    if (lane == 0 && leader) {
+      const uint32_t idesc = make_idesc_f16(kBM * CG, L::kBN, ab_bf16, 0, 1);
       int s = 0, it = 0;
       uint32_t ph = 0, eph[2] = {0, 0};
       bool ok = true;
 #pragma unroll 1
-      for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x, ++it) {
+      for (int t = unit0; ok && t < args.num_tiles; t += units_step, ++it) {
         const int b = it & 1;
         if (it >= 2) {
-          if (!mbar_wait(smem_u32(&acc_empty[b]), eph[b], wctx, kDevTimeoutMma)) break;
+          if (!mbar_wait<kPair>(smem_u32(&acc_empty[b]), eph[b], wctx, kDevTimeoutMma)) break;
           eph[b] ^= 1;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + b * L::kBN;
 #pragma unroll 1
         for (int kp = 0; kp < kpanels; ++kp) {
-          if (!mbar_wait(smem_u32(&full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait<kPair>(smem_u32(&full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * L::kStageBytes);
           const uint64_t adesc = make_sdesc_sw128(st, 16, 1024);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t bdesc = make_sdesc_sw128(st + L::kABytes + k * 2048, kPanel * 128, 1024);
-            mma_ss(d, adesc + static_cast<uint64_t>(k * 2), bdesc, idesc, (kp | k) != 0 ? 1u : 0u);
+            const uint32_t acc = (kp | k) != 0 ? 1u : 0u;
+            if constexpr (kPair) {
+              mma_ss_pair(d, adesc + static_cast<uint64_t>(k * 2), bdesc, idesc, acc);
+            } else {
+              mma_ss(d, adesc + static_cast<uint64_t>(k * 2), bdesc, idesc, acc);
+            }
           }
-          mma_commit(smem_u32(&empty[s]));
+          commit_any(&empty[s]);
           if (++s == kS) { s = 0; ph ^= 1; }
         }
-        if (ok) mma_commit(smem_u32(&acc_full[b]));
+        if (ok) commit_any(&acc_full[b]);
       }
-      mma_commit(smem_u32(mma_done));
+      // drain: every issued MMA has completed before TMEM can be released
+      commit_any(mma_done);
+    }
+    if (lane == 0) {
       volatile int no_abort = 0;
       WaitCtx drain{args.status, &no_abort, args.timeout_ns};
-      mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
+      mbar_wait<kPair>(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -207,14 +250,15 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t aph[2] = {0, 0};
     int it = 0;
 #pragma unroll 1
-    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++it) {
+    for (int t = unit0; t < args.num_tiles; t += units_step, ++it) {
       const int b = it & 1;
       const int mt = t / args.n_tiles, nt = t % args.n_tiles;
-      if (!mbar_wait(smem_u32(&acc_full[b]), aph[b], wctx, kDevTimeoutEpilogue)) break;
+      if (!mbar_wait<kPair>(smem_u32(&acc_full[b]), aph[b], wctx, kDevTimeoutEpilogue)) break;
       aph[b] ^= 1;
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(mt) * kBM + r;
-      const int row0 = mt * kBM + q * 32;
+      const int rbase = (mt * CG + static_cast<int>(rank)) * kBM;
+      const int64_t row = static_cast<int64_t>(rbase) + r;
+      const int row0 = rbase + q * 32;
       const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * L::kBN;
 #pragma unroll 1
       for (int c = eg; c < L::kBN / 32; c += 2) {
@@ -224,7 +268,9 @@ __global__ void __launch_bounds__(320, 1)
         if (c + 2 >= L::kBN / 32) {  // this warp's part of the accumulator is read
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+          if (lane == 0) {
+            if constexpr (kPair) mbar_arrive_cluster(leader_bar(&acc_empty[b])); else mbar_arrive(smem_u32(&acc_empty[b]));
+          }
         }
         const int col0 = nt * L::kBN + c * 32;
         float y[32];
@@ -285,11 +331,27 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // no CTA leaves while the pair's MMAs may still read its memory
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if constexpr (kPair) tmem_dealloc_pair(tmem_base, 512); else tmem_dealloc(tmem_base, 512);
   }
+}
+
+template <int ACT, bool OUT_F32>
+__global__ void __launch_bounds__(320, 1)
+    mlp_gemm_kernel(const __grid_constant__ TensorMaps tm, const GemmArgs args, int ab_bf16) {
+  mlp_gemm_body<ACT, OUT_F32, 1>(tm, args, ab_bf16);
+}
+
+template <int ACT, bool OUT_F32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    mlp_gemm_pair_kernel(const __grid_constant__ TensorMaps tm, const GemmArgs args, int ab_bf16) {
+  mlp_gemm_body<ACT, OUT_F32, 2>(tm, args, ab_bf16);
 }
 
 // Row LayerNorm over fp32 rows of width N (multiple of 128): one warp per row, two passes in

@@ -15,13 +15,40 @@
 namespace gp {
 namespace {
 
+// CTA-pair launch: 256 x 256 tiles, one cluster of two CTAs per tile in flight.
 template <int ACT, bool OUT_F32>
-int gemm_launch_t(cudaStream_t s, int grid, const TensorMaps& tm, const GemmArgs& g, int a_bf16) {
+int gemm_launch_t(cudaStream_t s, int sm_count, const TensorMaps& tm, const GemmArgs& g, int a_bf16) {
+  using L = GemmLayoutT<2>;
   static unsigned long long done_mask = 0;
-  const void* kern = reinterpret_cast<const void*>(&mlp_gemm_kernel<ACT, OUT_F32>);
-  int rc = ensure_smem_attr(kern, GemmLayout::kSmemBytes, &done_mask);
+  static int max_clusters[64] = {0};
+  const void* kern = reinterpret_cast<const void*>(&mlp_gemm_pair_kernel<ACT, OUT_F32>);
+  int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
   if (rc != GP_OK) return rc;
-  mlp_gemm_kernel<ACT, OUT_F32><<<grid, GemmLayout::kThreads, GemmLayout::kSmemBytes, s>>>(tm, g, a_bf16);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& mc = max_clusters[dev & 63];
+  if (mc == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(L::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = sm_count / 2;
+    }
+    mc = n;
+  }
+  const int clusters = g.num_tiles < mc ? g.num_tiles : mc;
+  mlp_gemm_pair_kernel<ACT, OUT_F32><<<2 * clusters, L::kThreads, L::kSmemBytes, s>>>(tm, g, a_bf16);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
 }
@@ -36,7 +63,8 @@ int gemm_launch(cudaStream_t s, int sm_count, const void* a, int a_bf16, int64_t
   std::memset(&tm, 0, sizeof(tm));
   const int adt = a_bf16 ? GP_BF16 : GP_F16;
   int rc = make_tmap_2d(&tm.x, a, adt, m, k, kPanel, kBM, 128);
-  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], w, adt, k, n, kPanel, GemmLayout::kBN / 64);
+  // each CTA of a pair loads half of the tile's 64-column blocks
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], w, adt, k, n, kPanel, GemmLayout::kBN / 64 / 2);
   if (rc == GP_OK) {
     rc = out_kind == 2 ? make_tmap_2d_f32(&tm.out, out, m, n, 32, 32, 128)
                        : make_tmap_2d(&tm.out, out, out_kind == 0 ? GP_BF16 : GP_F16, m, n, 32, 32, 64);
@@ -48,7 +76,7 @@ int gemm_launch(cudaStream_t s, int sm_count, const void* a, int a_bf16, int64_t
   g.n = n;
   g.k = k;
   g.n_tiles = n / GemmLayout::kBN;
-  g.num_tiles = static_cast<int>((m + kBM - 1) / kBM) * g.n_tiles;
+  g.num_tiles = static_cast<int>((m + 2 * kBM - 1) / (2 * kBM)) * g.n_tiles;  // 256-row units
   g.act = act;
   g.out_f32 = out_kind == 2;
   g.out_f16 = out_kind == 1;
@@ -59,7 +87,7 @@ int gemm_launch(cudaStream_t s, int sm_count, const void* a, int a_bf16, int64_t
   g.out = out;
   g.status = status;
   g.timeout_ns = timeout_ns;
-  const int grid = g.num_tiles < sm_count ? g.num_tiles : sm_count;
+  const int grid = sm_count;
   const bool f32 = out_kind == 2;
   switch (act) {
     case kActNone: return f32 ? gemm_launch_t<kActNone, true>(s, grid, tm, g, a_bf16)
