@@ -48,7 +48,7 @@ struct GemmArgs {
 template <int CG>
 struct GemmLayoutT {
   static constexpr int kBN = 256;
-  static constexpr int kStages = CG == 2 ? 4 : 3;
+  static constexpr int kStages = CG == 2 ? 5 : 3;
   static constexpr int kABytes = kPanelBytes;             // 128 x 64 x 2
   static constexpr int kBBytes = kPanel * kBN * 2 / CG;   // 64 x 256 (/ 2) x 2
   static constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB, or 32 KB per CTA of a pair
@@ -59,7 +59,9 @@ struct GemmLayoutT {
   static constexpr int kOffBias = kStages * kStageBytes;
   static constexpr int kOffStg = kOffBias + kMaxN * 4;
   static constexpr int kOffBar = kOffStg + kEpiWarps * kStgWarpBytes;
-  static constexpr int kSmemBytes = kOffBar + 256;
+  static constexpr int kBarBytes = 256;  // 24 eight-byte slots used (see the kernel)
+  static constexpr int kSmemBytes = kOffBar + kBarBytes;
+  static_assert(kStages <= 8, "barrier slots for at most 8 stages");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kOffStg % 1024 == 0, "staging alignment (SWIZZLE_128B fp32 tiles)");
   static_assert(kThreads == 320, "launch bounds of mlp_gemm_kernel");
@@ -104,13 +106,13 @@ __device__ __forceinline__ void mlp_gemm_body(const TensorMaps& tm, const GemmAr
   constexpr bool kPair = CG == 2;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* full = bars;            // [kS]
-  uint64_t* empty = bars + 4;       // [kS]
-  uint64_t* acc_full = bars + 8;    // [2]
-  uint64_t* acc_empty = bars + 10;  // [2]
-  uint64_t* mma_done = bars + 12;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  uint64_t* full = bars;            // [kS <= 8]
+  uint64_t* empty = bars + 8;       // [kS <= 8]
+  uint64_t* acc_full = bars + 16;   // [2]
+  uint64_t* acc_empty = bars + 18;  // [2]
+  uint64_t* mma_done = bars + 20;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
   float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = kPair ? cluster_ctarank() : 0u;

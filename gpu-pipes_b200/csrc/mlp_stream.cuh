@@ -92,7 +92,8 @@ struct StreamLayout {
   static_assert(CG == 1 || (CG == 2 && pairOk()), "CTA pairs need output halves of 128-column multiples");
   static constexpr int kBiasBytes = ((biasFloats() * 4 + 1023) / 1024) * 1024;
   static constexpr int kLnBytes = C::TAIL == kTailLayerNorm ? 2 * C::N(NL - 1) * 4 : 0;
-  static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * 16 * 4 + 64 * 4) : 0;
+  static constexpr int kHeadPad = ((C::HEAD_N + 3) / 4) * 4;  // head outputs, padded to float4
+  static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * kHeadPad * 4 + 64 * 4) : 0;
   static constexpr int kEpiWarps = 8;
   static constexpr int kStageBytes = 32 * 64;  // per epilogue warp output staging (32 x 32 x 2 B)
   // LayerNorm tails stage their output in the activation buffer (free once the last layer's MMAs
@@ -100,7 +101,6 @@ struct StreamLayout {
   static constexpr bool kStgInAct = C::TAIL == kTailLayerNorm && actW() >= 2 * kPanel;
   static constexpr int kStgBytes = (C::TAIL == kTailHead || kStgInAct) ? 0 : kEpiWarps * kStageBytes;
   // cross-group exchange: LayerNorm (sum, sum of squares) or head partial sums, per row
-  static constexpr int kHeadPad = ((C::HEAD_N + 3) / 4) * 4;
   static constexpr int kXchgBytes =
       C::TAIL == kTailHead ? kBM * kHeadPad * 4 : (C::TAIL == kTailLayerNorm ? 2 * kBM * 8 : 0);
   static constexpr int kBarBytes = 512;
@@ -168,8 +168,8 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
   float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
   float* ln_b = ln_g + C::N(NL - 1);
-  float* head_w = reinterpret_cast<float*>(smem + L::kOffHead);  // [N_last][16] fp32
-  float* head_b = head_w + C::N(NL - 1) * 16;                    // [16]
+  float* head_w = reinterpret_cast<float*>(smem + L::kOffHead);  // [N_last][kHeadPad] fp32
+  float* head_b = head_w + C::N(NL - 1) * L::kHeadPad;           // [16]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -226,11 +226,11 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
     }
   }
   if constexpr (C::TAIL == kTailHead) {
-    // head weights [N_last, HEAD_N] (row-major, 16-bit) -> fp32 [N_last][16], zero padded
+    // head weights [N_last, HEAD_N] (row-major, 16-bit) -> fp32 [N_last][kHeadPad], zero padded
     const T* hw = reinterpret_cast<const T*>(args.head_w);
     const T* hb = reinterpret_cast<const T*>(args.head_b);
-    for (int i = threadIdx.x; i < C::N(NL - 1) * 16; i += blockDim.x) {
-      const int k = i / 16, o = i % 16;
+    for (int i = threadIdx.x; i < C::N(NL - 1) * L::kHeadPad; i += blockDim.x) {
+      const int k = i / L::kHeadPad, o = i % L::kHeadPad;
       head_w[i] = o < C::HEAD_N ? Elem<T>::to_f(hw[k * C::HEAD_N + o]) : 0.0f;
     }
     for (int i = threadIdx.x; i < 16; i += blockDim.x)
@@ -565,7 +565,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               for (int i = 0; i < 32; ++i) {
                 const int k = c * 32 + i;
                 const float y = apply_act(act_id, __uint_as_float(v[i]) + bl[k]);
-                const float4* w4 = reinterpret_cast<const float4*>(head_w + k * 16);
+                const float4* w4 = reinterpret_cast<const float4*>(head_w + k * HP);
 #pragma unroll
                 for (int o4 = 0; o4 < HP / 4; ++o4) {
                   const float4 w = w4[o4];
