@@ -83,7 +83,10 @@ struct StreamLayout {
   }
   static_assert(halvesOk(), "every layer width must split into two halves of whole 64-column panels");
   static constexpr int kActBytes = kBM * actW() * 2;
-  static constexpr int kXBytes = kXRes ? 2 * kPanelBytes : 0;  // double-buffered resident x
+  // resident x: one buffer. x is released once its last reader (layer 0, or the skip layer) has
+  // run, so the next tile's x loads while the remaining layers run; the 16 KB saved go to the
+  // weight ring.
+  static constexpr int kXBytes = kXRes ? kPanelBytes : 0;
   __host__ __device__ static constexpr bool pairOk() {
     for (int l = 0; l < NL; ++l)
       if ((C::N(l) / NH) % 128 != 0) return false;
@@ -96,14 +99,18 @@ struct StreamLayout {
   static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * kHeadPad * 4 + 64 * 4) : 0;
   static constexpr int kEpiWarps = 8;
   static constexpr int kStageBytes = 32 * 64;  // per epilogue warp output staging (32 x 32 x 2 B)
-  // LayerNorm tails stage their output in the activation buffer (free once the last layer's MMAs
-  // are complete; two 2 KB buffers per warp in its own lane quarter of panels 0 and 1)
-  static constexpr bool kStgInAct = C::TAIL == kTailLayerNorm && actW() >= 2 * kPanel;
+  // Output staging inside the activation buffer, two 2 KB buffers per warp in its own lane
+  // quarter of two consecutive panels from kStgPanel0: for LayerNorm tails panels 0 and 1 (all of
+  // the last layer's MMAs are complete before its epilogue stages anything); otherwise the first
+  // panels the last layer does not read (its A operand is panels 0 .. K/64 - 1).
+  static constexpr int kStgPanel0 = C::TAIL == kTailLayerNorm ? 0 : (C::K(NL - 1) + kPanel - 1) / kPanel;
+  static constexpr bool kStgInAct = C::TAIL != kTailHead && (C::SKIP == 0 || C::SKIP != NL - 1) &&
+                                    actW() >= (kStgPanel0 + 2) * kPanel;
   static constexpr int kStgBytes = (C::TAIL == kTailHead || kStgInAct) ? 0 : kEpiWarps * kStageBytes;
   // cross-group exchange: LayerNorm (sum, sum of squares) or head partial sums, per row
   static constexpr int kXchgBytes =
       C::TAIL == kTailHead ? kBM * kHeadPad * 4 : (C::TAIL == kTailLayerNorm ? 2 * kBM * 8 : 0);
-  static constexpr int kBarBytes = 512;
+  static constexpr int kBarBytes = 256;  // 32 eight-byte slots (see the kernel)
   static constexpr int kFixed = kActBytes + kXBytes + kBiasBytes + kLnBytes + kHeadBytes +
                                 kXchgBytes + kStgBytes + kBarBytes + 1024;  // + alignment of the staging area
   // ring of x panels (streamed x only), then as many B stages as fit (at most 8). A stage holds
@@ -111,6 +118,7 @@ struct StreamLayout {
   // the columns) and arrives as ONE 3-D TMA request: TMA cost is largely per request, so 64-row
   // stages are used whenever three of them fit, 32-row stages otherwise.
   static constexpr int kXStages = kXRes ? 0 : 2;
+  static constexpr int kXSlots = kXRes ? 1 : kXStages;  // x buffers cycled by xs
   static constexpr int kRingBytes = kSmemLimit - kFixed - kXStages * kPanelBytes;
   static constexpr int kBK = kRingBytes / (64 * kNB * 2 / CG) >= 3 ? 64 : 32;  // weight rows per stage
   static constexpr int kSub = kPanel / kBK;                                     // stages per K panel
@@ -296,7 +304,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
         if constexpr (L::kXRes) {
           if (!mbar_wait<kPair>(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
           if (args.inject != 1) load_x(0, row_base);
-          if (++xs == 2) { xs = 0; xph ^= 1; }
+          if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
         }
 #pragma unroll 1
         for (int l = 0; ok && l < NL; ++l) {
@@ -306,7 +314,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
             for (int p = 0; ok && p < panels; ++p) {
               if (!mbar_wait<kPair>(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) { ok = false; break; }
               if (args.inject != 1) load_x(p, row_base);
-              if (++xs == 2) { xs = 0; xph ^= 1; }
+              if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
               for (int hf = 0; ok && hf < NH; ++hf)
                 for (int kh = 0; ok && kh < L::kSub; ++kh) ok = stage(l, p, hf, kh);
             }
@@ -412,7 +420,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               if (a == 0u) { ok = false; break; }
               ok = issue(a, p, 0) && (NH == 1 || issue(a, p, 1));
               commit_any(&x_empty[xs]);
-              if (++xs == 2) { xs = 0; xph ^= 1; }
+              if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
             }
             if (!ok) break;
             commit_any(&acc_full[0]);
@@ -438,7 +446,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
           }
         }
         if constexpr (L::kXRes) {
-          if (++xs == 2) { xs = 0; xph ^= 1; }
+          if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
         }
       }
       // drain: every issued MMA has completed before TMEM can be released
@@ -457,9 +465,9 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
     const int r = q * 32 + lane;      // row within the tile
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     uint8_t* act = smem + L::kOffAct;
-    // output staging: two buffers per warp inside the activation buffer (LayerNorm tails) or one
-    // dedicated buffer per warp
-    uint8_t* stg = L::kStgInAct ? act + q * 4096 + eg * 2048
+    // output staging: two buffers per warp inside the activation buffer (panels the last layer
+    // no longer reads), or one dedicated buffer per warp
+    uint8_t* stg = L::kStgInAct ? act + L::kStgPanel0 * kPanelBytes + q * 4096 + eg * 2048
                                 : smem + L::kOffStg + (warp - 2) * L::kStageBytes;
     float* xchg = reinterpret_cast<float*>(smem + L::kOffXchg);
     int sb = 0;
