@@ -120,8 +120,14 @@ struct StreamLayout {
   static constexpr int kXStages = kXRes ? 0 : 2;
   static constexpr int kXSlots = kXRes ? 1 : kXStages;  // x buffers cycled by xs
   static constexpr int kRingBytes = kSmemLimit - kFixed - kXStages * kPanelBytes;
-  static constexpr int kBK = kRingBytes / (64 * kNB * 2 / CG) >= 3 ? 64 : 32;  // weight rows per stage
-  static constexpr int kSub = kPanel / kBK;                                     // stages per K panel
+  // Stage rows: 128 (two K panels per request; only where x is resident, since a streamed x
+  // panel is consumed with its own weight rows), else 64, else 32 -- the largest of which three
+  // stages fit. The weight ring delivers about one stage per fixed interval whatever its size,
+  // so larger stages carry more bytes per interval.
+  static constexpr int kBK = (kXRes && kRingBytes / (128 * kNB * 2 / CG) >= 3) ? 128
+                             : kRingBytes / (64 * kNB * 2 / CG) >= 3 ? 64 : 32;
+  static constexpr int kSub = kBK >= kPanel ? 1 : kPanel / kBK;  // stages per K panel (kBK <= 64)
+  static_assert(C::SKIP == 0 || kXRes, "skip concat reads a resident x panel");
   static constexpr int kBStageBytes = kBK * kNB * 2 / CG;
   static constexpr int kBStagesRaw = (kSmemLimit - kFixed - kXStages * kPanelBytes) / kBStageBytes;
   static constexpr int kBStages = kBStagesRaw > 8 ? 8 : kBStagesRaw;
@@ -269,8 +275,9 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
       int bs = 0, xs = 0;
       uint32_t bph = 0, xph = 0;
       bool ok = true;
-      auto stage = [&](int l, int p, int hf, int kh) -> bool {
-        if (ksteps_in<C, L::kBK>(l, p, kh) == 0) return true;
+      // weight rows [row, row + kBK) of output half hf of layer l into the next ring slot
+      auto stage = [&](int l, int row, int hf) -> bool {
+        if (row >= C::K(l)) return true;
         if (!mbar_wait<kPair>(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) return false;
         const int hw = C::N(l) / NH;
         const int hwc = hw / CG;  // columns staged by this CTA
@@ -279,7 +286,6 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
         const uint32_t fb = leader_bar(&b_full[bs]);
         // one request: kBK rows x (hwc / 64) column blocks, block after block in shared memory
         const int blk = (hf * hw + static_cast<int>(rank) * hwc) / 64;
-        const int row = p * kPanel + kh * L::kBK;
         if constexpr (kPair) {
           tma_load_3d_pair(dst, &tm.w[l], fb, 0, row, blk, keep);
         } else {
@@ -316,14 +322,13 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               if (args.inject != 1) load_x(p, row_base);
               if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
               for (int hf = 0; ok && hf < NH; ++hf)
-                for (int kh = 0; ok && kh < L::kSub; ++kh) ok = stage(l, p, hf, kh);
+                for (int kh = 0; ok && kh < L::kSub; ++kh) ok = stage(l, p * kPanel + kh * L::kBK, hf);
             }
           } else {
 #pragma unroll 1
             for (int hf = 0; ok && hf < NH; ++hf)
 #pragma unroll 1
-              for (int p = 0; ok && p < panels; ++p)
-                for (int kh = 0; ok && kh < L::kSub; ++kh) ok = stage(l, p, hf, kh);
+              for (int row = 0; ok && row < C::K(l); row += L::kBK) ok = stage(l, row, hf);
           }
         }
       }
@@ -385,6 +390,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               return x_sm + xs * kPanelBytes;
             }
           };
+          // the weight stages of K panel p (stages of at most one panel)
           auto issue = [&](uint32_t a_base, int p, int hf) -> bool {
             for (int kh = 0; kh < L::kSub; ++kh) {
               const int ks = ksteps_in<C, L::kBK>(l, p, kh);
@@ -429,12 +435,50 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
 #pragma unroll 1
             for (int hf = 0; ok && hf < NH; ++hf) {
               if (hf == 1 && !need(1)) { ok = false; break; }
+              if constexpr (L::kBK < kPanel) {
+                // 32-row stages: per K panel (measured faster here than the stage loop below)
 #pragma unroll 1
-              for (int p = 0; ok && p < panels; ++p) {
-                if (p >= hi_p && !need(1)) { ok = false; break; }
-                const uint32_t a = a_panel(p);
-                if (a == 0u) { ok = false; break; }
-                ok = issue(a, p, hf);
+                for (int p = 0; ok && p < panels; ++p) {
+                  if (p >= hi_p && !need(1)) { ok = false; break; }
+                  const uint32_t a = a_panel(p);
+                  if (a == 0u) { ok = false; break; }
+                  ok = issue(a, p, hf);
+                }
+                if (ok) commit_any(&acc_full[hf]);
+                continue;
+              }
+              // stages of kBK weight rows (one or two K panels); each K step takes its A operand
+              // from the shared-memory activation panels or the resident x panel (layer 0, and the
+              // skip concat's last panel)
+              // descriptors advance by address >> 4: +2 per 32-byte K step inside a panel, +1024
+              // per 16 KB panel, +128 per 2 KB (16-row) step of a B stage
+              const uint64_t act_desc = make_sdesc_sw128(act_sm, 16, 1024);
+              const uint64_t x_desc = make_sdesc_sw128(x_sm + xcur * kPanelBytes, 16, 1024);
+#pragma unroll 1
+              for (int r0 = 0; ok && r0 < C::K(l); r0 += L::kBK) {
+                const int ks = (C::K(l) - r0) / 16 < L::kBK / 16 ? (C::K(l) - r0) / 16 : L::kBK / 16;
+                if ((r0 + ks * 16 - 1) / kPanel >= hi_p && !need(1)) { ok = false; break; }
+                if (!mbar_wait<kPair>(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
+                tc_fence_after();
+                const uint64_t bdesc0 = make_sdesc_sw128(b_sm + bs * L::kBStageBytes, L::kBK * 128, 1024);
+                const uint32_t d_tmem = tmem_base + hf * hw;
+                const int kg0 = r0 >> 4;
+                for (int k = 0; k < ks; ++k) {
+                  const int kg = kg0 + k;  // 16-wide K step within the layer
+                  const int p = kg >> 2;
+                  const uint64_t bdesc = bdesc0 + static_cast<uint64_t>(k * 128);
+                  const uint32_t acc = (r0 | k) != 0 ? 1u : 0u;
+                  const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1);
+                  const uint64_t adesc = from_x ? x_desc + static_cast<uint64_t>((kg & 3) * 2)
+                                                : act_desc + static_cast<uint64_t>(kg * 2 + p * (1024 - 8));
+                  if constexpr (kPair) {
+                    mma_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
+                  } else {
+                    mma_ss(d_tmem, adesc, bdesc, idesc, acc);
+                  }
+                }
+                commit_any(&b_empty[bs]);
+                if (++bs == kBS) { bs = 0; bph ^= 1; }
               }
               if (ok) commit_any(&acc_full[hf]);
             }
