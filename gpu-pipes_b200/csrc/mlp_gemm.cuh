@@ -366,6 +366,27 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   if (row >= m) return;
   constexpr int kPer = N / 128;  // float4 per lane
+  // gamma / beta as four 16-bit values per load (when both are 8-byte aligned; the interface
+  // only requires 4), issued first so their latency overlaps the row's
+  const bool vec = ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 7u) == 0;
+  uint2 gv[kPer], bv[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int col = (i * 32 + lane) * 4;
+    if (vec) {
+      gv[i] = gamma != nullptr ? __ldg(reinterpret_cast<const uint2*>(gamma) + i * 32 + lane) : make_uint2(0, 0);
+      bv[i] = beta != nullptr ? __ldg(reinterpret_cast<const uint2*>(beta) + i * 32 + lane) : make_uint2(0, 0);
+    } else {
+      const uint16_t* g16 = static_cast<const uint16_t*>(gamma);
+      const uint16_t* b16 = static_cast<const uint16_t*>(beta);
+      gv[i] = gamma != nullptr ? make_uint2(__ldg(g16 + col) | (uint32_t(__ldg(g16 + col + 1)) << 16),
+                                            __ldg(g16 + col + 2) | (uint32_t(__ldg(g16 + col + 3)) << 16))
+                               : make_uint2(0, 0);
+      bv[i] = beta != nullptr ? make_uint2(__ldg(b16 + col) | (uint32_t(__ldg(b16 + col + 1)) << 16),
+                                           __ldg(b16 + col + 2) | (uint32_t(__ldg(b16 + col + 3)) << 16))
+                              : make_uint2(0, 0);
+    }
+  }
   float4 v[kPer];
   const float4* src = reinterpret_cast<const float4*>(y + row * N);
   float s = 0.f;
@@ -389,14 +410,23 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int col = (i * 32 + lane) * 4;
-    float o4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    const float o4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    const uint32_t gw[2] = {gv[i].x, gv[i].y}, bw[2] = {bv[i].x, bv[i].y};
     uint32_t pk[2];
 #pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      float a = (o4[e] - mean) * rstd, b = (o4[e + 1] - mean) * rstd;
-      if (gamma != nullptr) { a *= load16(gamma, col + e, g_bf16); b *= load16(gamma, col + e + 1, g_bf16); }
-      if (beta != nullptr) { a += load16(beta, col + e, g_bf16); b += load16(beta, col + e + 1, g_bf16); }
-      pk[e / 2] = out_bf16 ? Elem<__nv_bfloat16>::pack(a, b) : Elem<__half>::pack(a, b);
+    for (int e = 0; e < 2; ++e) {
+      float a = (o4[2 * e] - mean) * rstd, b = (o4[2 * e + 1] - mean) * rstd;
+      if (gamma != nullptr) {
+        const float2 g = unpack16x2(gw[e], g_bf16);
+        a *= g.x;
+        b *= g.y;
+      }
+      if (beta != nullptr) {
+        const float2 bb = unpack16x2(bw[e], g_bf16);
+        a += bb.x;
+        b += bb.y;
+      }
+      pk[e] = out_bf16 ? Elem<__nv_bfloat16>::pack(a, b) : Elem<__half>::pack(a, b);
     }
     *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + row * N + col) = make_uint2(pk[0], pk[1]);
   }

@@ -70,3 +70,22 @@ def test_named_entry_points(cuda_dev):
     out = cuda_ext.dlrm_topmlp(x.to(cuda_dev), *d)
     torch.cuda.synchronize()
     assert O.compare(out.float().cpu(), O.workload_forward(w, x, layers, None))["ok"]
+
+
+def test_bert_ffn_gamma_beta_4_byte_aligned(cuda_dev):
+    """gamma/beta need only 4-byte alignment: a copy at a 4-byte (not 8-byte) offset takes the
+    LayerNorm kernel's scalar path and must give the same bits as the aligned one."""
+    w = W.BERT_FFN.with_m(513)
+    x, layers, ln, out = _run(w, cuda_dev)
+    g, b = (t.to(cuda_dev) for t in ln)
+    buf = torch.zeros(2 * (w.n_out + 4), dtype=g.dtype, device=cuda_dev)
+    g_off = buf[2:2 + w.n_out]  # 4-byte offset from a 256-byte aligned base
+    b_off = buf[w.n_out + 6:w.n_out + 6 + w.n_out]
+    assert g_off.data_ptr() % 8 == 4 and b_off.data_ptr() % 8 == 4
+    g_off.copy_(g)
+    b_off.copy_(b)
+    out2 = torch.empty_like(out)
+    cuda_ext.run_workload_out(w, x.to(cuda_dev), [(a.to(cuda_dev), bb.to(cuda_dev)) for a, bb in layers],
+                              (g_off, b_off), out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
