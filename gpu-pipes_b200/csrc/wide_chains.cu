@@ -157,45 +157,53 @@ int launch_bert_ffn_bf16(const LaunchCtx& c) {
 }
 
 // DLRM top MLP (fp16): three wide layers on mlp_gemm_kernel, then 512 -> 256 -> 1 on the
-// streaming chain kernel.
+// streaming chain kernel. The tail runs once per two row chunks (h3 holds both), so each of its
+// launches has two 128-row tiles per SM to pipeline instead of one.
 int launch_dlrm_top_f16(const LaunchCtx& c) {
-  constexpr int64_t kChunk = 16384;  // h1 + h2 + h3 = 80 MB
+  constexpr int64_t kChunk = 16384;  // h1 + h2 + 2 x h3 = 96 MB
   const int64_t chunk = c.m < kChunk ? c.m : kChunk;
   const size_t h1_bytes = align256(size_t(chunk) * 1024 * 2);
-  const size_t h3_bytes = align256(size_t(chunk) * 512 * 2);
+  const size_t h3_bytes = align256(size_t(2 * chunk) * 512 * 2);
   void* ws = nullptr;
   int rc = workspace_acquire(2 * h1_bytes + h3_bytes, c.stream, &ws);
   if (rc != GP_OK) return rc;
   char* base = static_cast<char*>(ws);
   void* h1 = base;
   void* h2 = base + h1_bytes;
-  void* h3 = base + 2 * h1_bytes;
+  char* h3 = base + 2 * h1_bytes;
   int* st = c.args.status;
   const int k0 = c.spec->widths[0];
-  for (int64_t r0 = 0; rc == GP_OK && r0 < c.m; r0 += chunk) {
-    const int64_t rows = (c.m - r0) < chunk ? (c.m - r0) : chunk;
-    const void* xr = static_cast<const char*>(c.x) + r0 * k0 * 2;
-    rc = gemm_launch(c.stream, c.sm_count, xr, 0, rows, k0, c.w[0], 1024, c.args.bias[0], 0, nullptr,
-                     0, kActRelu, h1, 1, st, c.args.timeout_ns);
-    if (rc == GP_OK)
-      rc = gemm_launch(c.stream, c.sm_count, h1, 0, rows, 1024, c.w[1], 1024, c.args.bias[1], 0,
-                       nullptr, 0, kActRelu, h2, 1, st, c.args.timeout_ns);
-    if (rc == GP_OK)
-      rc = gemm_launch(c.stream, c.sm_count, h2, 0, rows, 1024, c.w[2], 512, c.args.bias[2], 0,
-                       nullptr, 0, kActRelu, h3, 1, st, c.args.timeout_ns);
+  for (int64_t r0 = 0; rc == GP_OK && r0 < c.m; r0 += 2 * chunk) {
+    int64_t tail_rows = 0;
+    for (int sub = 0; rc == GP_OK && sub < 2; ++sub) {
+      const int64_t s0 = r0 + sub * chunk;
+      if (s0 >= c.m) break;
+      const int64_t rows = (c.m - s0) < chunk ? (c.m - s0) : chunk;
+      const void* xr = static_cast<const char*>(c.x) + s0 * k0 * 2;
+      void* h3s = h3 + tail_rows * 512 * 2;
+      rc = gemm_launch(c.stream, c.sm_count, xr, 0, rows, k0, c.w[0], 1024, c.args.bias[0], 0, nullptr,
+                       0, kActRelu, h1, 1, st, c.args.timeout_ns);
+      if (rc == GP_OK)
+        rc = gemm_launch(c.stream, c.sm_count, h1, 0, rows, 1024, c.w[1], 1024, c.args.bias[1], 0,
+                         nullptr, 0, kActRelu, h2, 1, st, c.args.timeout_ns);
+      if (rc == GP_OK)
+        rc = gemm_launch(c.stream, c.sm_count, h2, 0, rows, 1024, c.w[2], 512, c.args.bias[2], 0,
+                         nullptr, 0, kActRelu, h3s, 1, st, c.args.timeout_ns);
+      tail_rows += rows;
+    }
     if (rc == GP_OK) {
       gp_mlp_spec tail_spec = *c.spec;
       LaunchCtx t = c;
       t.spec = &tail_spec;
-      t.m = rows;
+      t.m = tail_rows;
       t.x = h3;
       t.out = static_cast<char*>(c.out) + r0 * 2;
       t.w[0] = c.w[3];
       t.w[1] = c.w[4];
       t.args.bias[0] = c.args.bias[3];
       t.args.bias[1] = c.args.bias[4];
-      t.args.m = rows;
-      t.args.num_tiles = static_cast<int>((rows + kBM - 1) / kBM);
+      t.args.m = tail_rows;
+      t.args.num_tiles = static_cast<int>((tail_rows + kBM - 1) / kBM);
       t.args.out = t.out;
       rc = launch_stream<ChainDlrmTail>(t);
     }
