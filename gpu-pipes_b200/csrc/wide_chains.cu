@@ -160,7 +160,9 @@ int launch_bert_ffn_bf16(const LaunchCtx& c) {
 // streaming chain kernel. The tail runs once per two row chunks (h3 holds both), so each of its
 // launches has two 128-row tiles per SM to pipeline instead of one.
 int launch_dlrm_top_f16(const LaunchCtx& c) {
-  constexpr int64_t kChunk = 16384;  // h1 + h2 + 2 x h3 = 96 MB
+  // 18,944 rows = 74 pair tiles of 256 rows: the 1024-wide layers run exactly 4 waves of 74
+  // clusters and the 512-wide one exactly 2. h1 + h2 + 2 x h3 = 116 MB (L2: 126 MB).
+  constexpr int64_t kChunk = 18944;
   const int64_t chunk = c.m < kChunk ? c.m : kChunk;
   const size_t h1_bytes = align256(size_t(chunk) * 1024 * 2);
   const size_t h3_bytes = align256(size_t(2 * chunk) * 512 * 2);
