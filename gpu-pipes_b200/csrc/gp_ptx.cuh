@@ -12,6 +12,7 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
@@ -506,21 +507,47 @@ struct Elem<__nv_bfloat16> {
 // ------------------------------------------------------------------------------------------------
 enum Act : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActSilu = 3, kActSigmoid = 4 };
 
+// GELU, tanh form 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))) (Hendrycks & Gimpel), with the
+// hardware tanh approximation (tanh.approx.f32, max relative error about 2^-11, below the 16-bit
+// rounding of the stored activation).
+__device__ __forceinline__ float gelu_tanh_fast(float v) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * v * (1.0f + t);
+}
+
+// Activation chosen at compile time. SiLU v / (1 + e^-v) and the logistic sigmoid use the fast
+// exponential and division intrinsics; both tend to the right limits (x / inf = 0).
+template <int ACT>
+__device__ __forceinline__ float act_t(float v) {
+  if constexpr (ACT == kActRelu) return fmaxf(v, 0.0f);
+  else if constexpr (ACT == kActGeluTanh) return gelu_tanh_fast(v);
+  else if constexpr (ACT == kActSilu) return __fdividef(v, 1.0f + __expf(-v));
+  else if constexpr (ACT == kActSigmoid) return __fdividef(1.0f, 1.0f + __expf(-v));
+  else return v;
+}
+
 __device__ __forceinline__ float apply_act(int act, float v) {
   switch (act) {
-    case kActRelu:
-      return fmaxf(v, 0.0f);
-    case kActGeluTanh: {
-      // 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))  -- GELU, tanh form (Hendrycks & Gimpel)
-      const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-      return 0.5f * v * (1.0f + tanhf(u));
-    }
-    case kActSilu:
-      return v / (1.0f + __expf(-v));
-    case kActSigmoid:
-      return 1.0f / (1.0f + __expf(-v));
-    default:
-      return v;
+    case kActRelu: return act_t<kActRelu>(v);
+    case kActGeluTanh: return act_t<kActGeluTanh>(v);
+    case kActSilu: return act_t<kActSilu>(v);
+    case kActSigmoid: return act_t<kActSigmoid>(v);
+    default: return v;
+  }
+}
+
+// Calls f(std::integral_constant<int, A>{}) for the runtime activation id `act`, so per-element
+// code is specialised once per call site instead of switching per element.
+template <class F>
+__device__ __forceinline__ void act_dispatch(int act, F&& f) {
+  switch (act) {
+    case kActRelu: f(std::integral_constant<int, kActRelu>{}); break;
+    case kActGeluTanh: f(std::integral_constant<int, kActGeluTanh>{}); break;
+    case kActSilu: f(std::integral_constant<int, kActSilu>{}); break;
+    case kActSigmoid: f(std::integral_constant<int, kActSigmoid>{}); break;
+    default: f(std::integral_constant<int, kActNone>{}); break;
   }
 }
 

@@ -74,23 +74,8 @@ __device__ __forceinline__ float load16(const void* p, int64_t i, int is_bf16) {
   return __half2float(__ushort_as_half(bits));
 }
 
-// GELU, tanh form 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))) (Hendrycks & Gimpel), with the
-// hardware tanh approximation (tanh.approx.f32, max relative error about 2^-11, below the 16-bit
-// rounding of the stored activation).
-__device__ __forceinline__ float gelu_tanh_fast(float v) {
-  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
-  return 0.5f * v * (1.0f + t);
-}
-
 template <int ACT>
-__device__ __forceinline__ float gemm_act(float v) {
-  if constexpr (ACT == kActRelu) return fmaxf(v, 0.0f);
-  else if constexpr (ACT == kActGeluTanh) return gelu_tanh_fast(v);
-  else if constexpr (ACT == kActNone) return v;
-  else return apply_act(ACT, v);
-}
+__device__ __forceinline__ float gemm_act(float v) { return act_t<ACT>(v); }
 
 __device__ __forceinline__ float2 unpack16x2(uint32_t w, int is_bf16) {
   if (is_bf16) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));

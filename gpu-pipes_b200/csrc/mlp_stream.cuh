@@ -579,21 +579,24 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               tmem_ld32(t_lane + c * 32, v);
               tmem_wait_ld();
               uint8_t* line = act + (c >> 1) * kPanelBytes + r * 128;
+              act_dispatch(act_id, [&](auto actc) {
+                constexpr int A = decltype(actc)::value;
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint32_t pk[4];
+                for (int j = 0; j < 4; ++j) {
+                  uint32_t pk[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int i = j * 8 + e * 2;
-                  const float2 bb = *reinterpret_cast<const float2*>(bl + c * 32 + i);
-                  const float y0 = apply_act(act_id, __uint_as_float(v[i]) + bb.x);
-                  const float y1 = apply_act(act_id, __uint_as_float(v[i + 1]) + bb.y);
-                  pk[e] = C::HIDDEN_F16 ? Elem<__half>::pack(y0, y1) : Elem<T>::pack(y0, y1);
+                  for (int e = 0; e < 4; ++e) {
+                    const int i = j * 8 + e * 2;
+                    const float2 bb = *reinterpret_cast<const float2*>(bl + c * 32 + i);
+                    const float y0 = act_t<A>(__uint_as_float(v[i]) + bb.x);
+                    const float y1 = act_t<A>(__uint_as_float(v[i + 1]) + bb.y);
+                    pk[e] = C::HIDDEN_F16 ? Elem<__half>::pack(y0, y1) : Elem<T>::pack(y0, y1);
+                  }
+                  const int chunk = (c & 1) * 4 + j;
+                  *reinterpret_cast<uint4*>(line + ((chunk ^ (r & 7)) * 16)) =
+                      make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
-                const int chunk = (c & 1) * 4 + j;
-                *reinterpret_cast<uint4*>(line + ((chunk ^ (r & 7)) * 16)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
-              }
+              });
             }
             fence_proxy_async_smem();
             release(hf);
@@ -613,20 +616,23 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               uint32_t v[32];
               tmem_ld32(t_lane + c * 32, v);
               tmem_wait_ld();
+              act_dispatch(act_id, [&](auto actc) {
+                constexpr int A = decltype(actc)::value;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int k = c * 32 + i;
-                const float y = apply_act(act_id, __uint_as_float(v[i]) + bl[k]);
-                const float4* w4 = reinterpret_cast<const float4*>(head_w + k * HP);
+                for (int i = 0; i < 32; ++i) {
+                  const int k = c * 32 + i;
+                  const float y = act_t<A>(__uint_as_float(v[i]) + bl[k]);
+                  const float4* w4 = reinterpret_cast<const float4*>(head_w + k * HP);
 #pragma unroll
-                for (int o4 = 0; o4 < HP / 4; ++o4) {
-                  const float4 w = w4[o4];
-                  o[o4 * 4 + 0] = fmaf(y, w.x, o[o4 * 4 + 0]);
-                  o[o4 * 4 + 1] = fmaf(y, w.y, o[o4 * 4 + 1]);
-                  o[o4 * 4 + 2] = fmaf(y, w.z, o[o4 * 4 + 2]);
-                  o[o4 * 4 + 3] = fmaf(y, w.w, o[o4 * 4 + 3]);
+                  for (int o4 = 0; o4 < HP / 4; ++o4) {
+                    const float4 w = w4[o4];
+                    o[o4 * 4 + 0] = fmaf(y, w.x, o[o4 * 4 + 0]);
+                    o[o4 * 4 + 1] = fmaf(y, w.y, o[o4 * 4 + 1]);
+                    o[o4 * 4 + 2] = fmaf(y, w.z, o[o4 * 4 + 2]);
+                    o[o4 * 4 + 3] = fmaf(y, w.w, o[o4 * 4 + 3]);
+                  }
                 }
-              }
+              });
             }
             release(hf);
           }
@@ -651,7 +657,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               T* dst = reinterpret_cast<T*>(args.out) + row * C::HEAD_N;
 #pragma unroll
               for (int i = 0; i < C::HEAD_N; ++i) {
-                const float y = apply_act(C::HEAD_ACT, o[i] + head_b[i]);
+                const float y = act_t<C::HEAD_ACT>(o[i] + head_b[i]);
                 if constexpr (Elem<T>::kIsBf16) dst[i] = __float2bfloat16_rn(y); else dst[i] = __float2half_rn(y);
               }
             }
@@ -697,19 +703,22 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               tmem_wait_ld();
               if (c + 2 >= (hf + 1) * hc) release(hf);  // this warp's part of the half is read
               uint32_t pk[16];
+              act_dispatch(C::TAIL == kTailLayerNorm ? int(kActNone) : act_id, [&](auto actc) {
+                constexpr int A = decltype(actc)::value;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                float y0 = __uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i];
-                float y1 = __uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1];
-                if constexpr (C::TAIL == kTailLayerNorm) {
-                  y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
-                  y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
-                } else {
-                  y0 = apply_act(act_id, y0);
-                  y1 = apply_act(act_id, y1);
+                for (int i = 0; i < 16; ++i) {
+                  float y0 = __uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i];
+                  float y1 = __uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1];
+                  if constexpr (C::TAIL == kTailLayerNorm) {
+                    y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
+                    y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
+                  } else {
+                    y0 = act_t<A>(y0);
+                    y1 = act_t<A>(y1);
+                  }
+                  pk[i] = Elem<T>::pack(y0, y1);
                 }
-                pk[i] = Elem<T>::pack(y0, y1);
-              }
+              });
               store_chunk(c, row0, pk);
             }
           }
