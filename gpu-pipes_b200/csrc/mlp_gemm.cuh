@@ -8,9 +8,9 @@
 // (apps/bert_ffn/pipelined/bert_ffn_pl.cuh:132-162, apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl.cuh:
 // 185-224). Here each layer is one persistent launch over 256 x 256 output tiles, one per CTA
 // pair (cta_group::2: the leader issues 256-row MMAs over both CTAs' operands; each CTA loads its
-// own 128 A rows and half of the B columns), and the host runs a chain over row chunks sized so
-// that every intermediate stays within L2: the hand-off between layers goes through L2, as in the
-// reference, rather than HBM.
+// own 128 A rows and half of the B columns), and the host runs a chain over large row chunks
+// whose intermediates sit in a device workspace (their HBM traffic overlaps the GEMMs; fewer,
+// larger launches lose less to partial last waves than L2-sized chunks did).
 //
 //   warp 0     TMA producer: per 64-wide K step one A panel (128 x 64, K-major SW128) and one
 //              B stage (64 x 128 per CTA, N-major SW128, one 3-D request) into an mbarrier ring
