@@ -141,7 +141,7 @@ def cpu_oracle_rate(w, seconds: float) -> dict:
     rows, t0 = 0, time.perf_counter()
     while True:
         O.workload_forward(w, x, layers, ln)
-        rows += x.shape[0]
+        rows += W.rows_of(w, x)
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
@@ -337,7 +337,7 @@ def main():
                        "l2": ("L2 flushed (256 MB write) between timed steps: x %d MB + out %d MB "
                               "per GPU < 2 x 126 MB" if flush else
                               "inputs larger than L2 (x %d MB + out %d MB per GPU)") % (
-                           w.m * w.k0 * 2 >> 20, w.m * w.n_out * 2 >> 20),
+                           w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20),
                        "parallelism": f"rows sharded over {world} GPU(s), weights replicated"},
             "tflops": value * w.flop_per_row / 1e12,
             "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit,

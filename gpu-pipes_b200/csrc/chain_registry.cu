@@ -23,6 +23,8 @@ GP_DECLARE(launch_mgn_ln_bf16_k384_pair)
 GP_DECLARE(launch_mgn_ln_bf16_k256_single)
 GP_DECLARE(launch_mgn_ln_bf16_k128_single)
 GP_DECLARE(launch_dlrm_bot_f16)
+GP_DECLARE(launch_addln0_f16_h128)
+GP_DECLARE(launch_ffn_resln_f16_h128)
 GP_DECLARE(launch_gc_silu_bf16_k1536)
 GP_DECLARE(launch_gc_relu_f16_k1536)
 GP_DECLARE(launch_gc_relu_bf16_k1536)
@@ -71,7 +73,11 @@ static const ChainEntry kChains[] = {
      GP_TAIL_NONE, launch_nerf_f16, 0, 5},
     {"nerf_trunk_f16", GP_F16, 8, {64, 256, 256, 256, 256, 256, 256, 256, 256}, {R, R, R, R, R, R, R, R},
      GP_TAIL_NONE, launch_nerf_trunk_f16, 0, 5},
-    // chains with activations too wide for one SM: per-layer GEMMs through L2-sized chunks
+    // BERT attention-output block at the reference's widths (apps/bert_addln_ffn): 128 -> 128 with
+    // residual + LN0, then 128 -> 512 ReLU -> 128 with residual + LN2
+    {"addln0_f16_h128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_RESIDUAL_LN, launch_addln0_f16_h128, 0},
+    {"ffn_resln_f16_h128", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128, 0},
+    // chains with activations too wide for one SM: per-layer GEMMs over large row chunks
     {"bert_ffn_bf16", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
      launch_bert_ffn_bf16, 0},
     {"dlrm_top_f16", GP_F16, 5, {480, 1024, 1024, 512, 256, 1}, {R, R, R, R, GP_ACT_SIGMOID},

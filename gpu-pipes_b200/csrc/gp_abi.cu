@@ -277,9 +277,10 @@ int finish_launch(cudaStream_t stream, int dev_status_check) {
   return GP_OK;
 }
 
+// resid: residual rows of a GP_TAIL_RESIDUAL_LN chain ([m, N_last]); null means x itself.
 int fused_mlp(const gp_mlp_spec* spec, int64_t m, const void* x, const void* const* w,
               const void* const* b, const void* gamma, const void* beta, void* out,
-              cudaStream_t stream) {
+              cudaStream_t stream, const void* resid = nullptr) {
   clear_error();
   int rc = validate(spec, m, x, w, b, gamma, beta, out);
   if (rc != GP_OK) return rc;
@@ -310,7 +311,7 @@ int fused_mlp(const gp_mlp_spec* spec, int64_t m, const void* x, const void* con
   }
   c.args.gamma = gamma;
   c.args.beta = beta;
-  c.args.resid = x;
+  c.args.resid = resid != nullptr ? resid : x;
   c.args.out = out;
   c.args.ln_eps = spec->ln_eps;
   c.args.status = st->status;
@@ -441,6 +442,50 @@ int gp_dlrm_topmlp_out(int64_t m, const void* x, const void* const* w, const voi
   s.tail = GP_TAIL_NONE;
   s.dtype = GP_F16;
   return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+// BERT attention-output block, apps/bert_addln_ffn/pipelined/bert_addln_ffn_pl_ext.cu:15-58
+// (H = 128, ff = 512, fp16): h = LN0(attn_out W0 + b0 + x), out = LN2(ReLU(h W1 + b1) W2 + b2 + h).
+// Two fused chain launches; h ([m, 128] fp16) lives in the per-device workspace between them.
+int gp_bert_addln_ffn_out(int64_t m, const void* attn_out, const void* x, const void* w0,
+                          const void* b0, const void* w1, const void* b1, const void* w2,
+                          const void* b2, const void* ga0, const void* be0, const void* ga2,
+                          const void* be2, void* out, void* stream) {
+  clear_error();
+  if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
+  if (attn_out == nullptr || x == nullptr || out == nullptr || w0 == nullptr || w1 == nullptr ||
+      w2 == nullptr)
+    return set_error(GP_ERR_ARG, "attn_out, x, w0, w1, w2 and out must not be NULL");
+  if (!aligned(x, 16)) return set_error(GP_ERR_ALIGN, "x must be 16-byte aligned");
+  if (m == 0) return GP_OK;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  gp_mlp_spec sa{};
+  sa.n_layers = 1;
+  sa.widths[0] = 128;
+  sa.widths[1] = 128;
+  sa.act[0] = GP_ACT_NONE;
+  sa.tail = GP_TAIL_RESIDUAL_LN;
+  sa.dtype = GP_F16;
+  sa.ln_eps = 1e-5f;
+  gp_mlp_spec sb = sa;
+  sb.n_layers = 2;
+  sb.widths[1] = 512;
+  sb.widths[2] = 128;
+  sb.act[0] = GP_ACT_RELU;
+  sb.act[1] = GP_ACT_NONE;
+  void* h = nullptr;
+  int rc = workspace_acquire(static_cast<size_t>(m) * 128 * 2, s, &h);
+  if (rc != GP_OK) return rc;
+  const void* wa[1] = {w0};
+  const void* ba[1] = {b0};
+  rc = fused_mlp(&sa, m, attn_out, wa, ba, ga0, be0, h, s, x);
+  if (rc == GP_OK) {
+    const void* wb[2] = {w1, w2};
+    const void* bb[2] = {b1, b2};
+    rc = fused_mlp(&sb, m, h, wb, bb, ga2, be2, out, s);
+  }
+  workspace_release(s);
+  return rc;
 }
 
 static gp_mlp_spec nerf_spec(bool head) {

@@ -48,6 +48,34 @@ struct ChainNerfTrunk : ChainNerf {
   static constexpr int TAIL = kTailNone, HEAD_N = 0;
 };
 
+// BERT attention-output block (apps/bert_addln_ffn/torch/model.py:4-19, H = 128, ff = 512):
+//   stage 1: h = LN0(attn_out W0 + b0 + x)        -- one 128-wide layer, residual x
+//   stage 2: y = LN2(ReLU(h W1 + b1) W2 + b2 + h)  -- 128 -> 512 -> 128, residual h
+struct ChainAddLn0 {
+  using T = __half;
+  static constexpr int NL = 1;
+  __host__ __device__ static constexpr int K(int) { return 128; }
+  __host__ __device__ static constexpr int N(int) { return 128; }
+  __host__ __device__ static constexpr int ACT(int) { return kActNone; }
+  static constexpr int SKIP = 0, TAIL = kTailResidualLN, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 1;
+};
+
+struct ChainFfnResLn {
+  using T = __half;
+  static constexpr int NL = 2;
+  __host__ __device__ static constexpr int K(int l) { return l == 0 ? 128 : 512; }
+  __host__ __device__ static constexpr int N(int l) { return l == 0 ? 512 : 128; }
+  __host__ __device__ static constexpr int ACT(int l) { return l == 0 ? kActRelu : kActNone; }
+  static constexpr int SKIP = 0, TAIL = kTailResidualLN, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 2;
+};
+
+int launch_addln0_f16_h128(const LaunchCtx& c) { return launch_stream<ChainAddLn0>(c); }
+int launch_ffn_resln_f16_h128(const LaunchCtx& c) { return launch_stream<ChainFfnResLn>(c); }
+
 int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot>(c); }
 int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>, 2>(c); }
 int launch_gc_relu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActRelu>, 2>(c); }

@@ -41,7 +41,8 @@ constexpr int kTailHead = 3;  // narrow output layer on CUDA cores (stream kerne
 // and drained as two column halves so the epilogue of one overlaps the MMAs of the other;
 // 1 = one pass per layer):
 //   using T;  NL (tensor-core layers); K(l), N(l), ACT(l); SKIP (layer whose A operand is
-//   [act || x], 0 = none); TAIL (kTailNone / kTailLayerNorm / kTailHead); HEAD_N, HEAD_ACT;
+//   [act || x], 0 = none); TAIL (kTailNone / kTailLayerNorm / kTailResidualLN / kTailHead; the
+//   residual rows [M, N_last] of kTailResidualLN come from args.resid); HEAD_N, HEAD_ACT;
 //   HIDDEN_F16: with bf16 data, keep hidden activations in fp16 (11-bit mantissa instead of 8)
 //   and run layers >= 1 as fp16 x fp16 MMAs on fp16 copies of their weights (bf16 -> fp16 is
 //   exact for weights within fp16 range). Input, first layer and output stay bf16.
@@ -94,7 +95,8 @@ struct StreamLayout {
   }
   static_assert(CG == 1 || (CG == 2 && pairOk()), "CTA pairs need output halves of 128-column multiples");
   static constexpr int kBiasBytes = ((biasFloats() * 4 + 1023) / 1024) * 1024;
-  static constexpr int kLnBytes = C::TAIL == kTailLayerNorm ? 2 * C::N(NL - 1) * 4 : 0;
+  static constexpr bool kLN = C::TAIL == kTailLayerNorm || C::TAIL == kTailResidualLN;
+  static constexpr int kLnBytes = kLN ? 2 * C::N(NL - 1) * 4 : 0;
   static constexpr int kHeadPad = ((C::HEAD_N + 3) / 4) * 4;  // head outputs, padded to float4
   static constexpr int kHeadBytes = C::TAIL == kTailHead ? (C::N(NL - 1) * kHeadPad * 4 + 64 * 4) : 0;
   static constexpr int kEpiWarps = 8;
@@ -103,13 +105,13 @@ struct StreamLayout {
   // quarter of two consecutive panels from kStgPanel0: for LayerNorm tails panels 0 and 1 (all of
   // the last layer's MMAs are complete before its epilogue stages anything); otherwise the first
   // panels the last layer does not read (its A operand is panels 0 .. K/64 - 1).
-  static constexpr int kStgPanel0 = C::TAIL == kTailLayerNorm ? 0 : (C::K(NL - 1) + kPanel - 1) / kPanel;
+  static constexpr int kStgPanel0 = kLN ? 0 : (C::K(NL - 1) + kPanel - 1) / kPanel;
   static constexpr bool kStgInAct = C::TAIL != kTailHead && (C::SKIP == 0 || C::SKIP != NL - 1) &&
                                     actW() >= (kStgPanel0 + 2) * kPanel;
   static constexpr int kStgBytes = (C::TAIL == kTailHead || kStgInAct) ? 0 : kEpiWarps * kStageBytes;
   // cross-group exchange: LayerNorm (sum, sum of squares) or head partial sums, per row
   static constexpr int kXchgBytes =
-      C::TAIL == kTailHead ? kBM * kHeadPad * 4 : (C::TAIL == kTailLayerNorm ? 2 * kBM * 8 : 0);
+      C::TAIL == kTailHead ? kBM * kHeadPad * 4 : (kLN ? 2 * kBM * 8 : 0);
   static constexpr int kBarBytes = 256;  // 32 eight-byte slots (see the kernel)
   static constexpr int kFixed = kActBytes + kXBytes + kBiasBytes + kLnBytes + kHeadBytes +
                                 kXchgBytes + kStgBytes + kBarBytes + 1024;  // + alignment of the staging area
@@ -232,7 +234,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
     for (int i = threadIdx.x; i < C::N(l); i += blockDim.x)
       bias_s[L::biasOff(l) + i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
   }
-  if constexpr (C::TAIL == kTailLayerNorm) {
+  if constexpr (L::kLN) {
     const T* g = reinterpret_cast<const T*>(args.gamma);
     const T* b = reinterpret_cast<const T*>(args.beta);
     for (int i = threadIdx.x; i < C::N(NL - 1); i += blockDim.x) {
@@ -665,9 +667,25 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
           }
           if (!pair_sync()) { ok = false; break; }  // the exchange slots are free again
         } else {
-          // last layer: optional LayerNorm (statistics pass over TMEM), then store via staging
+          // last layer: optional (residual +) LayerNorm (statistics pass over TMEM), then store via
+          // staging. The residual rows are read with 16-byte loads, once per pass.
+          auto resid_add = [&](int c, float (&y)[32]) {
+            if constexpr (C::TAIL == kTailResidualLN) {
+              if (row < args.m) {
+                const uint4* src = reinterpret_cast<const uint4*>(
+                    reinterpret_cast<const T*>(args.resid) + row * C::N(NL - 1) + c * 32);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint4 w = __ldg(src + j);
+                  const T* t = reinterpret_cast<const T*>(&w);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) y[j * 8 + e] += Elem<T>::to_f(t[e]);
+                }
+              }
+            }
+          };
           float mean = 0.f, rstd = 1.f;
-          if constexpr (C::TAIL == kTailLayerNorm) {
+          if constexpr (L::kLN) {
             if (!wait_acc(0) || (NH == 2 && !wait_acc(1))) { ok = false; break; }
             float s = 0.f, sq = 0.f;
 #pragma unroll 1
@@ -675,11 +693,14 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               uint32_t v[32];
               tmem_ld32(t_lane + c * 32, v);
               tmem_wait_ld();
+              float y[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(v[i]) + bl[c * 32 + i];
+              resid_add(c, y);
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                const float y = __uint_as_float(v[i]) + bl[c * 32 + i];
-                s += y;
-                sq = fmaf(y, y, sq);
+                s += y[i];
+                sq = fmaf(y[i], y[i], sq);
               }
             }
             float2* xs = reinterpret_cast<float2*>(xchg);
@@ -694,7 +715,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
           }
 #pragma unroll 1
           for (int hf = 0; hf < NH; ++hf) {
-            if constexpr (C::TAIL != kTailLayerNorm) {
+            if constexpr (!L::kLN) {
               if (!wait_acc(hf)) { ok = false; break; }
             }
 #pragma unroll 1
@@ -704,13 +725,17 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               tmem_wait_ld();
               if (c + 2 >= (hf + 1) * hc) release(hf);  // this warp's part of the half is read
               uint32_t pk[16];
-              act_dispatch(C::TAIL == kTailLayerNorm ? int(kActNone) : act_id, [&](auto actc) {
+              float yr[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) yr[i] = __uint_as_float(v[i]) + bl[c * 32 + i];
+              resid_add(c, yr);
+              act_dispatch(L::kLN ? int(kActNone) : act_id, [&](auto actc) {
                 constexpr int A = decltype(actc)::value;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                  float y0 = __uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i];
-                  float y1 = __uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1];
-                  if constexpr (C::TAIL == kTailLayerNorm) {
+                  float y0 = yr[2 * i];
+                  float y1 = yr[2 * i + 1];
+                  if constexpr (L::kLN) {
                     y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
                     y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
                   } else {

@@ -215,6 +215,37 @@ def bert_ffn(x, w1, b1, w2, b2, ga, be, eps=1e-12) -> torch.Tensor:
     return out
 
 
+def bert_addln_ffn_out(attn_out, x, w0, b0, w1, b1, w2, b2, ga0, be0, ga2, be2, out) -> None:
+    """apps/bert_addln_ffn (H = 128, ff = 512, fp16): h = LN0(attn_out W0 + b0 + x),
+    out = LN2(ReLU(h W1 + b1) W2 + b2 + h). Same argument order as the reference's
+    bert_addln_ffn_out (bert_addln_ffn_pl_ext.cu:15-58)."""
+    for name, t in (("attn_out", attn_out), ("x", x), ("out", out)):
+        _check_input(name, t, torch.float16)
+        if t.dim() != 2 or t.shape[1] != 128 or t.shape[0] != x.shape[0]:
+            raise RuntimeError(f"{name} has shape {tuple(t.shape)}, expected [{x.shape[0]}, 128]")
+    for name, w, shp in (("w0", w0, (128, 128)), ("w1", w1, (128, 512)), ("w2", w2, (512, 128))):
+        _check_input(name, w, torch.float16)
+        if tuple(w.shape) != shp:
+            raise RuntimeError(f"{name} has shape {tuple(w.shape)}, expected {shp}")
+    for name, t, n in (("b0", b0, 128), ("b1", b1, 512), ("b2", b2, 128), ("ga0", ga0, 128),
+                       ("be0", be0, 128), ("ga2", ga2, 128), ("be2", be2, 128)):
+        _check_input(name, t, torch.float16)
+        if t is not None and tuple(t.shape) != (n,):
+            raise RuntimeError(f"{name} has shape {tuple(t.shape)}, expected ({n},)")
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_bert_addln_ffn_out(
+            x.shape[0], _ptr(attn_out), _ptr(x), _ptr(w0), _ptr(b0), _ptr(w1), _ptr(b1), _ptr(w2),
+            _ptr(b2), _ptr(ga0), _ptr(be0), _ptr(ga2), _ptr(be2), _ptr(out), _stream(x)))
+
+
+def bert_addln_ffn(attn_out, x, w0, b0, w1, b1, w2, b2, ga0, be0, ga2, be2) -> torch.Tensor:
+    """Allocating form. (The reference's passes be0 where be2 belongs,
+    bert_addln_ffn_pl_ext.cu:74; this one passes be2.)"""
+    out = _out_like(x, 128)
+    bert_addln_ffn_out(attn_out, x, w0, b0, w1, b1, w2, b2, ga0, be0, ga2, be2, out)
+    return out
+
+
 def dlrm_topmlp_out(x, w1, b1, w2, b2, w3, b3, w4, b4, w5, b5, out) -> None:
     """x [M, 480] -> 1024 -> 1024 -> 512 -> 256 (ReLU) -> 1 (sigmoid)."""
     fused_mlp_out(x, [w1, w2, w3, w4, w5], [b1, b2, b3, b4, b5], out,
@@ -229,6 +260,12 @@ def dlrm_topmlp(x, *wb) -> torch.Tensor:
 
 def run_workload_out(w, x, weights, ln, out) -> None:
     """Run a workloads.Workload chain through the generic C entry point."""
+    if w.block == "bert_addln":
+        m = x.shape[0] // 2
+        (w0, b0), (w1, b1), (w2, b2) = weights
+        ga0, be0, ga2, be2 = ln
+        bert_addln_ffn_out(x[:m], x[m:], w0, b0, w1, b1, w2, b2, ga0, be0, ga2, be2, out)
+        return
     gamma, beta = ln if ln is not None else (None, None)
     fused_mlp_out(x, [p[0] for p in weights], [p[1] for p in weights], out, acts=w.acts,
                   tail=w.tail, gamma=gamma, beta=beta, ln_eps=w.ln_eps, skip_layer=w.skip_layer)

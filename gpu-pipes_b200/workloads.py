@@ -47,6 +47,8 @@ class Workload:
     weight_init: str = "kaiming"  # kaiming (nn.Linear default) | normal002 | xavier
     bias_init: str = "default"    # default (nn.Linear) | zero
     skip_layer: int = 0           # layer reading [previous output || x] (NeRF), 0 = none
+    block: str = ""               # "" = one chain; "bert_addln" = attention-output Linear + x +
+                                  # LN0, then the FFN chain (inputs: attn_out rows, then x rows)
     description: str = ""
 
     @property
@@ -74,8 +76,13 @@ class Workload:
         return sum(2 * l.k_logical * l.n_logical for l in self.layers)
 
     @property
+    def in_width(self) -> int:
+        """Stored input bytes per row / 2 (attn_out and x for the bert_addln block)."""
+        return 2 * self.k0 if self.block == "bert_addln" else self.k0
+
+    @property
     def bytes_per_row(self) -> int:
-        return 2 * (self.k0 + self.n_out)
+        return 2 * (self.in_width + self.n_out)
 
     @property
     def n_out_logical(self) -> int:
@@ -165,8 +172,21 @@ DLRM_TOP = Workload(
             Layer(256, 1, L.ACT_SIGMOID, 256, 1)),
     description="DLRM top MLP: 479(480)->1024->1024->512->256 ReLU ->1 sigmoid, fp16")
 
+# BERT attention-output block (apps/bert_addln_ffn, model.py:4-19) at the reference's widths and
+# row count (perf.py: M = 64 * 512): h = LN0(attn_out W0 + b0 + x), LN2(FFN(h) + h), fp16, ReLU.
+BERT_ADDLN = Workload(
+    name="bert_addln", m=32768, dtype=torch.float16, seed=5, tail=L.TAIL_RESIDUAL_LN, ln_eps=1e-5,
+    input_logical=128, block="bert_addln",
+    layers=(Layer(128, 128, _N, 128, 128), Layer(128, 512, _R, 128, 512), Layer(512, 128, _N, 512, 128)),
+    description="BERT attention-output block: 128->128 +x LN0, 128->512 ReLU->128 +h LN2, fp16")
+
 WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF,
-                                 BERT_FFN, DLRM_TOP)}
+                                 BERT_FFN, DLRM_TOP, BERT_ADDLN)}
+
+
+def rows_of(w: Workload, x: torch.Tensor) -> int:
+    """Rows of workload input `x` (the bert_addln block stacks attn_out rows over x rows)."""
+    return x.shape[0] // 2 if w.block == "bert_addln" else x.shape[0]
 
 
 # ------------------------------------------------------------------------------------------------
@@ -213,6 +233,8 @@ def make_weights(w: Workload):
     ln = None
     if w.tail != L.TAIL_NONE:
         ln = (torch.ones(w.n_out, dtype=w.dtype), torch.zeros(w.n_out, dtype=w.dtype))
+        if w.block == "bert_addln":  # LN0 and LN2
+            ln = ln + (torch.ones(w.n_out, dtype=w.dtype), torch.zeros(w.n_out, dtype=w.dtype))
     return layers, ln
 
 
@@ -220,6 +242,10 @@ def make_input_chunk(w: Workload, chunk: int, rows: int | None = None) -> torch.
     """Rows [chunk*CHUNK_ROWS, chunk*CHUNK_ROWS + rows) of the input, in w.dtype."""
     rows = CHUNK_ROWS if rows is None else rows
     g = _gen(w.seed, 1, chunk)
+    if w.block == "bert_addln":
+        # [attn_out rows; x rows], both ~N(0, 1)
+        return torch.cat([torch.randn(rows, w.k0, generator=g),
+                          torch.randn(rows, w.k0, generator=_gen(w.seed, 2, chunk))]).to(w.dtype)
     if w.input_kind == "normal":
         x = torch.randn(rows, w.k0, generator=g)
     elif w.input_kind == "dlrm_dense":
@@ -244,6 +270,24 @@ def make_input(w: Workload, row0: int = 0, rows: int | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """Rows [row0, row0+rows) of the input (host tensor, optionally written into `out`)."""
     rows = w.m - row0 if rows is None else rows
+    if w.block == "bert_addln":
+        a = torch.empty(rows, w.k0, dtype=w.dtype)
+        b = torch.empty(rows, w.k0, dtype=w.dtype)
+        r = row0
+        while r < row0 + rows:
+            c = r // CHUNK_ROWS
+            c0 = c * CHUNK_ROWS
+            take = min(c0 + CHUNK_ROWS, row0 + rows) - r
+            need = r - c0 + take
+            chunk = make_input_chunk(w, c, need)
+            a[r - row0:r - row0 + take] = chunk[r - c0:r - c0 + take]
+            b[r - row0:r - row0 + take] = chunk[need + r - c0:need + r - c0 + take]
+            r += take
+        res = torch.cat([a, b])
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
     if out is None:
         out = torch.empty(rows, w.k0, dtype=w.dtype)
     r = row0

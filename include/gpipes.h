@@ -140,6 +140,16 @@ GP_API int gp_bert_ffn_out(int64_t m, const void* x, const void* w1, const void*
                     const void* w2, const void* b2, const void* gamma, const void* beta,
                     float ln_eps, void* out, void* stream);
 
+/* BERT attention-output block at the reference's widths (H = 128, ff = 512, fp16, ReLU, LN eps
+ * 1e-5): out = LN2(ReLU(h W1 + b1) W2 + b2 + h) with h = LN0(attn_out W0 + b0 + x).
+ * Replaces apps/bert_addln_ffn/pipelined/bert_addln_ffn_pl_ext.cu:15-58 bert_addln_ffn_out
+ * (same argument order). attn_out, x, out: [m, 128]; w0 [128, 128], w1 [128, 512], w2 [512, 128];
+ * b*, ga*, be*: [N]. Runs as two fused chains with h in a per-device workspace. */
+GP_API int gp_bert_addln_ffn_out(int64_t m, const void* attn_out, const void* x, const void* w0,
+                                 const void* b0, const void* w1, const void* b1, const void* w2,
+                                 const void* b2, const void* ga0, const void* be0, const void* ga2,
+                                 const void* be2, void* out, void* stream);
+
 /* DLRM top MLP, fp16: x [m, 480] (479 interaction features, zero padded) -> 1024 -> 1024 -> 512
  * -> 256 (ReLU) -> 1 (sigmoid); w[5], b[5]; w1 is [480, 1024]; out [m, 1].
  * Replaces dlrm_topmlp_out (apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl_ext.cu:24-71), which pads

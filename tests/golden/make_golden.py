@@ -165,6 +165,8 @@ def main() -> None:
     _save("nerf_63", seed=np.int64(seed), dims_in=np.array(dims_in), dims_out=np.array(dims_out),
           x=_u16(x), y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
 
+    gen_bert_addln(ref, rows)
+
     # ---- known-answer LayerNorm row from misc_tests/layer_norm/torch_val.py:87-116
     src = (ref / "misc_tests/layer_norm/torch_val.py").read_text()
     body = src[src.index("def manual_test"):]
@@ -174,6 +176,33 @@ def main() -> None:
     row = torch.tensor(vals, dtype=torch.float16)
     y = torch.nn.functional.layer_norm(row.float()[None], [128])[0]
     _save("ln_known_row", x=_u16(row), y=y.numpy().astype(np.float32))
+
+
+def gen_bert_addln(ref: Path, rows: int = 48) -> None:
+    """BertFfn of apps/bert_addln_ffn/torch/model.py:4-19 (attention-output Linear + x + LN0, then
+    the 128 -> 512 ReLU -> 128 FFN + residual + LN2), fp16 inputs, perturbed LayerNorm params."""
+    mod = _load(ref, "apps/bert_addln_ffn/torch/model.py", "ref_bert_addln")
+    seed = 61
+    layers = layer_params(seed, [128, 128]) + layer_params(seed + 1, [128, 512, 128])
+    net = mod.BertFfn(128, 512).eval()
+    _set_linear(net.y0w0, *layers[0])
+    _set_linear(net.ffn[0], *layers[1])
+    _set_linear(net.ffn[2], *layers[2])
+    g = torch.Generator().manual_seed(seed + 100)
+    attn = torch.randn(rows, 128, generator=g).half()
+    x = torch.randn(rows, 128, generator=g).half()
+    lnp = {}
+    for name, lnm in (("ln0", net.ln0), ("ln2", net.ln2)):
+        ga = (1 + 0.1 * torch.randn(128, generator=g)).half()
+        be = (0.1 * torch.randn(128, generator=g)).half()
+        with torch.no_grad():
+            lnm.weight.copy_(ga.float())
+            lnm.bias.copy_(be.float())
+        lnp[name + "_gamma"], lnp[name + "_beta"] = _u16(ga), _u16(be)
+    with torch.no_grad():
+        y = net(attn.float(), x.float())
+    _save("bert_addln_ffn_128", seed=np.int64(seed), attn=_u16(attn), x=_u16(x),
+          y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)), **lnp)
 
 
 if __name__ == "__main__":

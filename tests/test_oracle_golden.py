@@ -97,3 +97,16 @@ def test_compare_thresholds():
     nan = e.clone()
     nan[0, 0] = float("nan")
     assert not O.compare(nan, e)["ok"]
+
+
+def test_bert_addln_ffn_matches_reference_model():
+    g = load_golden("bert_addln_ffn_128")
+    seed = int(g["seed"])
+    layers = layer_params(seed, [128, 128]) + layer_params(seed + 1, [128, 512, 128])
+    assert abs(checksum(layers) - float(g["wsum"])) < 1e-6, "weight generator drifted"
+    attn = u16_to(g["attn"], torch.float16)
+    x = u16_to(g["x"], torch.float16)
+    ln0 = (u16_to(g["ln0_gamma"], torch.float16), u16_to(g["ln0_beta"], torch.float16))
+    ln2 = (u16_to(g["ln2_gamma"], torch.float16), u16_to(g["ln2_beta"], torch.float16))
+    y = O.bert_addln_ffn(attn, x, layers, ln0, ln2)
+    torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
