@@ -25,6 +25,7 @@ GP_DECLARE(launch_mgn_ln_bf16_k128_single)
 GP_DECLARE(launch_dlrm_bot_f16)
 GP_DECLARE(launch_addln0_f16_h128)
 GP_DECLARE(launch_ffn_resln_f16_h128)
+GP_DECLARE(launch_ffn_resln_bf16_h128)
 GP_DECLARE(launch_gc_silu_bf16_k1536)
 GP_DECLARE(launch_gc_relu_f16_k1536)
 GP_DECLARE(launch_gc_relu_bf16_k1536)
@@ -74,9 +75,11 @@ static const ChainEntry kChains[] = {
     {"nerf_trunk_f16", GP_F16, 8, {64, 256, 256, 256, 256, 256, 256, 256, 256}, {R, R, R, R, R, R, R, R},
      GP_TAIL_NONE, launch_nerf_trunk_f16, 0, 5},
     // BERT attention-output block at the reference's widths (apps/bert_addln_ffn): 128 -> 128 with
-    // residual + LN0, then 128 -> 512 ReLU -> 128 with residual + LN2
+    // residual + LN0, then 128 -> 512 ReLU -> 128 with residual + LN2 (the latter is also the
+    // reference's small BERT FFN, apps/bert_ffn)
     {"addln0_f16_h128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_RESIDUAL_LN, launch_addln0_f16_h128, 0},
     {"ffn_resln_f16_h128", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128, 0},
+    {"ffn_resln_bf16_h128", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128, 0},
     // chains with activations too wide for one SM: per-layer GEMMs over large row chunks
     {"bert_ffn_bf16", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
      launch_bert_ffn_bf16, 0},

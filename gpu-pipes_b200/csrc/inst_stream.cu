@@ -62,19 +62,25 @@ struct ChainAddLn0 {
   static constexpr int HALVES = 1;
 };
 
+// The FFN stage is also the reference's own small BERT FFN (apps/bert_ffn, 128 -> 512 ReLU -> 128,
+// + x, LN): fp16, and bf16 with fp16 hidden activations.
+template <typename TT>
 struct ChainFfnResLn {
-  using T = __half;
+  using T = TT;
   static constexpr int NL = 2;
   __host__ __device__ static constexpr int K(int l) { return l == 0 ? 128 : 512; }
   __host__ __device__ static constexpr int N(int l) { return l == 0 ? 512 : 128; }
   __host__ __device__ static constexpr int ACT(int l) { return l == 0 ? kActRelu : kActNone; }
   static constexpr int SKIP = 0, TAIL = kTailResidualLN, HEAD_N = 0, HEAD_ACT = kActNone;
-  static constexpr bool HIDDEN_F16 = false;
+  static constexpr bool HIDDEN_F16 = std::is_same<TT, __nv_bfloat16>::value;
   static constexpr int HALVES = 2;
 };
 
 int launch_addln0_f16_h128(const LaunchCtx& c) { return launch_stream<ChainAddLn0>(c); }
-int launch_ffn_resln_f16_h128(const LaunchCtx& c) { return launch_stream<ChainFfnResLn>(c); }
+int launch_ffn_resln_f16_h128(const LaunchCtx& c) { return launch_stream<ChainFfnResLn<__half>>(c); }
+int launch_ffn_resln_bf16_h128(const LaunchCtx& c) {
+  return launch_stream<ChainFfnResLn<__nv_bfloat16>>(c);
+}
 
 int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot>(c); }
 int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>, 2>(c); }

@@ -203,13 +203,21 @@ def nerf_out(x, weights, biases, out) -> None:
                   skip_layer=5)
 
 
-def bert_ffn_out(x, w1, b1, w2, b2, ga, be, out, eps=1e-12) -> None:
-    """BERT-large FFN, bf16: out = LN(x + W2 gelu_tanh(W1 x + b1) + b2); x [M, 1024]."""
-    fused_mlp_out(x, [w1, w2], [b1, b2], out, acts=[L.ACT_GELU_TANH, L.ACT_NONE],
+def bert_ffn_out(x, w1, b1, w2, b2, ga, be, out, eps=None) -> None:
+    """out = LN(x + W2 act(W1 x + b1) + b2).
+
+    x [M, 128]: the reference's own BERT FFN (apps/bert_ffn: 128 -> 512 ReLU -> 128, LayerNorm eps
+    1e-5), fp16 or bf16. x [M, 1024]: BERT-large (1024 -> 4096 GELU(tanh) -> 1024, eps 1e-12),
+    bf16."""
+    if x.dim() == 2 and x.shape[1] == 128:
+        act0, eps = L.ACT_RELU, 1e-5 if eps is None else eps
+    else:
+        act0, eps = L.ACT_GELU_TANH, 1e-12 if eps is None else eps
+    fused_mlp_out(x, [w1, w2], [b1, b2], out, acts=[act0, L.ACT_NONE],
                   tail=L.TAIL_RESIDUAL_LN, gamma=ga, beta=be, ln_eps=eps)
 
 
-def bert_ffn(x, w1, b1, w2, b2, ga, be, eps=1e-12) -> torch.Tensor:
+def bert_ffn(x, w1, b1, w2, b2, ga, be, eps=None) -> torch.Tensor:
     out = _out_like(x, x.shape[1])
     bert_ffn_out(x, w1, b1, w2, b2, ga, be, out, eps=eps)
     return out

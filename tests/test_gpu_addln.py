@@ -72,3 +72,26 @@ def test_allocating_form_and_shape_errors(cuda_dev):
     with pytest.raises(RuntimeError):
         cuda_ext.bert_addln_ffn(attn.to(cuda_dev), x.to(cuda_dev), w0[:64], b0, w1, b1, w2, b2,
                                 ga0, be0, ga2, be2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_reference_bert_ffn_128(cuda_dev, dtype):
+    """The reference's own small BERT FFN (apps/bert_ffn: 128 -> 512 ReLU -> 128, + x, LN eps
+    1e-5) through cuda_ext.bert_ffn; the bf16 case against the reference model's golden output."""
+    if dtype == torch.bfloat16:
+        g = load_golden("bert_ffn_128")
+        layers = layer_params(int(g["seed"]), [128, 512, 128], dtype=torch.bfloat16, init="normal002")
+        x = u16_to(g["x"], torch.bfloat16)
+        expected = torch.from_numpy(g["y"])
+        ln = (torch.ones(128, dtype=dtype), torch.zeros(128, dtype=dtype))
+    else:
+        layers = layer_params(91, [128, 512, 128], dtype=dtype)
+        gx = torch.Generator().manual_seed(92)
+        x = torch.randn(5000, 128, generator=gx).to(dtype)
+        ln = ((1 + 0.1 * torch.randn(128, generator=gx)).to(dtype), (0.1 * torch.randn(128, generator=gx)).to(dtype))
+        expected = O.bert_ffn(x, layers, ln, act_id=O.ACT_RELU, ln_eps=1e-5)
+    d = [t.to(cuda_dev) for wb in layers for t in wb]
+    out = cuda_ext.bert_ffn(x.to(cuda_dev), *d, *[t.to(cuda_dev) for t in ln])
+    torch.cuda.synchronize()
+    r = O.compare(out.float().cpu(), expected)
+    assert r["ok"], r
