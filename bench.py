@@ -130,6 +130,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# The kernel that dominates each config's step (the one the roofline line describes).
+KERNEL_OF = {
+    "mgn_node": "mlp_resident_kernel", "mgn_edge": "mlp_resident_pair_kernel",
+    "mgn_linears": "mlp_resident_pair_kernel", "test_mlp": "mlp_resident_kernel",
+    "dlrm_bot": "mlp_stream_kernel", "nerf": "mlp_stream_kernel", "gc_edge": "mlp_stream_pair_kernel",
+    "bert_ffn": "mlp_gemm_pair_kernel", "dlrm_top": "mlp_gemm_pair_kernel",
+    "bert_addln": "mlp_stream_kernel", "dlrm_interact": "dlrm_interaction_kernel",
+}
+
+
 def cpu_oracle_rate(w, seconds: float) -> dict:
     """The CPU oracle on whole 65,536-row chunks for about `seconds` (at least one chunk)."""
     from oracle import mlp_oracle as O
@@ -137,7 +147,7 @@ def cpu_oracle_rate(w, seconds: float) -> dict:
     torch.set_num_threads(os.cpu_count() or 1)
     layers, ln = W.make_weights(w)
     x = W.make_input_chunk(w, 0)
-    O.workload_forward(w, x[:4096], layers, ln)  # warm-up
+    O.workload_forward(w, W.make_input(w, 0, 256), layers, ln)  # warm-up
     rows, t0 = 0, time.perf_counter()
     while True:
         O.workload_forward(w, x, layers, ln)
@@ -344,8 +354,7 @@ def main():
                          "frac": achieved / peak,
                          "traffic": None if tr is None else tr * w.m,
                          "peak_source": f"{peak_note} (MEASURED_PEAKS.json)",
-                         "kernel": "mlp_resident_kernel" if w.name.startswith(("mgn", "test"))
-                                   else "mlp_stream_kernel",
+                         "kernel": KERNEL_OF.get(w.name, "mlp_stream_kernel"),
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "algorithmic_flops_per_launch": alg_flops},
             "e2e": {"value": e2e_value, "unit": "rows/s",

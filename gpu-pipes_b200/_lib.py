@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "gp_gc_nodes_out",
     "gp_bert_ffn_out",
     "gp_bert_addln_ffn_out",
+    "gp_dlrm_interaction_out",
     "gp_dlrm_topmlp_out",
     "gp_nerf_a_out",
     "gp_nerf_out",
@@ -113,6 +114,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_bert_ffn_out.restype = _INT
     lib.gp_bert_addln_ffn_out.argtypes = [_I64] + [_P] * 14
     lib.gp_bert_addln_ffn_out.restype = _INT
+    lib.gp_dlrm_interaction_out.argtypes = [_I64, _P, _P, _P, _P]
+    lib.gp_dlrm_interaction_out.restype = _INT
     lib.gp_dlrm_topmlp_out.argtypes = [_I64, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P]
     lib.gp_dlrm_topmlp_out.restype = _INT
     lib.gp_gc_edges_bf16_noalloc_out.argtypes = [_I64, _INT] + [_P] * 9

@@ -44,6 +44,10 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, u
                  uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 int make_tmap_2d_f32(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
                      uint32_t box_rows, int swizzle_bytes);
+// DLRM feature interaction (dlrm_interaction.cu): bot [m, 128], sparse [m, 26, 128] -> out [m, 480]
+int launch_dlrm_interaction(int64_t m, const void* bot, const void* sparse, void* out,
+                            cudaStream_t stream, int sm_count, int* status,
+                            unsigned long long timeout_ns);
 int make_tmap_w3d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
                   uint32_t box_rows, uint32_t box_blocks);
 

@@ -488,6 +488,26 @@ int gp_bert_addln_ffn_out(int64_t m, const void* attn_out, const void* x, const 
   return rc;
 }
 
+// DLRM feature interaction (graphmodel/dlrm.py:28-42): out [m, 480] = [bot | strict lower
+// triangle of [bot; e_0..e_25] [bot; e_0..e_25]^T | 0], the top MLP's input. fp16.
+int gp_dlrm_interaction_out(int64_t m, const void* bot, const void* sparse, void* out, void* stream) {
+  clear_error();
+  if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
+  if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
+  if (bot == nullptr || sparse == nullptr || out == nullptr)
+    return set_error(GP_ERR_ARG, "bot, sparse and out must not be NULL");
+  if (!aligned(bot, 16) || !aligned(sparse, 16) || !aligned(out, 16))
+    return set_error(GP_ERR_ALIGN, "bot, sparse and out must be 16-byte aligned");
+  if (m == 0) return GP_OK;
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != GP_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = launch_dlrm_interaction(m, bot, sparse, out, s, st->sm_count, st->status, g_timeout_ns.load());
+  if (rc != GP_OK) return rc;
+  return finish_launch(s, 1);
+}
+
 static gp_mlp_spec nerf_spec(bool head) {
   gp_mlp_spec s{};
   s.n_layers = head ? 9 : 8;

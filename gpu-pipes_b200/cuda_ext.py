@@ -254,6 +254,30 @@ def bert_addln_ffn(attn_out, x, w0, b0, w1, b1, w2, b2, ga0, be0, ga2, be2) -> t
     return out
 
 
+def dlrm_interaction_out(bot, sparse, out) -> None:
+    """DLRM feature interaction (graphmodel/dlrm.py:28-42): bot [M, 128] (bottom MLP output),
+    sparse [M, 26, 128] (embedding vectors) -> out [M, 480] = [bot | 351 pairwise dot products
+    below the diagonal, row-major | 0], the top MLP's input. fp16."""
+    _check_input("bot", bot, torch.float16)
+    _check_input("sparse", sparse, torch.float16)
+    _check_input("out", out, torch.float16)
+    m = bot.shape[0]
+    if bot.dim() != 2 or bot.shape[1] != 128:
+        raise RuntimeError(f"bot has shape {tuple(bot.shape)}, expected [M, 128]")
+    if tuple(sparse.shape) != (m, 26, 128):
+        raise RuntimeError(f"sparse has shape {tuple(sparse.shape)}, expected [{m}, 26, 128]")
+    if tuple(out.shape) != (m, 480):
+        raise RuntimeError(f"out has shape {tuple(out.shape)}, expected [{m}, 480]")
+    with torch.cuda.device(bot.device):
+        L.check(L.lib().gp_dlrm_interaction_out(m, _ptr(bot), _ptr(sparse), _ptr(out), _stream(bot)))
+
+
+def dlrm_interaction(bot, sparse) -> torch.Tensor:
+    out = torch.empty(bot.shape[0], 480, dtype=bot.dtype, device=bot.device)
+    dlrm_interaction_out(bot, sparse, out)
+    return out
+
+
 def dlrm_topmlp_out(x, w1, b1, w2, b2, w3, b3, w4, b4, w5, b5, out) -> None:
     """x [M, 480] -> 1024 -> 1024 -> 512 -> 256 (ReLU) -> 1 (sigmoid)."""
     fused_mlp_out(x, [w1, w2, w3, w4, w5], [b1, b2, b3, b4, b5], out,
@@ -268,6 +292,10 @@ def dlrm_topmlp(x, *wb) -> torch.Tensor:
 
 def run_workload_out(w, x, weights, ln, out) -> None:
     """Run a workloads.Workload chain through the generic C entry point."""
+    if w.block == "dlrm_interaction":
+        m = x.shape[0] // 27
+        dlrm_interaction_out(x[:m], x[m:].view(m, 26, x.shape[1]), out)
+        return
     if w.block == "bert_addln":
         m = x.shape[0] // 2
         (w0, b0), (w1, b1), (w2, b2) = weights

@@ -48,7 +48,9 @@ class Workload:
     bias_init: str = "default"    # default (nn.Linear) | zero
     skip_layer: int = 0           # layer reading [previous output || x] (NeRF), 0 = none
     block: str = ""               # "" = one chain; "bert_addln" = attention-output Linear + x +
-                                  # LN0, then the FFN chain (inputs: attn_out rows, then x rows)
+                                  # LN0, then the FFN chain (inputs: attn_out rows, then x rows);
+                                  # "dlrm_interaction" = the DLRM feature interaction (inputs: m
+                                  # bottom-output rows, then 26 m embedding rows; no layers)
     description: str = ""
 
     @property
@@ -57,7 +59,7 @@ class Workload:
 
     @property
     def n_out(self) -> int:
-        return self.layers[-1].n
+        return 480 if self.block == "dlrm_interaction" else self.layers[-1].n
 
     @property
     def widths(self) -> list:
@@ -73,11 +75,15 @@ class Workload:
 
     @property
     def flop_per_row(self) -> int:
+        if self.block == "dlrm_interaction":
+            return 351 * 2 * 128  # the dot products below the diagonal
         return sum(2 * l.k_logical * l.n_logical for l in self.layers)
 
     @property
     def in_width(self) -> int:
         """Stored input bytes per row / 2 (attn_out and x for the bert_addln block)."""
+        if self.block == "dlrm_interaction":
+            return 27 * 128
         return 2 * self.k0 if self.block == "bert_addln" else self.k0
 
     @property
@@ -180,12 +186,21 @@ BERT_ADDLN = Workload(
     layers=(Layer(128, 128, _N, 128, 128), Layer(128, 512, _R, 128, 512), Layer(512, 128, _N, 512, 128)),
     description="BERT attention-output block: 128->128 +x LN0, 128->512 ReLU->128 +h LN2, fp16")
 
+# DLRM feature interaction between the bottom and top MLPs (graphmodel/dlrm.py:28-42) at the DLRM
+# batch: bottom outputs (ReLU-like, >= 0) and 26 embedding vectors per sample, fp16.
+DLRM_INTERACT = Workload(
+    name="dlrm_interact", m=262144, dtype=torch.float16, seed=6, block="dlrm_interaction",
+    layers=(Layer(128, 480, _N, 128, 480),), input_logical=128,
+    description="DLRM interaction: [bot; 26 embeddings] (27 x 128) -> bot | 351 dot products | 0 (480), fp16")
+
 WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF,
-                                 BERT_FFN, DLRM_TOP, BERT_ADDLN)}
+                                 BERT_FFN, DLRM_TOP, BERT_ADDLN, DLRM_INTERACT)}
 
 
 def rows_of(w: Workload, x: torch.Tensor) -> int:
     """Rows of workload input `x` (the bert_addln block stacks attn_out rows over x rows)."""
+    if w.block == "dlrm_interaction":
+        return x.shape[0] // 27
     return x.shape[0] // 2 if w.block == "bert_addln" else x.shape[0]
 
 
@@ -207,6 +222,8 @@ def make_weights(w: Workload):
     Weights use the [K, N] layout the reference's C++ kernels take (`weight.t().contiguous()`).
     Padded input rows/columns (stored k > logical k) are zero.
     """
+    if w.block == "dlrm_interaction":
+        return [], None
     g = _gen(w.seed, 7777)
     layers = []
     for l in w.layers:
@@ -242,6 +259,11 @@ def make_input_chunk(w: Workload, chunk: int, rows: int | None = None) -> torch.
     """Rows [chunk*CHUNK_ROWS, chunk*CHUNK_ROWS + rows) of the input, in w.dtype."""
     rows = CHUNK_ROWS if rows is None else rows
     g = _gen(w.seed, 1, chunk)
+    if w.block == "dlrm_interaction":
+        # [bottom-output rows (ReLU of N(0, 0.3^2)); 26 embedding rows per sample, N(0, 0.1^2)]
+        bot = torch.relu(torch.randn(rows, w.k0, generator=g)) * 0.3
+        emb = torch.randn(rows * 26, w.k0, generator=_gen(w.seed, 2, chunk)) * 0.1
+        return torch.cat([bot, emb]).to(w.dtype)
     if w.block == "bert_addln":
         # [attn_out rows; x rows], both ~N(0, 1)
         return torch.cat([torch.randn(rows, w.k0, generator=g),
@@ -270,6 +292,23 @@ def make_input(w: Workload, row0: int = 0, rows: int | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """Rows [row0, row0+rows) of the input (host tensor, optionally written into `out`)."""
     rows = w.m - row0 if rows is None else rows
+    if w.block == "dlrm_interaction":
+        bots, embs = [], []
+        r = row0
+        while r < row0 + rows:
+            c = r // CHUNK_ROWS
+            c0 = c * CHUNK_ROWS
+            take = min(c0 + CHUNK_ROWS, row0 + rows) - r
+            need = r - c0 + take
+            chunk = make_input_chunk(w, c, need)
+            bots.append(chunk[r - c0:r - c0 + take])
+            embs.append(chunk[need + 26 * (r - c0):need + 26 * (r - c0 + take)])
+            r += take
+        res = torch.cat(bots + embs) if rows else torch.empty(0, w.k0, dtype=w.dtype)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
     if w.block == "bert_addln":
         a = torch.empty(rows, w.k0, dtype=w.dtype)
         b = torch.empty(rows, w.k0, dtype=w.dtype)

@@ -140,6 +140,15 @@ GP_API int gp_bert_ffn_out(int64_t m, const void* x, const void* w1, const void*
                     const void* w2, const void* b2, const void* gamma, const void* beta,
                     float ln_eps, void* out, void* stream);
 
+/* DLRM feature interaction between the bottom and top MLPs (graphmodel/dlrm.py:28-42, where it
+ * is the `interact_bmm` + `interact_index` + concat nodes; the reference has no kernel for it).
+ * For each of the m samples, F = [bot; e_0 .. e_25] (27 x 128) with bot [m, 128] the bottom MLP
+ * output and sparse [m, 26, 128] the embedding vectors; out [m, 480] = [bot | Z[a][b], a > b,
+ * row-major over the strict lower triangle of Z = F F^T (351 values) | 0]: the top MLP's input.
+ * fp16, fp32 accumulation. */
+GP_API int gp_dlrm_interaction_out(int64_t m, const void* bot, const void* sparse, void* out,
+                                   void* stream);
+
 /* BERT attention-output block at the reference's widths (H = 128, ff = 512, fp16, ReLU, LN eps
  * 1e-5): out = LN2(ReLU(h W1 + b1) W2 + b2 + h) with h = LN0(attn_out W0 + b0 + x).
  * Replaces apps/bert_addln_ffn/pipelined/bert_addln_ffn_pl_ext.cu:15-58 bert_addln_ffn_out
