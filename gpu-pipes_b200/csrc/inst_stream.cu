@@ -15,6 +15,7 @@ struct ChainDlrmBot {
   static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 2;
+  static constexpr bool SPLIT_ACT = false;
 };
 
 // GraphCast-style edge / node MLP (apps/gc_edges/torch/model.py:4-14): K0 -> 512 act -> 512, LN.
@@ -28,6 +29,7 @@ struct ChainGc {
   static constexpr int SKIP = 0, TAIL = kTailLayerNorm, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = std::is_same<TT, __nv_bfloat16>::value;
   static constexpr int HALVES = 2;
+  static constexpr bool SPLIT_ACT = false;
 };
 
 // NeRF trunk without view directions (apps/nerf_full/torch/model.py:5-66, use_viewdirs=False):
@@ -41,6 +43,7 @@ struct ChainNerf {
   static constexpr int SKIP = 5, TAIL = kTailHead, HEAD_N = 4, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 1;
+  static constexpr bool SPLIT_ACT = true;
 };
 
 // The same trunk without the head: layer 8's ReLU output is the result (apps/nerf_a).
@@ -60,6 +63,7 @@ struct ChainAddLn0 {
   static constexpr int SKIP = 0, TAIL = kTailResidualLN, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 1;
+  static constexpr bool SPLIT_ACT = false;
 };
 
 // The FFN stage is also the reference's own small BERT FFN (apps/bert_ffn, 128 -> 512 ReLU -> 128,
@@ -74,6 +78,7 @@ struct ChainFfnResLn {
   static constexpr int SKIP = 0, TAIL = kTailResidualLN, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = std::is_same<TT, __nv_bfloat16>::value;
   static constexpr int HALVES = 2;
+  static constexpr bool SPLIT_ACT = false;
 };
 
 int launch_addln0_f16_h128(const LaunchCtx& c) { return launch_stream<ChainAddLn0>(c); }

@@ -83,6 +83,12 @@ struct StreamLayout {
     return true;
   }
   static_assert(halvesOk(), "every layer width must split into two halves of whole 64-column panels");
+  // SPLIT_ACT (one pass per layer, N <= 256): accumulators alternate between TMEM columns
+  // [0, 256) and [256, 512) from layer to layer, and each epilogue releases the activation panels
+  // in two halves, so the next layer's MMAs start on the first half of its K while the epilogue
+  // still writes the second.
+  static constexpr bool kSplit = C::SPLIT_ACT;
+  static_assert(!kSplit || (NH == 1 && maxN() <= 256), "SPLIT_ACT: one pass per layer, N <= 256");
   static constexpr int kActBytes = kBM * actW() * 2;
   // resident x: one buffer. x is released once its last reader (layer 0, or the skip layer) has
   // run, so the next tile's x loads while the remaining layers run; the 16 KB saved go to the
@@ -353,6 +359,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
       const uint32_t b_sm = smem_u32(smem + L::kOffB);
       int bs = 0, xs = 0;
       uint32_t bph = 0, xph = 0, rph[2] = {0, 0};
+      uint32_t lstep = 0;  // layers issued so far (selects the accumulator region with SPLIT_ACT)
       bool first = true, ok = true;
 #pragma unroll 1
       for (int unit = unit0; ok && unit < num_units; unit += units_step) {
@@ -377,7 +384,8 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
           const int panels = (C::K(l) + kPanel - 1) / kPanel;
           const int hw = C::N(l) / NH;
           // activation panels at or beyond hi_p were written by the previous epilogue's half 1
-          const int hi_p = (l == 0 || NH == 1) ? panels + 1 : C::N(l - 1) / 128;
+          const int hi_p = (l == 0 || (NH == 1 && !L::kSplit)) ? panels + 1 : C::N(l - 1) / 128;
+          const uint32_t dcol = L::kSplit ? (lstep & 1u) * 256u : 0u;
           const int ab_bf16 = (l == 0 || !C::HIDDEN_F16) ? Elem<T>::kIsBf16 : 0;
           const uint32_t idesc = make_idesc_f16(kBM * CG, hw, ab_bf16, 0, 1);
           const bool p_outer = !L::kXRes && l == 0;
@@ -407,9 +415,9 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
                 const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK * 128, 1024);
                 const uint32_t acc = (p == 0 && kh == 0 && k == 0) ? 0u : 1u;
                 if constexpr (kPair) {
-                  mma_ss_pair(tmem_base + hf * hw, adesc, bdesc, idesc, acc);
+                  mma_ss_pair(tmem_base + dcol + hf * hw, adesc, bdesc, idesc, acc);
                 } else {
-                  mma_ss(tmem_base + hf * hw, adesc, bdesc, idesc, acc);
+                  mma_ss(tmem_base + dcol + hf * hw, adesc, bdesc, idesc, acc);
                 }
               }
               commit_any(&b_empty[bs]);
@@ -464,7 +472,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
                 if (!mbar_wait<kPair>(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
                 tc_fence_after();
                 const uint64_t bdesc0 = make_sdesc_sw128(b_sm + bs * L::kBStageBytes, L::kBK * 128, 1024);
-                const uint32_t d_tmem = tmem_base + hf * hw;
+                const uint32_t d_tmem = tmem_base + dcol + hf * hw;
                 const int kg0 = r0 >> 4;
                 for (int k = 0; k < ks; ++k) {
                   const int kg = kg0 + k;  // 16-wide K step within the layer
@@ -491,6 +499,10 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
             const int last_x_layer = C::SKIP != 0 ? C::SKIP : 0;
             if (l == last_x_layer) commit_any(&x_empty[xcur]);
           }
+          // with SPLIT_ACT every epilogue releases both halves: consume the second one once per
+          // layer even where no K panel needed it, so the barrier phases stay in step
+          if (L::kSplit && !need(1)) { ok = false; break; }
+          ++lstep;
         }
         if constexpr (L::kXRes) {
           if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
@@ -557,6 +569,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
       }
       if constexpr (L::kStgInAct) sb ^= 1;
     };
+    uint32_t estep = 0;  // layers drained so far (the accumulator region with SPLIT_ACT)
 #pragma unroll 1
     for (int unit = unit0; ok && unit < num_units; unit += units_step) {
       const int row_base = unit * kBM * CG + static_cast<int>(rank) * kBM;
@@ -564,6 +577,8 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
       const int row0 = row_base + q * 32;
 #pragma unroll 1
       for (int l = 0; ok && l < NL; ++l) {
+        const uint32_t dcol = L::kSplit ? (estep & 1u) * 256u : 0u;
+        ++estep;
         const float* bl = bias_s + L::biasOff(l);
         const int act_id = C::ACT(l);
         const int hc = C::N(l) / 32 / NH;  // 32-column chunks per half (even)
@@ -579,7 +594,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
 #pragma unroll 1
             for (int c = hf * hc + eg; c < (hf + 1) * hc; c += 2) {
               uint32_t v[32];
-              tmem_ld32(t_lane + c * 32, v);
+              tmem_ld32(t_lane + dcol + c * 32, v);
               tmem_wait_ld();
               uint8_t* line = act + (c >> 1) * kPanelBytes + r * 128;
               act_dispatch(act_id, [&](auto actc) {
@@ -600,9 +615,13 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
                       make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
               });
+              if (L::kSplit && c < hc / 2 && c + 2 >= hc / 2) {  // first half of the panels written
+                fence_proxy_async_smem();
+                release(0);
+              }
             }
             fence_proxy_async_smem();
-            release(hf);
+            release(L::kSplit ? 1 : hf);
           }
         } else if constexpr (C::TAIL == kTailHead) {
           // last tensor layer + activation, then the narrow head on CUDA cores: each group forms
@@ -617,7 +636,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
 #pragma unroll 1
             for (int c = hf * hc + eg; c < (hf + 1) * hc; c += 2) {
               uint32_t v[32];
-              tmem_ld32(t_lane + c * 32, v);
+              tmem_ld32(t_lane + dcol + c * 32, v);
               tmem_wait_ld();
               act_dispatch(act_id, [&](auto actc) {
                 constexpr int A = decltype(actc)::value;
@@ -638,6 +657,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               });
             }
             release(hf);
+            if (L::kSplit) release(1);
           }
           if (!ok) break;
           float4* xo = reinterpret_cast<float4*>(xchg + r * HP);
@@ -691,7 +711,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
 #pragma unroll 1
             for (int c = eg; c < C::N(l) / 32; c += 2) {
               uint32_t v[32];
-              tmem_ld32(t_lane + c * 32, v);
+              tmem_ld32(t_lane + dcol + c * 32, v);
               tmem_wait_ld();
               float y[32];
 #pragma unroll
@@ -721,7 +741,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
 #pragma unroll 1
             for (int c = hf * hc + eg; c < (hf + 1) * hc; c += 2) {
               uint32_t v[32];
-              tmem_ld32(t_lane + c * 32, v);
+              tmem_ld32(t_lane + dcol + c * 32, v);
               tmem_wait_ld();
               if (c + 2 >= (hf + 1) * hc) release(hf);  // this warp's part of the half is read
               uint32_t pk[16];
@@ -748,6 +768,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               store_chunk(c, row0, pk);
             }
           }
+          if (L::kSplit) release(1);
           if constexpr (L::kStgInAct) {
             // the next tile's hidden epilogue rewrites this lane quarter of the activation
             // buffer: both warps' stores must have read their staging first

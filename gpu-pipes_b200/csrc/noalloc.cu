@@ -51,6 +51,7 @@ struct ChainGcNoAlloc {
   static constexpr int SKIP = 0, TAIL = kTailLayerNorm, HEAD_N = 0, HEAD_ACT = kActNone;
   static constexpr bool HIDDEN_F16 = true;
   static constexpr int HALVES = 2;
+  static constexpr bool SPLIT_ACT = false;
 };
 
 __global__ void noalloc_bf16_to_f16(const __nv_bfloat16* __restrict__ src, __half* __restrict__ dst,

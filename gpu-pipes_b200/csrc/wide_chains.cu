@@ -114,6 +114,7 @@ struct ChainDlrmTail {
   static constexpr int SKIP = 0, TAIL = kTailHead, HEAD_N = 1, HEAD_ACT = kActSigmoid;
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 1;
+  static constexpr bool SPLIT_ACT = false;
 };
 
 }  // namespace
