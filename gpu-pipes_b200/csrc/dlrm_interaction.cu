@@ -62,19 +62,29 @@ __global__ void __launch_bounds__(kIntThreads)
   bool ok = true;
 #pragma unroll 1
   for (int64_t t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-    // ---- load the tile: row r = 32 s + i, 16 chunks of 16 B per row
-#pragma unroll 4
-    for (int q = threadIdx.x; q < 128 * 16; q += kIntThreads) {
-      const int r = q >> 4, c = q & 15;
-      const int s = r >> 5, i = r & 31;
-      const int64_t g = t * kIntSamples + s;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (g < m && i <= 26) {
-        const __half* src = i < 26 ? sparse + (g * 26 + i) * 128 : bot + g * 128;
-        v = __ldg(reinterpret_cast<const uint4*>(src) + c);
+    // ---- load the tile: row r = 32 s + i, 16 chunks of 16 B per row; all 16 loads of a thread
+    // are issued before any store, so a CTA keeps its whole tile in flight
+    {
+      uint4 v[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int q = threadIdx.x + u * kIntThreads;
+        const int r = q >> 4, c = q & 15;
+        const int s = r >> 5, i = r & 31;
+        const int64_t g = t * kIntSamples + s;
+        v[u] = make_uint4(0, 0, 0, 0);
+        if (g < m && i <= 26) {
+          const __half* src = i < 26 ? sparse + (g * 26 + i) * 128 : bot + g * 128;
+          v[u] = __ldg(reinterpret_cast<const uint4*>(src) + c);
+        }
       }
-      const int panel = c >> 3, cp = c & 7;
-      *reinterpret_cast<uint4*>(tile + panel * 16384 + r * 128 + ((cp ^ (r & 7)) * 16)) = v;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int q = threadIdx.x + u * kIntThreads;
+        const int r = q >> 4, c = q & 15;
+        const int panel = c >> 3, cp = c & 7;
+        *reinterpret_cast<uint4*>(tile + panel * 16384 + r * 128 + ((cp ^ (r & 7)) * 16)) = v[u];
+      }
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -92,25 +102,36 @@ __global__ void __launch_bounds__(kIntThreads)
     if (!mbar_wait(smem_u32(bar), phase, wctx, kDevTimeoutEpilogue)) ok = false;
     phase ^= 1;
     tc_fence_after();
-    // ---- epilogue: warp w = sample w of the tile; lane i = row i of its Gram block
+    // ---- epilogue: warp w = sample w of the tile; lane i = row i of its Gram block. The output
+    // row (480 halves, 960 B) is assembled in shared memory, then written with 16-byte stores. It
+    // goes to bytes [4096 w, 4096 w + 960): sample w's own tile rows 0..7 of the first panel, no
+    // longer read by the (complete) MMAs nor by any other warp, and disjoint from its row 26.
     const int64_t g = t * kIntSamples + warp;
     uint32_t v[32];
     tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + warp * 32, v);
     tmem_wait_ld();
+    __half* srow = reinterpret_cast<__half*>(tile + warp * 4096);
+    if (lane < 16) {  // the bottom output, from its tile row 32 w + 26 (un-swizzled)
+      const int r = warp * 32 + 26;
+      const int panel = lane >> 3, cp = lane & 7;
+      reinterpret_cast<uint4*>(srow)[lane] =
+          *reinterpret_cast<const uint4*>(tile + panel * 16384 + r * 128 + ((cp ^ (r & 7)) * 16));
+    }
+    if (lane < 26) {
+      // tile row `lane` is embedding lane = feature a = lane + 1 of F = [bot; e_0 .. e_25]; its
+      // pairs (a, b < a) start at a (a - 1) / 2: b = 0 is the bottom output (tile row 26),
+      // b = j + 1 is embedding j (tile row j)
+      const int a = lane + 1;
+      __half* z = srow + 128 + a * (a - 1) / 2;
+      z[0] = __float2half_rn(__uint_as_float(v[26]));
+      for (int j = 0; j < lane; ++j) z[j + 1] = __float2half_rn(__uint_as_float(v[j]));
+    }
+    if (lane == 31) srow[479] = __float2half_rn(0.0f);
+    __syncwarp();
     if (ok && g < m) {
-      __half* row = out + g * 480;
-      if (lane < 16)
-        reinterpret_cast<uint4*>(row)[lane] = __ldg(reinterpret_cast<const uint4*>(bot + g * 128) + lane);
-      if (lane < 26) {
-        // tile row `lane` is embedding lane = feature a = lane + 1 of F = [bot; e_0 .. e_25];
-        // its pairs (a, b < a) start at a (a - 1) / 2: b = 0 is the bottom output (tile row 26),
-        // b = j + 1 is embedding j (tile row j)
-        const int a = lane + 1;
-        __half* z = row + 128 + a * (a - 1) / 2;
-        z[0] = __float2half_rn(__uint_as_float(v[26]));
-        for (int j = 0; j < lane; ++j) z[j + 1] = __float2half_rn(__uint_as_float(v[j]));
-      }
-      if (lane == 31) row[479] = __float2half_rn(0.0f);
+      const uint4* src = reinterpret_cast<const uint4*>(srow);
+      uint4* dst = reinterpret_cast<uint4*>(out + g * 480);
+      for (int c = lane; c < 60; c += 32) dst[c] = src[c];
     }
     tc_fence_before();
     // TMEM and the tile are reused by the next tile; a wait that ran out anywhere ends the loop
