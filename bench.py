@@ -137,6 +137,7 @@ KERNEL_OF = {
     "dlrm_bot": "mlp_stream_kernel", "nerf": "mlp_stream_kernel", "gc_edge": "mlp_stream_pair_kernel",
     "bert_ffn": "mlp_gemm_pair_kernel", "dlrm_top": "mlp_gemm_pair_kernel",
     "bert_addln": "mlp_stream_kernel", "dlrm_interact": "dlrm_interaction_kernel",
+    "nerf_full": "mlp_stream_kernel (trunk, alpha and rgb launches)",
 }
 
 

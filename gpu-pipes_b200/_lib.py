@@ -55,6 +55,7 @@ EXPORTED_SYMBOLS = (
     "gp_dlrm_topmlp_out",
     "gp_nerf_a_out",
     "gp_nerf_out",
+    "gp_nerf_full_out",
     "gp_gc_edges_bf16_noalloc_out",
     "gp_last_error",
     "gp_device_status",
@@ -114,6 +115,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_bert_ffn_out.restype = _INT
     lib.gp_bert_addln_ffn_out.argtypes = [_I64] + [_P] * 14
     lib.gp_bert_addln_ffn_out.restype = _INT
+    lib.gp_nerf_full_out.argtypes = [_I64, _P, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P, _P]
+    lib.gp_nerf_full_out.restype = _INT
     lib.gp_dlrm_interaction_out.argtypes = [_I64, _P, _P, _P, _P]
     lib.gp_dlrm_interaction_out.restype = _INT
     lib.gp_dlrm_topmlp_out.argtypes = [_I64, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P]

@@ -14,6 +14,8 @@ struct LaunchCtx {
   int64_t m;
   const void* x;
   void* out;
+  int64_t x_ld = 0;    // row strides in elements (0 = contiguous rows); stream chains only
+  int64_t out_ld = 0;
   const void* w[kMaxLayers];
   cudaStream_t stream;
   int sm_count;
@@ -40,10 +42,14 @@ void set_kernel_variant(int v);
 // helpers implemented in gp_abi.cu
 int set_error(int code, const char* fmt, ...);
 // swizzle_bytes: 128, 64, 32 or 0 (none)
+// ld: row stride in elements (0 = cols, a contiguous matrix)
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
-                 uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
+                 uint32_t box_cols, uint32_t box_rows, int swizzle_bytes, uint64_t ld = 0);
 int make_tmap_2d_f32(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
                      uint32_t box_rows, int swizzle_bytes);
+// NeRF with view directions (inst_stream.cu): three chain launches sharing a workspace
+int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void* d,
+                     const void* const* w, const void* const* b, void* out_r, void* out_rgb);
 // DLRM feature interaction (dlrm_interaction.cu): bot [m, 128], sparse [m, 26, 128] -> out [m, 480]
 int launch_dlrm_interaction(int64_t m, const void* bot, const void* sparse, void* out,
                             cudaStream_t stream, int sm_count, int* status,

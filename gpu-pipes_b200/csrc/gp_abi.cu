@@ -107,7 +107,7 @@ static int get_device_state(DeviceState** out) {
 // 2-D tensor map over a row-major [rows, cols] 16-bit matrix, box [box_rows, box_cols], the given
 // swizzle, zero fill outside the tensor.
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
-                 uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
+                 uint32_t box_cols, uint32_t box_rows, int swizzle_bytes, uint64_t ld) {
   const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                 : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
@@ -115,7 +115,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, u
   const CUtensorMapDataType dt =
       dtype == GP_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * 2};
+  cuuint64_t strides[1] = {(ld != 0 ? ld : cols) * 2};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -534,6 +534,43 @@ int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* cons
   if (w == nullptr) return set_error(GP_ERR_ARG, "w is NULL");
   gp_mlp_spec s = nerf_spec(true);
   return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
+}
+
+// NeRF with view directions (apps/nerf_full/pipelined/nerf_full_pl_ext.cu:22-95): x [m, 64],
+// d [m, 32] -> out_r [m, 64] = encoded w9 + b9, out_rgb [m, 64] = ReLU([encoded w10 + b10 | d]
+// w11 + b11) w12 + b12. fp16. w[0..11] / b[0..11] are the reference's w1..w12 / b1..b12 (b may
+// be NULL, or hold NULL entries).
+int gp_nerf_full_out(int64_t m, const void* x, const void* d, const void* const* w,
+                     const void* const* b, void* out_r, void* out_rgb, void* stream) {
+  clear_error();
+  if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
+  if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
+  if (m == 0) return GP_OK;
+  if (x == nullptr || d == nullptr || w == nullptr || out_r == nullptr || out_rgb == nullptr)
+    return set_error(GP_ERR_ARG, "x, d, w, out_r and out_rgb must not be NULL");
+  const void* bb[12] = {nullptr};
+  for (int i = 0; i < 12; ++i) {
+    if (w[i] == nullptr) return set_error(GP_ERR_ARG, "w[%d] is NULL", i);
+    if (!aligned(w[i], 16)) return set_error(GP_ERR_ALIGN, "w[%d] must be 16-byte aligned", i);
+    bb[i] = b != nullptr ? b[i] : nullptr;
+    if (bb[i] != nullptr && !aligned(bb[i], 16)) return set_error(GP_ERR_ALIGN, "b[%d] must be 16-byte aligned", i);
+  }
+  if (!aligned(x, 16) || !aligned(d, 16) || !aligned(out_r, 16) || !aligned(out_rgb, 16))
+    return set_error(GP_ERR_ALIGN, "x, d, out_r and out_rgb must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != GP_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchCtx c{};
+  c.stream = s;
+  c.sm_count = st->sm_count;
+  c.args.status = st->status;
+  c.args.timeout_ns = g_timeout_ns.load();
+  c.args.inject = g_inject.load();
+  rc = launch_nerf_full(c, m, x, d, w, bb, out_r, out_rgb);
+  if (rc != GP_OK) return rc;
+  g_launches.fetch_add(3, std::memory_order_relaxed);  // weight staging + trunk + alpha + rgb
+  return finish_launch(s, 1);
 }
 
 int gp_testmlp_out(int64_t m, const void* x, const void* w1, const void* b1, const void* w2,

@@ -87,6 +87,129 @@ int launch_ffn_resln_bf16_h128(const LaunchCtx& c) {
   return launch_stream<ChainFfnResLn<__nv_bfloat16>>(c);
 }
 
+// NeRF with view directions (apps/nerf_full, model.py:40-64 with use_viewdirs=True; the
+// reference's pipelined shapes, nerf_full_pl_ext.cu:24-68): x [M, 64], d [M, 32]; trunk w1..w8
+// (w6 [320, 256] reads [h | x]); alpha w9 [256, 64]; bottleneck w10 [256, 256];
+// rgb w11 [288, 128] reads [bottleneck | d], w12 [128, 64]. Three chain launches:
+//   trunk  x -> encoded, stored in columns 0..255 of a [M, 384] buffer E
+//   alpha  encoded (E, row stride 384) -> out_r [M, 64]
+//   rgb    E = [encoded | d | 0] (384) -> 384 -> 128 (ReLU) -> 128 -> out_rgb (first 64 columns)
+// The rgb chain's first layer carries the bottleneck in its first 256 columns and a 32 x 32
+// identity that passes d through unchanged (x 1.0, exact) to columns 256..287, so the concat
+// [bottleneck | d] is simply its output; w11 is zero-padded to 384 rows, w12 to 128 columns.
+struct ChainNerfAlpha {
+  using T = __half;
+  static constexpr int NL = 1;
+  __host__ __device__ static constexpr int K(int) { return 256; }
+  __host__ __device__ static constexpr int N(int) { return 64; }
+  __host__ __device__ static constexpr int ACT(int) { return kActNone; }
+  static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 1;
+  static constexpr bool SPLIT_ACT = false;
+};
+
+struct ChainNerfRgb {
+  using T = __half;
+  static constexpr int NL = 3;
+  __host__ __device__ static constexpr int K(int l) { return l == 2 ? 128 : 384; }
+  __host__ __device__ static constexpr int N(int l) { return l == 0 ? 384 : 128; }
+  __host__ __device__ static constexpr int ACT(int l) { return l == 1 ? kActRelu : kActNone; }
+  static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 2;
+  static constexpr bool SPLIT_ACT = false;
+};
+
+__global__ void nerf_identity_block_kernel(__half* w0p) {  // w0p [384, 384]: 1.0 at (256 + i, 256 + i)
+  const int i = threadIdx.x;
+  if (i < 32) w0p[(256 + i) * 384 + 256 + i] = __float2half_rn(1.0f);
+}
+
+int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void* d,
+                     const void* const* w, const void* const* b, void* out_r, void* out_rgb) {
+  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+  const size_t e_bytes = al(size_t(m) * 384 * 2), w0_bytes = al(384 * 384 * 2), b0_bytes = al(384 * 2);
+  const size_t w1_bytes = al(384 * 128 * 2), w2_bytes = al(128 * 128 * 2), b2_bytes = al(128 * 2);
+  const size_t t_bytes = al(size_t(m) * 128 * 2);
+  void* ws = nullptr;
+  const cudaStream_t s = base.stream;
+  int rc = workspace_acquire(e_bytes + w0_bytes + b0_bytes + w1_bytes + w2_bytes + b2_bytes + t_bytes, s, &ws);
+  if (rc != GP_OK) return rc;
+  char* p = static_cast<char*>(ws);
+  __half* E = reinterpret_cast<__half*>(p);
+  char* w0p = p + e_bytes;
+  char* b0p = w0p + w0_bytes;
+  char* w1p = b0p + b0_bytes;
+  char* w2p = w1p + w1_bytes;
+  char* b2p = w2p + w2_bytes;
+  char* tmp = b2p + b2_bytes;
+  cudaError_t e = cudaSuccess;
+  auto ck = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
+  // augmented weights of the rgb chain
+  ck(cudaMemsetAsync(w0p, 0, w0_bytes + b0_bytes + w1_bytes + w2_bytes + b2_bytes, s));
+  ck(cudaMemcpy2DAsync(w0p, 384 * 2, w[9], 256 * 2, 256 * 2, 256, cudaMemcpyDeviceToDevice, s));
+  nerf_identity_block_kernel<<<1, 32, 0, s>>>(reinterpret_cast<__half*>(w0p));
+  if (b[9] != nullptr) ck(cudaMemcpyAsync(b0p, b[9], 256 * 2, cudaMemcpyDeviceToDevice, s));
+  ck(cudaMemcpyAsync(w1p, w[10], 288 * 128 * 2, cudaMemcpyDeviceToDevice, s));
+  ck(cudaMemcpy2DAsync(w2p, 128 * 2, w[11], 64 * 2, 64 * 2, 128, cudaMemcpyDeviceToDevice, s));
+  if (b[11] != nullptr) ck(cudaMemcpyAsync(b2p, b[11], 64 * 2, cudaMemcpyDeviceToDevice, s));
+  // E = [encoded | d | 0]: d into columns 256..287, zeros into 288..383 (encoded by the trunk)
+  ck(cudaMemcpy2DAsync(E + 256, 384 * 2, d, 32 * 2, 32 * 2, m, cudaMemcpyDeviceToDevice, s));
+  ck(cudaMemset2DAsync(E + 288, 384 * 2, 0, 96 * 2, m, s));
+  if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "nerf_full staging: %s", cudaGetErrorString(e));
+
+  gp_mlp_spec spec{};
+  spec.dtype = GP_F16;
+  LaunchCtx t = base;
+  t.spec = &spec;
+  t.m = m;
+  t.args.m = m;
+  t.args.num_tiles = static_cast<int>((m + kBM - 1) / kBM);
+  for (int l = 0; l < kMaxLayers; ++l) t.args.bias[l] = nullptr;
+  if (rc == GP_OK) {  // trunk: x -> E[:, 0:256]
+    t.x = x;
+    t.x_ld = 0;
+    t.out = E;
+    t.out_ld = 384;
+    for (int l = 0; l < 8; ++l) {
+      t.w[l] = w[l];
+      t.args.bias[l] = b[l];
+    }
+    t.args.out = t.out;
+    rc = launch_stream<ChainNerfTrunk>(t);
+  }
+  if (rc == GP_OK) {  // alpha: encoded -> out_r
+    t.x = E;
+    t.x_ld = 384;
+    t.out = out_r;
+    t.out_ld = 0;
+    t.w[0] = w[8];
+    t.args.bias[0] = b[8];
+    t.args.out = t.out;
+    rc = launch_stream<ChainNerfAlpha>(t);
+  }
+  if (rc == GP_OK) {  // rgb: [encoded | d | 0] -> tmp
+    t.x = E;
+    t.x_ld = 0;
+    t.out = tmp;
+    t.w[0] = w0p;
+    t.w[1] = w1p;
+    t.w[2] = w2p;
+    t.args.bias[0] = b0p;
+    t.args.bias[1] = b[10];
+    t.args.bias[2] = b2p;
+    t.args.out = t.out;
+    rc = launch_stream<ChainNerfRgb>(t);
+  }
+  if (rc == GP_OK) {
+    e = cudaMemcpy2DAsync(out_rgb, 64 * 2, tmp, 128 * 2, 64 * 2, m, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "nerf_full output copy: %s", cudaGetErrorString(e));
+  }
+  workspace_release(s);
+  return rc;
+}
+
 int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot>(c); }
 int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>, 2>(c); }
 int launch_gc_relu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActRelu>, 2>(c); }

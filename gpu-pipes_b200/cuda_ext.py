@@ -203,6 +203,53 @@ def nerf_out(x, weights, biases, out) -> None:
                   skip_layer=5)
 
 
+_NERF_FULL_W = [(64, 256)] + [(256, 256)] * 4 + [(320, 256), (256, 256), (256, 256),
+                (256, 64), (256, 256), (288, 128), (128, 64)]
+
+
+def nerf_full_out(x, d, weights, biases, out_r, out_rgb) -> None:
+    """NeRF with view directions (apps/nerf_full/pipelined/nerf_full_pl_ext.cu:22-95): x [M, 64],
+    d [M, 32], weights w1..w12 ([K, N], shapes as the reference asserts), biases b1..b12 (entries
+    may be None) -> out_r [M, 64] (alpha head), out_rgb [M, 64]. fp16."""
+    _check_input("x", x, torch.float16)
+    _check_input("d", d, torch.float16)
+    _check_input("out_r", out_r, torch.float16)
+    _check_input("out_rgb", out_rgb, torch.float16)
+    m = x.shape[0]
+    if x.dim() != 2 or x.shape[1] != 64:
+        raise RuntimeError(f"x has shape {tuple(x.shape)}, expected [M, 64]")
+    if tuple(d.shape) != (m, 32):
+        raise RuntimeError(f"d has shape {tuple(d.shape)}, expected [{m}, 32]")
+    for name, o in (("out_r", out_r), ("out_rgb", out_rgb)):
+        if tuple(o.shape) != (m, 64):
+            raise RuntimeError(f"{name} has shape {tuple(o.shape)}, expected [{m}, 64]")
+    weights, biases = list(weights), list(biases) if biases is not None else [None] * 12
+    if len(weights) != 12 or len(biases) != 12:
+        raise RuntimeError("nerf_full takes 12 weights and 12 biases")
+    for i, (wt, bt) in enumerate(zip(weights, biases)):
+        _check_input(f"w{i + 1}", wt, torch.float16)
+        _check_input(f"b{i + 1}", bt, torch.float16)
+        if tuple(wt.shape) != _NERF_FULL_W[i]:
+            raise RuntimeError(f"w{i + 1} has shape {tuple(wt.shape)}, expected {_NERF_FULL_W[i]}")
+        if bt is not None and tuple(bt.shape) != (_NERF_FULL_W[i][1],):
+            raise RuntimeError(f"b{i + 1} has shape {tuple(bt.shape)}, expected ({_NERF_FULL_W[i][1]},)")
+    wp = (ctypes.c_void_p * 12)(*[wt.data_ptr() for wt in weights])
+    bp = (ctypes.c_void_p * 12)(*[None if bt is None else bt.data_ptr() for bt in biases])
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_nerf_full_out(m, _ptr(x), _ptr(d), wp, bp, _ptr(out_r), _ptr(out_rgb),
+                                         _stream(x)))
+
+
+def nerf_full(x, d, *wb):
+    """nerf_full(x, d, w1, b1, ..., w12, b12) -> (out_r, out_rgb), like the reference's binding."""
+    if len(wb) != 24:
+        raise RuntimeError("nerf_full takes x, d and 12 (weight, bias) pairs")
+    out_r = torch.zeros(x.shape[0], 64, dtype=x.dtype, device=x.device)
+    out_rgb = torch.zeros_like(out_r)
+    nerf_full_out(x, d, wb[0::2], wb[1::2], out_r, out_rgb)
+    return out_r, out_rgb
+
+
 def bert_ffn_out(x, w1, b1, w2, b2, ga, be, out, eps=None) -> None:
     """out = LN(x + W2 act(W1 x + b1) + b2).
 
@@ -295,6 +342,12 @@ def run_workload_out(w, x, weights, ln, out) -> None:
     if w.block == "dlrm_interaction":
         m = x.shape[0] // 27
         dlrm_interaction_out(x[:m], x[m:].view(m, 26, x.shape[1]), out)
+        return
+    if w.block == "nerf_full":
+        m = x.numel() // 96
+        o = out.view(-1)
+        nerf_full_out(x[:m * 64].view(m, 64), x[m * 64:].view(m, 32), [p[0] for p in weights],
+                      [p[1] for p in weights], o[:m * 64].view(m, 64), o[m * 64:].view(m, 64))
         return
     if w.block == "bert_addln":
         m = x.shape[0] // 2

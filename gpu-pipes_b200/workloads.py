@@ -50,7 +50,10 @@ class Workload:
     block: str = ""               # "" = one chain; "bert_addln" = attention-output Linear + x +
                                   # LN0, then the FFN chain (inputs: attn_out rows, then x rows);
                                   # "dlrm_interaction" = the DLRM feature interaction (inputs: m
-                                  # bottom-output rows, then 26 m embedding rows; no layers)
+                                  # bottom-output rows, then 26 m embedding rows; no layers);
+                                  # "nerf_full" = NeRF with view directions (input: one flat
+                                  # tensor, m x-rows of 64 then m d-rows of 32; output [m, 128]
+                                  # holding out_r [m, 64] then out_rgb [m, 64] in memory order)
     description: str = ""
 
     @property
@@ -59,6 +62,8 @@ class Workload:
 
     @property
     def n_out(self) -> int:
+        if self.block == "nerf_full":
+            return 128
         return 480 if self.block == "dlrm_interaction" else self.layers[-1].n
 
     @property
@@ -84,6 +89,8 @@ class Workload:
         """Stored input bytes per row / 2 (attn_out and x for the bert_addln block)."""
         if self.block == "dlrm_interaction":
             return 27 * 128
+        if self.block.startswith("nerf_full"):
+            return 96
         return 2 * self.k0 if self.block == "bert_addln" else self.k0
 
     @property
@@ -193,14 +200,31 @@ DLRM_INTERACT = Workload(
     layers=(Layer(128, 480, _N, 128, 480),), input_logical=128,
     description="DLRM interaction: [bot; 26 embeddings] (27 x 128) -> bot | 351 dot products | 0 (480), fp16")
 
+# NeRF with view directions (apps/nerf_full, model.py:40-64 with use_viewdirs=True) at the
+# reference's pipelined shapes (nerf_full_pl_ext.cu:54-66: x 64, d 32, alpha and rgb padded to
+# 64): trunk as NERF, alpha 256 -> 64, bottleneck 256 -> 256, rgb [bottleneck | d] 288 -> 128 ReLU
+# -> 64. x is the 63-feature positional encoding (padded to 64); d the 27-feature encoding of a
+# unit view direction (direction + 4 octaves of sin/cos), padded to 32. Layer list = w1..w12.
+NERF_FULL = Workload(
+    name="nerf_full", m=1048576, dtype=torch.float16, seed=8, input_kind="nerf_posenc",
+    input_logical=63, skip_layer=5, block="nerf_full",
+    layers=(Layer(64, 256, _R, 63, 256),) + tuple(Layer(256, 256, _R, 256, 256) for _ in range(4)) +
+           (Layer(320, 256, _R, 319, 256), Layer(256, 256, _R, 256, 256), Layer(256, 256, _R, 256, 256),
+            Layer(256, 64, _N, 256, 64), Layer(256, 256, _N, 256, 256), Layer(288, 128, _R, 283, 128),
+            Layer(128, 64, _N, 128, 64)),
+    description="NeRF with view directions: trunk 63(64)->256 x8 (skip), alpha 256->64, "
+                "bottleneck 256->256, rgb [256 | d 27(32)] -> 128 ReLU -> 64, fp16")
+
 WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF,
-                                 BERT_FFN, DLRM_TOP, BERT_ADDLN, DLRM_INTERACT)}
+                                 BERT_FFN, DLRM_TOP, BERT_ADDLN, DLRM_INTERACT, NERF_FULL)}
 
 
 def rows_of(w: Workload, x: torch.Tensor) -> int:
     """Rows of workload input `x` (the bert_addln block stacks attn_out rows over x rows)."""
     if w.block == "dlrm_interaction":
         return x.shape[0] // 27
+    if w.block == "nerf_full":
+        return x.numel() // 96
     return x.shape[0] // 2 if w.block == "bert_addln" else x.shape[0]
 
 
@@ -273,6 +297,14 @@ def make_input_chunk(w: Workload, chunk: int, rows: int | None = None) -> torch.
     elif w.input_kind == "dlrm_dense":
         # log1p of Exp(1) draws (DLRM's dense-feature transform)
         x = torch.log1p(torch.empty(rows, w.k0).exponential_(1.0, generator=g))
+    elif w.input_kind == "nerf_posenc" and w.block.startswith("nerf_full"):
+        x = _nerf_posenc(torch.rand(rows, 3, generator=g) * 2 - 1, 10, 64)
+        v = torch.randn(rows, 3, generator=_gen(w.seed, 2, chunk))
+        d = _nerf_posenc(v / v.norm(dim=1, keepdim=True).clamp_min(1e-6), 4, 32)
+        xd = torch.cat([x, d], dim=1).to(w.dtype)  # [rows, 96]
+        if w.block == "nerf_full":
+            return torch.cat([xd[:, :64].reshape(-1), xd[:, 64:].reshape(-1)])
+        return xd
     elif w.input_kind == "nerf_posenc":
         # gamma(p) = [p, sin(2^k pi p), cos(2^k pi p)]_{k=0..9} for xyz ~ U(-1, 1)
         p = torch.rand(rows, 3, generator=g) * 2 - 1
@@ -286,6 +318,17 @@ def make_input_chunk(w: Workload, chunk: int, rows: int | None = None) -> torch.
     if w.input_logical < w.k0:
         x[:, w.input_logical:] = 0
     return x.to(w.dtype)
+
+
+def _nerf_posenc(p: torch.Tensor, octaves: int, width: int) -> torch.Tensor:
+    """[p, sin(2^k pi p), cos(2^k pi p)]_{k < octaves}, zero-padded to `width` columns."""
+    feats = [p]
+    for k in range(octaves):
+        feats += [torch.sin((2.0 ** k) * math.pi * p), torch.cos((2.0 ** k) * math.pi * p)]
+    f = torch.cat(feats, dim=1)
+    out = torch.zeros(p.shape[0], width)
+    out[:, :f.shape[1]] = f
+    return out
 
 
 def make_input(w: Workload, row0: int = 0, rows: int | None = None,
@@ -327,8 +370,15 @@ def make_input(w: Workload, row0: int = 0, rows: int | None = None,
             out.copy_(res)
             return out
         return res
+    if w.block == "nerf_full":
+        res = make_input(Workload(**{**w.__dict__, "block": "nerf_full_rows"}), row0, rows)
+        flat = torch.cat([res[:, :64].reshape(-1), res[:, 64:].reshape(-1)])
+        if out is not None:
+            out.copy_(flat)
+            return out
+        return flat
     if out is None:
-        out = torch.empty(rows, w.k0, dtype=w.dtype)
+        out = torch.empty(rows, w.in_width if w.block == "nerf_full_rows" else w.k0, dtype=w.dtype)
     r = row0
     while r < row0 + rows:
         c = r // CHUNK_ROWS

@@ -180,6 +180,20 @@ GP_API int gp_nerf_a_out(int64_t m, const void* x, const void* const* w, const v
 GP_API int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* const* b,
                 void* out, void* stream);
 
+/* NeRF with view directions (apps/nerf_full/torch/model.py:5-66, use_viewdirs = True, with the
+ * reference's pipelined shapes: radiance and rgb widths padded to 64). Replaces nerf_full_out
+ * (apps/nerf_full/pipelined/nerf_full_pl_ext.cu:22-95). fp16.
+ *   x [m, 64], d [m, 32]; w[12], b[12] = the reference's w1..w12, b1..b12:
+ *   trunk w1..w8 as gp_nerf_a_out -> encoded [m, 256]
+ *   out_r   [m, 64] = encoded w9 + b9                                   (w9  [256, 64])
+ *   out_rgb [m, 64] = ReLU([encoded w10 + b10 | d] w11 + b11) w12 + b12 (w10 [256, 256],
+ *                                                     w11 [288, 128], w12 [128, 64])
+ * The ReLU after w11 follows model.py:47-50 and the reference's bulk-synchronous kernel; the
+ * reference's pipelined kernel omits it. b may be NULL or hold NULL entries (no bias). Uses the
+ * per-device workspace ([m, 384] fp16 plus the padded rgb weights). */
+GP_API int gp_nerf_full_out(int64_t m, const void* x, const void* d, const void* const* w,
+                     const void* const* b, void* out_r, void* out_rgb, void* stream);
+
 /* GraphCast edge MLP in bf16 (as gp_gc_edges_out with dtype GP_BF16, act GP_ACT_RELU or
  * GP_ACT_SILU) for callers that cannot allocate GPU memory during a call: frameworks that own
  * every device allocation, or serving loops that must never enter an allocator. It allocates

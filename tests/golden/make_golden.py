@@ -166,6 +166,7 @@ def main() -> None:
           x=_u16(x), y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
 
     gen_bert_addln(ref, rows)
+    gen_nerf_full(ref, rows)
 
     # ---- known-answer LayerNorm row from misc_tests/layer_norm/torch_val.py:87-116
     src = (ref / "misc_tests/layer_norm/torch_val.py").read_text()
@@ -203,6 +204,33 @@ def gen_bert_addln(ref: Path, rows: int = 48) -> None:
         y = net(attn.float(), x.float())
     _save("bert_addln_ffn_128", seed=np.int64(seed), attn=_u16(attn), x=_u16(x),
           y=y.numpy().astype(np.float32), wsum=np.float64(checksum(layers)), **lnp)
+
+
+def gen_nerf_full(ref: Path, rows: int = 48) -> None:
+    """Nerf of apps/nerf_full/torch/model.py:5-66 with view directions, built the way the
+    reference's own check builds it (apps/nerf_full/pipelined/val.py:10: Nerf(64, 32,
+    radiance_dim=64, rgb_dim=64)); x and d from randn, as there."""
+    nf = _load(ref, "apps/nerf_full/torch/model.py", "ref_nerf_full")
+    seed = 71
+    net = nf.Nerf(64, 32, radiance_dim=64, rgb_dim=64).eval()
+    lins = [m for m in list(net.preskip) + list(net.postskip) if isinstance(m, torch.nn.Linear)]
+    lins += [net.alpha, net.bottleneck, net.rgb[0], net.rgb[2]]
+    dims_in = [lin.in_features for lin in lins]
+    dims_out = [lin.out_features for lin in lins]
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for lin, k, n in zip(lins, dims_in, dims_out):
+        p = layer_params(int(torch.randint(0, 2**31 - 1, (1,), generator=g)), [k, n])[0]
+        layers.append(p)
+        _set_linear(lin, *p)
+    gx = torch.Generator().manual_seed(seed + 100)
+    x = torch.randn(rows, 64, generator=gx).half()
+    d = torch.randn(rows, 32, generator=gx).half()
+    with torch.no_grad():
+        rgb, alpha = net(x.float(), d.float())
+    _save("nerf_full_viewdirs", seed=np.int64(seed), dims_in=np.array(dims_in),
+          dims_out=np.array(dims_out), x=_u16(x), d=_u16(d), rgb=rgb.numpy().astype(np.float32),
+          alpha=alpha.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
 
 
 if __name__ == "__main__":

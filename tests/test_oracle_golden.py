@@ -80,6 +80,29 @@ def test_nerf_matches_reference_model():
     torch.testing.assert_close(y, torch.from_numpy(g["y"]), **TOL)
 
 
+def _nerf_full_layers(g):
+    gen = torch.Generator().manual_seed(int(g["seed"]))
+    layers = []
+    for k, n in zip(g["dims_in"], g["dims_out"]):
+        s = int(torch.randint(0, 2**31 - 1, (1,), generator=gen))
+        layers.append(layer_params(s, [int(k), int(n)])[0])
+    return layers
+
+
+def test_nerf_full_matches_reference_model():
+    """Nerf(64, 32, radiance_dim=64, rgb_dim=64) with view directions, as
+    apps/nerf_full/pipelined/val.py:10 builds it."""
+    g = load_golden("nerf_full_viewdirs")
+    layers = _nerf_full_layers(g)
+    assert [tuple(w.shape) for w, _ in layers] == [
+        (64, 256), (256, 256), (256, 256), (256, 256), (256, 256), (320, 256), (256, 256),
+        (256, 256), (256, 64), (256, 256), (288, 128), (128, 64)]
+    assert abs(checksum(layers) - float(g["wsum"])) < 1e-6
+    alpha, rgb = O.nerf_full(u16_to(g["x"], torch.float16), u16_to(g["d"], torch.float16), layers)
+    torch.testing.assert_close(alpha, torch.from_numpy(g["alpha"]), **TOL)
+    torch.testing.assert_close(rgb, torch.from_numpy(g["rgb"]), **TOL)
+
+
 def test_layernorm_known_row():
     """misc_tests/layer_norm/torch_val.py:87-116: one 128-value row, gamma=1, beta=0."""
     g = load_golden("ln_known_row")
