@@ -569,7 +569,7 @@ int gp_nerf_full_out(int64_t m, const void* x, const void* d, const void* const*
   c.args.inject = g_inject.load();
   rc = launch_nerf_full(c, m, x, d, w, bb, out_r, out_rgb);
   if (rc != GP_OK) return rc;
-  g_launches.fetch_add(3, std::memory_order_relaxed);  // weight staging + trunk + alpha + rgb
+  g_launches.fetch_add(4, std::memory_order_relaxed);  // identity, staging, trunk, alpha, rgb
   return finish_launch(s, 1);
 }
 

@@ -93,7 +93,8 @@ int launch_ffn_resln_bf16_h128(const LaunchCtx& c) {
 // rgb w11 [288, 128] reads [bottleneck | d], w12 [128, 64]. Three chain launches:
 //   trunk  x -> encoded, stored in columns 0..255 of a [M, 384] buffer E
 //   alpha  encoded (E, row stride 384) -> out_r [M, 64]
-//   rgb    E = [encoded | d | 0] (384) -> 384 -> 128 (ReLU) -> 128 -> out_rgb (first 64 columns)
+//   rgb    E = [encoded | d | 0] (384) -> 384 -> 128 (ReLU) -> 128, of which the first 64
+//          columns are stored to out_rgb
 // The rgb chain's first layer carries the bottleneck in its first 256 columns and a 32 x 32
 // identity that passes d through unchanged (x 1.0, exact) to columns 256..287, so the concat
 // [bottleneck | d] is simply its output; w11 is zero-padded to 384 rows, w12 to 128 columns.
@@ -119,7 +120,19 @@ struct ChainNerfRgb {
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 2;
   static constexpr bool SPLIT_ACT = false;
+  static constexpr int OUT_N = 64;
 };
+
+// E[:, 256:384] = [d | 0] with 16-byte loads and stores (16 per row: 4 carry d, 12 zeros).
+__global__ void nerf_stage_d_kernel(const uint4* __restrict__ d, uint4* __restrict__ e, int64_t m) {
+  const int64_t n = m * 16;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i >> 4;
+    const int c = static_cast<int>(i & 15);
+    e[row * 48 + 32 + c] = c < 4 ? __ldg(d + row * 4 + c) : make_uint4(0, 0, 0, 0);
+  }
+}
 
 __global__ void nerf_identity_block_kernel(__half* w0p) {  // w0p [384, 384]: 1.0 at (256 + i, 256 + i)
   const int i = threadIdx.x;
@@ -131,10 +144,9 @@ int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void
   auto al = [](size_t v) { return (v + 255) / 256 * 256; };
   const size_t e_bytes = al(size_t(m) * 384 * 2), w0_bytes = al(384 * 384 * 2), b0_bytes = al(384 * 2);
   const size_t w1_bytes = al(384 * 128 * 2), w2_bytes = al(128 * 128 * 2), b2_bytes = al(128 * 2);
-  const size_t t_bytes = al(size_t(m) * 128 * 2);
   void* ws = nullptr;
   const cudaStream_t s = base.stream;
-  int rc = workspace_acquire(e_bytes + w0_bytes + b0_bytes + w1_bytes + w2_bytes + b2_bytes + t_bytes, s, &ws);
+  int rc = workspace_acquire(e_bytes + w0_bytes + b0_bytes + w1_bytes + w2_bytes + b2_bytes, s, &ws);
   if (rc != GP_OK) return rc;
   char* p = static_cast<char*>(ws);
   __half* E = reinterpret_cast<__half*>(p);
@@ -143,7 +155,6 @@ int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void
   char* w1p = b0p + b0_bytes;
   char* w2p = w1p + w1_bytes;
   char* b2p = w2p + w2_bytes;
-  char* tmp = b2p + b2_bytes;
   cudaError_t e = cudaSuccess;
   auto ck = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
   // augmented weights of the rgb chain
@@ -155,8 +166,11 @@ int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void
   ck(cudaMemcpy2DAsync(w2p, 128 * 2, w[11], 64 * 2, 64 * 2, 128, cudaMemcpyDeviceToDevice, s));
   if (b[11] != nullptr) ck(cudaMemcpyAsync(b2p, b[11], 64 * 2, cudaMemcpyDeviceToDevice, s));
   // E = [encoded | d | 0]: d into columns 256..287, zeros into 288..383 (encoded by the trunk)
-  ck(cudaMemcpy2DAsync(E + 256, 384 * 2, d, 32 * 2, 32 * 2, m, cudaMemcpyDeviceToDevice, s));
-  ck(cudaMemset2DAsync(E + 288, 384 * 2, 0, 96 * 2, m, s));
+  {
+    const int64_t want = (m * 16 + 255) / 256;
+    const int blocks = static_cast<int>(want < 8 * base.sm_count ? want : 8 * base.sm_count);
+    nerf_stage_d_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(d), reinterpret_cast<uint4*>(E), m);
+  }
   if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "nerf_full staging: %s", cudaGetErrorString(e));
 
   gp_mlp_spec spec{};
@@ -189,10 +203,10 @@ int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void
     t.args.out = t.out;
     rc = launch_stream<ChainNerfAlpha>(t);
   }
-  if (rc == GP_OK) {  // rgb: [encoded | d | 0] -> tmp
+  if (rc == GP_OK) {  // rgb: [encoded | d | 0] -> out_rgb
     t.x = E;
     t.x_ld = 0;
-    t.out = tmp;
+    t.out = out_rgb;
     t.w[0] = w0p;
     t.w[1] = w1p;
     t.w[2] = w2p;
@@ -201,10 +215,6 @@ int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void
     t.args.bias[2] = b2p;
     t.args.out = t.out;
     rc = launch_stream<ChainNerfRgb>(t);
-  }
-  if (rc == GP_OK) {
-    e = cudaMemcpy2DAsync(out_rgb, 64 * 2, tmp, 128 * 2, 64 * 2, m, cudaMemcpyDeviceToDevice, s);
-    if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "nerf_full output copy: %s", cudaGetErrorString(e));
   }
   workspace_release(s);
   return rc;

@@ -46,11 +46,24 @@ constexpr int kTailHead = 3;  // narrow output layer on CUDA cores (stream kerne
 //   HIDDEN_F16: with bf16 data, keep hidden activations in fp16 (11-bit mantissa instead of 8)
 //   and run layers >= 1 as fp16 x fp16 MMAs on fp16 copies of their weights (bf16 -> fp16 is
 //   exact for weights within fp16 range). Input, first layer and output stay bf16.
+//   OUT_N (optional): stored output columns, a multiple of 32 not above N_last (default N_last);
+//   the columns beyond it are computed and dropped, the output rows are OUT_N wide.
+template <class C, class = void>
+struct OutCols {
+  static constexpr int value = C::N(C::NL - 1);
+};
+template <class C>
+struct OutCols<C, std::void_t<decltype(C::OUT_N)>> {
+  static constexpr int value = C::OUT_N;
+};
+
 template <class C, int CG = 1>
 struct StreamLayout {
   static constexpr int NL = C::NL;
   static constexpr int K0 = C::K(0);
   static constexpr bool kXRes = K0 <= kPanel;  // whole x tile resident (one 64-column panel)
+  static constexpr int kOutN = OutCols<C>::value;
+  static_assert(kOutN % 32 == 0 && kOutN <= C::N(C::NL - 1), "OUT_N");
   __host__ __device__ static constexpr int maxN() {
     int m = 0;
     for (int l = 0; l < NL; ++l) m = C::N(l) > m ? C::N(l) : m;
@@ -564,7 +577,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        if (row0 < args.m) tma_store_2d(&tm.out, smem_u32(s), c * 32, row0);
+        if (row0 < args.m && c * 32 < L::kOutN) tma_store_2d(&tm.out, smem_u32(s), c * 32, row0);
         bulk_commit_group();
       }
       if constexpr (L::kStgInAct) sb ^= 1;

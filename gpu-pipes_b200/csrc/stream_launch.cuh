@@ -35,7 +35,7 @@ int launch_stream(const LaunchCtx& c) {
   std::memset(&tm, 0, sizeof(tm));
   rc = make_tmap_2d(&tm.x, c.x, dt, c.m, C::K(0), kPanel, kBM, 128, c.x_ld);
   if (rc == GP_OK && C::TAIL != kTailHead)
-    rc = make_tmap_2d(&tm.out, c.out, dt, c.m, C::N(C::NL - 1), 32, 32, 64, c.out_ld);
+    rc = make_tmap_2d(&tm.out, c.out, dt, c.m, L::kOutN, 32, 32, 64, c.out_ld);
   // fp16 copies of the weights of layers >= 1 (HIDDEN_F16), in the per-device workspace
   void* scratch = nullptr;
   size_t offs[kMaxLayers] = {0};
