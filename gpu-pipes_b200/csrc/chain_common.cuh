@@ -24,6 +24,7 @@ struct TensorMaps {
   CUtensorMap x;                 // input rows  [M, K0]
   CUtensorMap out;               // output rows [M, N_last]
   CUtensorMap w[kMaxLayers];     // weights [K_l, N_l], row-major (N contiguous)
+  CUtensorMap x2;                // second input source (resident kernel, x mode 2)
 };
 
 struct ChainArgs {
@@ -40,6 +41,11 @@ struct ChainArgs {
   int* status;                        // device status word (0 = ok)
   unsigned long long timeout_ns;      // budget of every bounded wait
   int inject;                         // fault injection: 1 = producer never loads x
+  // MeshGraphNet edge update (resident kernel, x mode 1): x = [nodes[gidx[0]] | x | nodes[gidx[1]]]
+  const void* gnodes;                 // node rows [n_nodes, 128]
+  const int64_t* gidx[2];             // per row: source and destination node
+  int64_t n_nodes;
+  float* scatter;                     // [n_nodes, N_last] fp32, += out row at gidx[1] (or null)
 };
 
 }  // namespace gp

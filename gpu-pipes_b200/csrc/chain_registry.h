@@ -14,6 +14,7 @@ struct LaunchCtx {
   int64_t m;
   const void* x;
   void* out;
+  const void* x2 = nullptr;  // second x source (resident kernel, x mode 2)
   int64_t x_ld = 0;    // row strides in elements (0 = contiguous rows); stream chains only
   int64_t out_ld = 0;
   const void* w[kMaxLayers];
@@ -50,6 +51,16 @@ int make_tmap_2d_f32(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols,
 // NeRF with view directions (inst_stream.cu): three chain launches sharing a workspace
 int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void* d,
                      const void* const* w, const void* const* b, void* out_r, void* out_rgb);
+// MeshGraphNet edge and node updates (mgn_graph.cu). base carries stream, SM count, status and
+// timeout. Edge: out[e] = LN(MLP([nf[src[e]] | ef[e] | nf[dst[e]]])), agg[dst[e]] += out[e] when
+// agg is set. Node: out[v] = LN(MLP([nf[v] | agg_0[v] | ... ])) over n_sets fp32 aggregates.
+int launch_mgn_edge_update(const LaunchCtx& base, int64_t m, int64_t n_nodes, const void* nf,
+                           const void* ef, const int64_t* srcs, const int64_t* dsts,
+                           const void* const* w, const void* const* b, const void* gamma,
+                           const void* beta, void* out, float* agg);
+int launch_mgn_node_update(const LaunchCtx& base, int64_t n, int n_sets, const void* nf,
+                           const float* const* aggs, const void* const* w, const void* const* b,
+                           const void* gamma, const void* beta, void* out);
 // DLRM feature interaction (dlrm_interaction.cu): bot [m, 128], sparse [m, 26, 128] -> out [m, 480]
 int launch_dlrm_interaction(int64_t m, const void* bot, const void* sparse, void* out,
                             cudaStream_t stream, int sm_count, int* status,

@@ -573,6 +573,77 @@ int gp_nerf_full_out(int64_t m, const void* x, const void* d, const void* const*
   return finish_launch(s, 1);
 }
 
+// MeshGraphNet edge update with the gather fused (graphmodel/mgn_dp.py:28-32) and, when agg is
+// set, the scatter-sum of the outputs by destination node fused into the same kernel.
+int gp_mgn_edge_update_out(int64_t m, int64_t n_nodes, const void* nf, const void* ef,
+                           const int64_t* srcs, const int64_t* dsts, const void* const* w,
+                           const void* const* b, const void* gamma, const void* beta, void* out,
+                           float* agg, void* stream) {
+  clear_error();
+  if (m < 0 || n_nodes < 0) return set_error(GP_ERR_ARG, "m = %lld, n_nodes = %lld", (long long)m, (long long)n_nodes);
+  if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
+  if (m == 0) return GP_OK;
+  if (n_nodes == 0) return set_error(GP_ERR_ARG, "edges need nodes (n_nodes = 0)");
+  if (nf == nullptr || ef == nullptr || srcs == nullptr || dsts == nullptr || w == nullptr || out == nullptr)
+    return set_error(GP_ERR_ARG, "nf, ef, srcs, dsts, w and out must not be NULL");
+  for (int l = 0; l < 3; ++l) {
+    if (w[l] == nullptr || !aligned(w[l], 16)) return set_error(GP_ERR_ALIGN, "w[%d] NULL or not 16-byte aligned", l);
+    if (b != nullptr && b[l] != nullptr && !aligned(b[l], 16))
+      return set_error(GP_ERR_ALIGN, "b[%d] must be 16-byte aligned", l);
+  }
+  if (!aligned(nf, 16) || !aligned(ef, 16) || !aligned(out, 16) || !aligned(srcs, 8) || !aligned(dsts, 8) ||
+      (agg != nullptr && !aligned(agg, 16)))
+    return set_error(GP_ERR_ALIGN, "nf, ef, out and agg must be 16-byte aligned, srcs and dsts 8-byte");
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != GP_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchCtx c{};
+  c.stream = s;
+  c.sm_count = st->sm_count;
+  c.args.status = st->status;
+  c.args.timeout_ns = g_timeout_ns.load();
+  c.args.ln_eps = 1e-5f;
+  rc = launch_mgn_edge_update(c, m, n_nodes, nf, ef, srcs, dsts, w, b, gamma, beta, out, agg);
+  if (rc != GP_OK) return rc;
+  return finish_launch(s, 1);
+}
+
+// MeshGraphNet node update (graphmodel/mgn_dp.py:46-54) on [nf | aggregates of n_sets edge sets].
+int gp_mgn_node_update_out(int64_t n, int n_sets, const void* nf, const float* const* aggs,
+                           const void* const* w, const void* const* b, const void* gamma,
+                           const void* beta, void* out, void* stream) {
+  clear_error();
+  if (n < 0) return set_error(GP_ERR_ARG, "n = %lld is negative", (long long)n);
+  if (n >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "n = %lld exceeds 2^31-1", (long long)n);
+  if (n_sets != 1 && n_sets != 2) return set_error(GP_ERR_UNSUPPORTED, "n_sets = %d (1 or 2 edge sets)", n_sets);
+  if (n == 0) return GP_OK;
+  if (nf == nullptr || aggs == nullptr || w == nullptr || out == nullptr)
+    return set_error(GP_ERR_ARG, "nf, aggs, w and out must not be NULL");
+  for (int i = 0; i < n_sets; ++i)
+    if (aggs[i] == nullptr || !aligned(aggs[i], 16)) return set_error(GP_ERR_ALIGN, "aggs[%d] NULL or not 16-byte aligned", i);
+  for (int l = 0; l < 3; ++l) {
+    if (w[l] == nullptr || !aligned(w[l], 16)) return set_error(GP_ERR_ALIGN, "w[%d] NULL or not 16-byte aligned", l);
+    if (b != nullptr && b[l] != nullptr && !aligned(b[l], 16))
+      return set_error(GP_ERR_ALIGN, "b[%d] must be 16-byte aligned", l);
+  }
+  if (!aligned(nf, 16) || !aligned(out, 16)) return set_error(GP_ERR_ALIGN, "nf and out must be 16-byte aligned");
+  DeviceState* st = nullptr;
+  int rc = get_device_state(&st);
+  if (rc != GP_OK) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchCtx c{};
+  c.stream = s;
+  c.sm_count = st->sm_count;
+  c.args.status = st->status;
+  c.args.timeout_ns = g_timeout_ns.load();
+  c.args.ln_eps = 1e-5f;
+  rc = launch_mgn_node_update(c, n, n_sets, nf, aggs, w, b, gamma, beta, out);
+  if (rc != GP_OK) return rc;
+  g_launches.fetch_add(1, std::memory_order_relaxed);  // the aggregate conversion
+  return finish_launch(s, 1);
+}
+
 int gp_testmlp_out(int64_t m, const void* x, const void* w1, const void* b1, const void* w2,
                    const void* b2, const void* w3, const void* b3, void* out, void* stream) {
   gp_mlp_spec s = mgn_spec(128, GP_TAIL_NONE, GP_F16);

@@ -28,6 +28,7 @@ enum DeviceStatus : int {
   kDevTimeoutEpilogue = 0x300,  // epilogue gave up waiting for an accumulator
   kDevTimeoutWeights = 0x400,   // weight staging never completed
   kDevBadSmemAlign = 0x500,     // dynamic shared memory not 1024-byte aligned
+  kDevBadIndex = 0x600,         // a gather / scatter index outside [0, n_nodes): row read as zeros
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -183,6 +184,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16-byte copy global -> shared through the LSU path (cp.async, L1 bypassed). `bytes` = 16 copies,
+// 0 writes 16 zero bytes and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed. The pending count is
+// raised by one when this executes, so the phase also needs its ordinary arrivals.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
@@ -483,6 +496,10 @@ struct Elem<__half> {
     return r;
   }
   __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
+  // inverse of pack: (low half, high half)
+  __device__ __forceinline__ static float2 unpack(uint32_t v) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+  }
 };
 
 template <>
@@ -500,6 +517,9 @@ struct Elem<__nv_bfloat16> {
     return r;
   }
   __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static float2 unpack(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+  }
 };
 
 // ------------------------------------------------------------------------------------------------

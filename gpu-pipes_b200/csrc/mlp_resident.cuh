@@ -191,9 +191,18 @@ __device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint
         make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
 }
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG>
+// x modes of the resident kernel (the XM template argument):
+//   0  x [M, K0] through one tensor map
+//   1  MeshGraphNet edge update (graphmodel/mgn_dp.py:28-32): x = [nodes[src] | ef | nodes[dst]]
+//      (K0 = 384; nodes and ef 128 wide). The ef panels come by TMA; the node rows are gathered
+//      by the producer warp, 16-byte cp.async per lane, into the same swizzled panels. With
+//      args.scatter set, the epilogue also adds each output row into scatter[dst] (fp32).
+//   2  two sources: x panels 0-1 from tm.x (128 wide), the rest from tm.x2
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG, int XM = 0>
 __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const ChainArgs& args) {
   using L = ResidentLayout<K0, N, NL, NBUF, CG>;
+  static_assert(XM != 1 || (CG == 1 && K0 == 384 && N == 128), "edge gather: single CTA, 384 -> 128");
+  static_assert(XM != 2 || K0 > 128, "two-source x: 128 columns from each source at least");
   constexpr int kXS = L::kXStages;
   constexpr int kPanels0 = K0 / kPanel;
   constexpr int NC = L::NC;
@@ -304,7 +313,81 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
   };
 
-  if (warp == 0) {
+  if (warp == 0 && XM == 1) {
+    // ---------------------------------------------------------------- gathering producer
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();
+      mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes);
+#pragma unroll 1
+      for (int l = 0; l < NL; ++l) {
+        const int kl = l == 0 ? K0 : N;
+        const uint32_t wbase = smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
+        for (int kp = 0; kp < kl / kPanel; ++kp)
+          for (int nb = 0; nb < NC / kPanel; ++nb)
+            tma_load_2d_hint(wbase + nb * (kl * 128) + kp * (kPanel * 128), &tm.w[l], smem_u32(w_full),
+                             nb * kPanel, kp * kPanel, keep);
+      }
+    }
+    const uint64_t stream = l2_policy_evict_first();
+    const T* nodes = static_cast<const T*>(args.gnodes);
+    int s = 0;
+    uint32_t ph = 0;
+#pragma unroll 1
+    for (int unit = unit0; unit < num_units; unit += units_step) {
+      const int64_t row = static_cast<int64_t>(unit) * kBM;
+      // node indices of this tile: lane holds rows lane + 32 j (-1: outside the rows or invalid)
+      int64_t gi[2][4];
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t r = row + lane + 32 * j;
+          int64_t v = -1;
+          if (r < args.m) {
+            v = __ldg(args.gidx[a] + r);
+            if (v < 0 || v >= args.n_nodes) {
+              atomicCAS(args.status, 0, kDevBadIndex);
+              v = -1;
+            }
+          }
+          gi[a][j] = v;
+        }
+#pragma unroll 1
+      for (int p = 0; p < kPanels0; ++p) {
+        int okw = 1;
+        if (lane == 0) okw = mbar_wait(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer) ? 1 : 0;
+        if (__shfl_sync(0xffffffffu, okw, 0) == 0) break;
+        const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
+        if (p == 2 || p == 3) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
+            tma_load_2d_hint(dst, &tm.x, smem_u32(&x_full[s]), (p - 2) * kPanel, static_cast<int>(row), stream);
+          }
+        } else {
+          // 4 rows x 8 chunks of 16 B per warp instruction: lanes 8i..8i+7 read one 128-byte row
+          const int a = p < 2 ? 0 : 1;
+          const int col0 = (p & 1) * kPanel;
+          const int chunk = lane & 7;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int r = (lane >> 3) + 4 * i;
+            const int64_t node = __shfl_sync(0xffffffffu, a == 0 ? gi[0][i >> 3] : gi[1][i >> 3], r & 31);
+            const uint32_t d = dst + r * 128 + ((chunk ^ (r & 7)) << 4);
+            if (node >= 0) {
+              cp_async16(d, nodes + node * 128 + col0 + chunk * 8, 16);
+            } else {
+              cp_async16(d, nodes, 0);
+            }
+          }
+          cp_async_mbar_arrive(smem_u32(&x_full[s]));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&x_full[s]));
+        }
+        if (++s == kXS) { s = 0; ph ^= 1; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
@@ -338,12 +421,15 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
             goto producer_done;
           if (args.inject != 1) {
             const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
+            // x mode 2: panels >= 2 come from the second source
+            const CUtensorMap* xm = (XM == 2 && p >= 2) ? &tm.x2 : &tm.x;
+            const int xc = (XM == 2 && p >= 2) ? (p - 2) * kPanel : p * kPanel;
             if constexpr (kPair) {
               if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
-              tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[s]), p * kPanel, row, stream);
+              tma_load_2d_pair(dst, xm, leader_bar(&x_full[s]), xc, row, stream);
             } else {
               mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
-              tma_load_2d_hint(dst, &tm.x, smem_u32(&x_full[s]), p * kPanel, row, stream);
+              tma_load_2d_hint(dst, xm, smem_u32(&x_full[s]), xc, row, stream);
             }
           }
           if (++s == kXS) { s = 0; ph ^= 1; }
@@ -409,6 +495,9 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
             for (int p = 0; p < kPanels0; ++p) {
               if (p > 0 && !mbar_wait<kPair>(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
               tc_fence_after();
+              // gathered panels were written by cp.async (generic proxy); the MMA reads them
+              // through the async proxy
+              if constexpr (XM == 1) fence_proxy_async_smem();
               const uint64_t adesc = make_sdesc_sw128(xsm + s * kPanelBytes, 16, 1024);
 #pragma unroll
               for (int k = 0; k < kPanel / 16; ++k) {
@@ -503,10 +592,30 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
           if constexpr (TAIL == kTailLayerNorm) row_stats<N>(v, args.ln_eps, mean, rstd);
           const float nmr = -mean * rstd;
           const int row0 = unit * L::kUnitRows + static_cast<int>(rank) * kBM + q * 32;
+          // x mode 1: this row's destination node for the scatter-add (-1: none)
+          int64_t snode = -1;
+          if constexpr (XM == 1) {
+            const int64_t rr = static_cast<int64_t>(row0) + lane;
+            if (args.scatter != nullptr && rr < args.m) {
+              snode = __ldg(args.gidx[1] + rr);
+              if (snode >= args.n_nodes) snode = -1;  // reported by the producer
+            }
+          }
 #pragma unroll
           for (int c = 0; c < N / 32; ++c) {
             uint32_t pk[16];
             finish_chunk32<T, TAIL, kLastAct>(v[c], ln_g + c * 32, ln_b + c * 32, ln_ident, rstd, nmr, pk);
+            if constexpr (XM == 1) {
+              if (snode >= 0) {
+                // the stored (16-bit) values, so the sum is exactly that of the output rows
+                float4* sp = reinterpret_cast<float4*>(args.scatter + snode * N + c * 32);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float2 lo = Elem<T>::unpack(pk[2 * j]), hi = Elem<T>::unpack(pk[2 * j + 1]);
+                  atomicAdd(sp + j, make_float4(lo.x, lo.y, hi.x, hi.y));
+                }
+              }
+            }
             const int sb = L::kStgBufs == 2 ? (c & 1) : 0;
             if (lane == 0) {
               if constexpr (L::kStgBufs == 2) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
@@ -541,16 +650,16 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   }
 }
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF>
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int XM = 0>
 __global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF, 1>::kThreads, 1)
     mlp_resident_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
-  mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 1>(tm, args);
+  mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 1, XM>(tm, args);
 }
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF>
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int XM = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(ResidentLayout<K0, N, NL, NBUF, 2>::kThreads, 1)
     mlp_resident_pair_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
-  mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 2>(tm, args);
+  mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 2, XM>(tm, args);
 }
 
 }  // namespace gp

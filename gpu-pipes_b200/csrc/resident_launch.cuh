@@ -8,12 +8,17 @@
 
 namespace gp {
 
-template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG>
+// XM: x mode of mlp_resident_body. 1: c.x = the edge rows ef [m, 128], args.gnodes / gidx set;
+// 2: c.x = first source [m, 128], c.x2 = second source [m, K0 - 128].
+template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG, int XM = 0>
 int launch_resident_cg(const LaunchCtx& c) {
   using L = ResidentLayout<K0, N, NL, NBUF, CG>;
-  const void* kern =
-      CG == 2 ? reinterpret_cast<const void*>(&mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>)
-              : reinterpret_cast<const void*>(&mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>);
+  const void* kern = nullptr;
+  if constexpr (CG == 2) {
+    kern = reinterpret_cast<const void*>(&mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>);
+  } else {
+    kern = reinterpret_cast<const void*>(&mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>);
+  }
   static unsigned long long done_mask = 0;
   static int max_clusters[64] = {0};
   int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
@@ -21,7 +26,8 @@ int launch_resident_cg(const LaunchCtx& c) {
   const int dt = c.spec->dtype;
   TensorMaps tm;
   std::memset(&tm, 0, sizeof(tm));
-  rc = make_tmap_2d(&tm.x, c.x, dt, c.m, K0, kPanel, kBM, 128);
+  rc = make_tmap_2d(&tm.x, c.x, dt, c.m, XM == 0 ? K0 : 128, kPanel, kBM, 128);
+  if (rc == GP_OK && XM == 2) rc = make_tmap_2d(&tm.x2, c.x2, dt, c.m, K0 - 128, kPanel, kBM, 128);
   if (rc == GP_OK) rc = make_tmap_2d(&tm.out, c.out, dt, c.m, N, 32, 32, 64);
   for (int l = 0; rc == GP_OK && l < NL; ++l)
     rc = make_tmap_2d(&tm.w[l], c.w[l], dt, l == 0 ? K0 : N, N, kPanel, kPanel, 128);
@@ -30,7 +36,7 @@ int launch_resident_cg(const LaunchCtx& c) {
   args.num_tiles = static_cast<int>((c.m + L::kUnitRows - 1) / L::kUnitRows);
   if constexpr (CG == 1) {
     const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-    mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+    mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -56,7 +62,7 @@ int launch_resident_cg(const LaunchCtx& c) {
       mc = n;
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
-    mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF>
+    mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>
         <<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
   }
   return GP_OK;

@@ -203,6 +203,82 @@ def nerf_out(x, weights, biases, out) -> None:
                   skip_layer=5)
 
 
+def _check_mgn_weights(k0, w1, b1, w2, b2, w3, b3, gamma, beta):
+    for name, t, shape in (("w1", w1, (k0, 128)), ("w2", w2, (128, 128)), ("w3", w3, (128, 128)),
+                           ("b1", b1, (128,)), ("b2", b2, (128,)), ("b3", b3, (128,)),
+                           ("gamma", gamma, (128,)), ("beta", beta, (128,))):
+        _check_input(name, t, torch.float16)
+        if t is not None and tuple(t.shape) != shape:
+            raise RuntimeError(f"{name} has shape {tuple(t.shape)}, expected {shape}")
+
+
+def mgn_edge_update_out(nf, ef, srcs, dsts, w1, b1, w2, b2, w3, b3, gamma, beta, out,
+                        agg=None) -> None:
+    """MeshGraphNet edge update (graphmodel/mgn_dp.py:28-32) with the gather fused:
+    out[e] = LN(MgnMlp([nf[srcs[e]] | ef[e] | nf[dsts[e]]])). nf [N, 128], ef [M, 128], srcs and
+    dsts int64 [M], fp16. With agg (fp32 [N, 128]) the output rows are also summed into
+    agg[dsts[e]] (accumulated onto agg's contents)."""
+    _check_input("nf", nf, torch.float16)
+    _check_input("ef", ef, torch.float16)
+    _check_input("srcs", srcs, torch.int64)
+    _check_input("dsts", dsts, torch.int64)
+    _check_input("out", out, torch.float16)
+    _check_input("agg", agg, torch.float32)
+    m, n = ef.shape[0], nf.shape[0]
+    if nf.dim() != 2 or nf.shape[1] != 128 or ef.dim() != 2 or ef.shape[1] != 128:
+        raise RuntimeError(f"nf {tuple(nf.shape)} and ef {tuple(ef.shape)} must be [*, 128]")
+    if tuple(srcs.shape) != (m,) or tuple(dsts.shape) != (m,):
+        raise RuntimeError(f"srcs {tuple(srcs.shape)} and dsts {tuple(dsts.shape)} must be [{m}]")
+    if tuple(out.shape) != (m, 128):
+        raise RuntimeError(f"out has shape {tuple(out.shape)}, expected [{m}, 128]")
+    if agg is not None and tuple(agg.shape) != (n, 128):
+        raise RuntimeError(f"agg has shape {tuple(agg.shape)}, expected [{n}, 128]")
+    _check_mgn_weights(384, w1, b1, w2, b2, w3, b3, gamma, beta)
+    wp = (ctypes.c_void_p * 3)(w1.data_ptr(), w2.data_ptr(), w3.data_ptr())
+    bp = (ctypes.c_void_p * 3)(*[None if t is None else t.data_ptr() for t in (b1, b2, b3)])
+    with torch.cuda.device(ef.device):
+        L.check(L.lib().gp_mgn_edge_update_out(m, n, _ptr(nf), _ptr(ef), _ptr(srcs), _ptr(dsts), wp,
+                                               bp, _ptr(gamma), _ptr(beta), _ptr(out), _ptr(agg),
+                                               _stream(ef)))
+
+
+def mgn_edge_update(nf, ef, srcs, dsts, w1, b1, w2, b2, w3, b3, gamma, beta, agg=None):
+    out = torch.empty(ef.shape[0], 128, dtype=ef.dtype, device=ef.device)
+    mgn_edge_update_out(nf, ef, srcs, dsts, w1, b1, w2, b2, w3, b3, gamma, beta, out, agg=agg)
+    return out
+
+
+def mgn_node_update_out(nf, aggs, w1, b1, w2, b2, w3, b3, gamma, beta, out) -> None:
+    """MeshGraphNet node update (graphmodel/mgn_dp.py:46-54): out = LN(MgnMlp([nf | aggs[0] |
+    ...])), nf [N, 128] fp16, aggs: one or two fp32 [N, 128] edge-set aggregates (rounded to
+    fp16 as the MLP input), w1 [128 (1 + len(aggs)), 128]."""
+    aggs = list(aggs)
+    _check_input("nf", nf, torch.float16)
+    _check_input("out", out, torch.float16)
+    n = nf.shape[0]
+    if len(aggs) not in (1, 2):
+        raise RuntimeError("one or two edge-set aggregates")
+    for i, a in enumerate(aggs):
+        _check_input(f"aggs[{i}]", a, torch.float32)
+        if tuple(a.shape) != (n, 128):
+            raise RuntimeError(f"aggs[{i}] has shape {tuple(a.shape)}, expected [{n}, 128]")
+    if nf.dim() != 2 or nf.shape[1] != 128 or tuple(out.shape) != (n, 128):
+        raise RuntimeError(f"nf {tuple(nf.shape)} and out {tuple(out.shape)} must be [{n}, 128]")
+    _check_mgn_weights(128 * (1 + len(aggs)), w1, b1, w2, b2, w3, b3, gamma, beta)
+    ap = (ctypes.c_void_p * 2)(*([a.data_ptr() for a in aggs] + [None] * (2 - len(aggs))))
+    wp = (ctypes.c_void_p * 3)(w1.data_ptr(), w2.data_ptr(), w3.data_ptr())
+    bp = (ctypes.c_void_p * 3)(*[None if t is None else t.data_ptr() for t in (b1, b2, b3)])
+    with torch.cuda.device(nf.device):
+        L.check(L.lib().gp_mgn_node_update_out(n, len(aggs), _ptr(nf), ap, wp, bp, _ptr(gamma),
+                                               _ptr(beta), _ptr(out), _stream(nf)))
+
+
+def mgn_node_update(nf, aggs, w1, b1, w2, b2, w3, b3, gamma, beta):
+    out = torch.empty_like(nf)
+    mgn_node_update_out(nf, aggs, w1, b1, w2, b2, w3, b3, gamma, beta, out)
+    return out
+
+
 _NERF_FULL_W = [(64, 256)] + [(256, 256)] * 4 + [(320, 256), (256, 256), (256, 256),
                 (256, 64), (256, 256), (288, 128), (128, 64)]
 

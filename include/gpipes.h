@@ -180,6 +180,32 @@ GP_API int gp_nerf_a_out(int64_t m, const void* x, const void* const* w, const v
 GP_API int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* const* b,
                 void* out, void* stream);
 
+/* MeshGraphNet edge update with the gather and the aggregation fused (graphmodel/mgn_dp.py:28-32
+ * update_edges, with the MLP of common/mlps.py MgnMlp(384, [128, 128, 128]); the aggregation is
+ * graphmodel/common.py:97-99 UnsortedSegmentSum by destination node). No reference kernel: the
+ * reference's mgn_fullmlp_out takes the concatenated [m, 384] rows, built beforehand in HBM.
+ *   nf [n_nodes, 128], ef [m, 128], srcs / dsts [m] (int64, node ids in [0, n_nodes)),
+ *   w[3] = [384, 128], [128, 128], [128, 128]; b[3]; gamma, beta [128] (NULL: 1 and 0); fp16.
+ *   out[e] = LN(ReLU(ReLU([nf[srcs[e]] | ef[e] | nf[dsts[e]]] W1 + b1) W2 + b2) W3 + b3), eps 1e-5
+ *   agg (optional, fp32 [n_nodes, 128]): agg[dsts[e]] += out[e] (the fp16 values as stored),
+ *   accumulated onto the caller's contents (zero it first; several edge sets may share it).
+ * An index outside [0, n_nodes) reads a zero row, is left out of agg, and sets device status
+ * 0x600 (gp_device_status). The [m, 384] concat never exists in memory. */
+GP_API int gp_mgn_edge_update_out(int64_t m, int64_t n_nodes, const void* nf, const void* ef,
+                           const int64_t* srcs, const int64_t* dsts, const void* const* w,
+                           const void* const* b, const void* gamma, const void* beta, void* out,
+                           float* agg, void* stream);
+
+/* MeshGraphNet node update (graphmodel/mgn_dp.py:46-54, with the aggregates of
+ * gp_mgn_edge_update_out in place of the graph's index-by-destination):
+ *   out[v] = LN(MLP([nf[v] | fp16(aggs[0][v]) | ... | fp16(aggs[n_sets-1][v])])), n_sets 1 or 2,
+ *   nf [n, 128], aggs[i] fp32 [n, 128], w[3] = [128 (1 + n_sets), 128], [128, 128], [128, 128].
+ * The aggregates are rounded to fp16 into the per-device workspace, then read with nf through
+ * two tensor maps (no concat in HBM). */
+GP_API int gp_mgn_node_update_out(int64_t n, int n_sets, const void* nf, const float* const* aggs,
+                           const void* const* w, const void* const* b, const void* gamma,
+                           const void* beta, void* out, void* stream);
+
 /* NeRF with view directions (apps/nerf_full/torch/model.py:5-66, use_viewdirs = True, with the
  * reference's pipelined shapes: radiance and rgb widths padded to 64). Replaces nerf_full_out
  * (apps/nerf_full/pipelined/nerf_full_pl_ext.cu:22-95). fp16.

@@ -167,6 +167,7 @@ def main() -> None:
 
     gen_bert_addln(ref, rows)
     gen_nerf_full(ref, rows)
+    gen_mgn_graph(ref)
 
     # ---- known-answer LayerNorm row from misc_tests/layer_norm/torch_val.py:87-116
     src = (ref / "misc_tests/layer_norm/torch_val.py").read_text()
@@ -231,6 +232,42 @@ def gen_nerf_full(ref: Path, rows: int = 48) -> None:
     _save("nerf_full_viewdirs", seed=np.int64(seed), dims_in=np.array(dims_in),
           dims_out=np.array(dims_out), x=_u16(x), d=_u16(d), rgb=rgb.numpy().astype(np.float32),
           alpha=alpha.numpy().astype(np.float32), wsum=np.float64(checksum(layers)))
+
+
+def gen_mgn_graph(ref: Path, n_nodes: int = 40, n_edges: int = 96) -> None:
+    """One MeshGraphNet message-passing step on a random graph (graphmodel/mgn_dp.py:28-54), with
+    the reference's MgnMlp (common/mlps.py:3-20) for the edge (384 -> 128 x 3 + LN) and node
+    (256 -> 128 x 3 + LN) MLPs. The aggregate is the segment sum by destination of the edge
+    outputs rounded to fp16, and enters the node MLP rounded to fp16."""
+    mlps = _load(ref, "common/mlps.py", "ref_mlps_graph")
+    seed = 81
+    g = torch.Generator().manual_seed(seed)
+    nf = torch.randn(n_nodes, 128, generator=g).half()
+    ef = torch.randn(n_edges, 128, generator=g).half()
+    srcs = torch.randint(0, n_nodes, (n_edges,), generator=g)
+    dsts = torch.randint(0, n_nodes, (n_edges,), generator=g)
+    out = {}
+    nets = {}
+    for name, k0, s in (("edge", 384, seed + 1), ("node", 256, seed + 2)):
+        layers = layer_params(s, [k0, 128, 128, 128])
+        net = mlps.MgnMlp(k0, [128, 128, 128], layernorm=True).eval()
+        for i, (w, b) in enumerate(layers):
+            _set_linear(net.model[i][0], w, b)
+        gamma = (1 + 0.1 * torch.randn(128, generator=g)).half()
+        beta = (0.1 * torch.randn(128, generator=g)).half()
+        with torch.no_grad():
+            net.model[3].weight.copy_(gamma.float())
+            net.model[3].bias.copy_(beta.float())
+        nets[name] = net
+        out[f"{name}_gamma"], out[f"{name}_beta"] = _u16(gamma), _u16(beta)
+        out[f"{name}_wsum"] = np.float64(checksum(layers))
+    with torch.no_grad():
+        y_edge = nets["edge"](torch.cat([nf[srcs], ef, nf[dsts]], dim=-1).float())
+        agg = torch.zeros(n_nodes, 128).index_add_(0, dsts, y_edge.half().float())
+        y_node = nets["node"](torch.cat([nf, agg.half()], dim=-1).float())
+    _save("mgn_graph_step", seed=np.int64(seed), nf=_u16(nf), ef=_u16(ef), srcs=srcs.numpy(),
+          dsts=dsts.numpy(), y_edge=y_edge.numpy().astype(np.float32), agg=agg.numpy(),
+          y_node=y_node.numpy().astype(np.float32), **out)
 
 
 if __name__ == "__main__":

@@ -103,6 +103,28 @@ def test_nerf_full_matches_reference_model():
     torch.testing.assert_close(rgb, torch.from_numpy(g["rgb"]), **TOL)
 
 
+def test_mgn_graph_step_matches_reference_model():
+    """Edge update, segment sum and node update (graphmodel/mgn_dp.py:28-54) with the reference's
+    MgnMlp."""
+    g = load_golden("mgn_graph_step")
+    seed = int(g["seed"])
+    le = layer_params(seed + 1, [384, 128, 128, 128])
+    ln_ = layer_params(seed + 2, [256, 128, 128, 128])
+    assert abs(checksum(le) - float(g["edge_wsum"])) < 1e-6
+    assert abs(checksum(ln_) - float(g["node_wsum"])) < 1e-6
+    nf, ef = u16_to(g["nf"], torch.float16), u16_to(g["ef"], torch.float16)
+    srcs, dsts = torch.from_numpy(g["srcs"]), torch.from_numpy(g["dsts"])
+    lne = (u16_to(g["edge_gamma"], torch.float16), u16_to(g["edge_beta"], torch.float16))
+    lnn = (u16_to(g["node_gamma"], torch.float16), u16_to(g["node_beta"], torch.float16))
+    y_edge = O.mgn_edge_update(nf, ef, srcs, dsts, le, lne)
+    torch.testing.assert_close(y_edge, torch.from_numpy(g["y_edge"]), **TOL)
+    # one fp16 ulp where the two fp32 edge outputs round to different halves
+    agg = O.mgn_aggregate(y_edge.half(), dsts, nf.shape[0])
+    torch.testing.assert_close(agg, torch.from_numpy(g["agg"]), atol=2e-3, rtol=1e-3)
+    y_node = O.mgn_node_update(nf, [torch.from_numpy(g["agg"])], ln_, lnn)
+    torch.testing.assert_close(y_node, torch.from_numpy(g["y_node"]), **TOL)
+
+
 def test_layernorm_known_row():
     """misc_tests/layer_norm/torch_val.py:87-116: one 128-value row, gamma=1, beta=0."""
     g = load_golden("ln_known_row")
