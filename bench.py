@@ -138,6 +138,7 @@ KERNEL_OF = {
     "bert_ffn": "mlp_gemm_pair_kernel", "dlrm_top": "mlp_gemm_pair_kernel",
     "bert_addln": "mlp_stream_kernel", "dlrm_interact": "dlrm_interaction_kernel",
     "nerf_full": "mlp_stream_kernel (trunk, alpha and rgb launches)",
+    "mgn_mp": "mlp_resident_kernel (edge update with gather and segment sum; node update)",
 }
 
 

@@ -584,6 +584,8 @@ int gp_mgn_edge_update_out(int64_t m, int64_t n_nodes, const void* nf, const voi
   if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
   if (m == 0) return GP_OK;
   if (n_nodes == 0) return set_error(GP_ERR_ARG, "edges need nodes (n_nodes = 0)");
+  if (n_nodes > (int64_t(1) << 25))  // node row offsets (node * 128) are 32-bit in the kernel
+    return set_error(GP_ERR_SHAPE, "n_nodes = %lld exceeds 2^25", (long long)n_nodes);
   if (nf == nullptr || ef == nullptr || srcs == nullptr || dsts == nullptr || w == nullptr || out == nullptr)
     return set_error(GP_ERR_ARG, "nf, ef, srcs, dsts, w and out must not be NULL");
   for (int l = 0; l < 3; ++l) {

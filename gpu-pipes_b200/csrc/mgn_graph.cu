@@ -5,8 +5,8 @@
 //   node update  out[v] = LN(MLP([nf[v] | agg_0[v] | agg_1[v] ...]))      mgn_dp.py:46-54
 // MLP = 128 -> 128 ReLU -> 128 ReLU -> 128 (common/mlps.py MgnMlp), fp16.
 //
-// The edge update is the weight-resident kernel in x mode 1: the concat is assembled in shared
-// memory (node rows gathered by the producer warp, ef by TMA) and never exists in HBM; the
+// The edge update is the weight-resident CTA-pair kernel in x mode 1: the concat is assembled in
+// shared memory (node rows gathered by the producer warps, ef by TMA) and never exists in HBM; the
 // aggregation is fused into its epilogue (fp32 vector atomics of the stored output rows). The
 // node update converts the fp32 aggregates to fp16 once ([n, 128 * n_sets] in the workspace) and
 // runs the resident kernel in x mode 2 on [nf | that buffer] through two tensor maps.
@@ -61,7 +61,7 @@ int launch_mgn_edge_update(const LaunchCtx& base, int64_t m, int64_t n_nodes, co
   c.args.gidx[1] = dsts;
   c.args.n_nodes = n_nodes;
   c.args.scatter = agg;
-  return launch_resident_cg<__half, 384, 128, 3, kActsMgn, kTailLayerNorm, 2, 1, 1>(c);
+  return launch_resident_cg<__half, 384, 128, 3, kActsMgn, kTailLayerNorm, 2, 2, 1>(c);
 }
 
 int launch_mgn_node_update(const LaunchCtx& base, int64_t n, int n_sets, const void* nf,

@@ -40,7 +40,10 @@
 
 namespace gp {
 
-template <int K0_, int N_, int NL_, int NBUF_, int CG_>
+// STG1: one output staging buffer per epilogue warp whatever the room (x mode 1 spends the
+// space on a seventh x stage, which covers gather latency: 0.90 -> 0.78 ms on 2M edges; dropping
+// the staging for direct stores from registers, for an eighth, measured slower)
+template <int K0_, int N_, int NL_, int NBUF_, int CG_, bool STG1 = false>
 struct ResidentLayout {
   static constexpr int K0 = K0_, N = N_, NL = NL_, NBUF = NBUF_, CG = CG_;
   static_assert(K0 % kPanel == 0 && K0 >= kPanel, "K0 must be a multiple of 64");
@@ -60,7 +63,7 @@ struct ResidentLayout {
   // output staging per epilogue warp: 32 rows x 32 cols x 2 B, double-buffered when that still
   // leaves at least four x stages
   static constexpr int kStageBytes = 32 * 64;
-  static constexpr int kStgBufs =
+  static constexpr int kStgBufs = STG1 ? 1 :
       (kSmemLimit - (kWBytes + kBiasBytes + 2 * kNumEpiWarps * kStageBytes + kLnBytes + kBarBytes)) /
                   kPanelBytes >= 4 ? 2 : 1;
   static constexpr int kStgBytes = kNumEpiWarps * kStageBytes * kStgBufs;
@@ -194,14 +197,19 @@ __device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint
 // x modes of the resident kernel (the XM template argument):
 //   0  x [M, K0] through one tensor map
 //   1  MeshGraphNet edge update (graphmodel/mgn_dp.py:28-32): x = [nodes[src] | ef | nodes[dst]]
-//      (K0 = 384; nodes and ef 128 wide). The ef panels come by TMA; the node rows are gathered
-//      by the producer warp, 16-byte cp.async per lane, into the same swizzled panels. With
+//      (K0 = 384; nodes and ef 128 wide; CTA pairs, so that half the weights per CTA leave six
+//      x stages to cover the gather latency). The ef panels come by TMA; the node rows are
+//      gathered by each CTA's producer warp, 16-byte cp.async per lane, into the same swizzled
+//      panels (warp 0 the source rows, an extra last warp the destination rows), their completion
+//      counted on a local barrier (gx_full). One more warp (the forwarder) waits for it, fences
+//      the writes into the async proxy and arrives on the leader's x_full, which then expects
+//      one arrival per CTA. With
 //      args.scatter set, the epilogue also adds each output row into scatter[dst] (fp32).
 //   2  two sources: x panels 0-1 from tm.x (128 wide), the rest from tm.x2
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG, int XM = 0>
 __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const ChainArgs& args) {
-  using L = ResidentLayout<K0, N, NL, NBUF, CG>;
-  static_assert(XM != 1 || (CG == 1 && K0 == 384 && N == 128), "edge gather: single CTA, 384 -> 128");
+  using L = ResidentLayout<K0, N, NL, NBUF, CG, XM == 1>;
+  static_assert(XM != 1 || (CG == 2 && K0 == 384 && N == 128), "edge gather: CTA pair, 384 -> 128");
   static_assert(XM != 2 || K0 > 128, "two-source x: 128 columns from each source at least");
   constexpr int kXS = L::kXStages;
   constexpr int kPanels0 = K0 / kPanel;
@@ -220,6 +228,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   uint64_t* mma_done = bars + 21;  // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+  uint64_t* gx_full = reinterpret_cast<uint64_t*>(smem + L::kSmemBytes);  // [kXS], x mode 1 only
   float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
   float* ln_b = ln_g + N;
 
@@ -239,8 +248,9 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXS; ++s) {
-      mbar_init(smem_u32(&x_full[s]), 1);
+      mbar_init(smem_u32(&x_full[s]), XM == 1 ? CG : 1);
       mbar_init(smem_u32(&x_empty[s]), 1);
+      if constexpr (XM == 1) mbar_init(smem_u32(&gx_full[s]), 1);
     }
     mbar_init(smem_u32(w_full), 1);
     for (int b = 0; b < NBUF; ++b) {
@@ -313,77 +323,114 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
   };
 
-  if (warp == 0 && XM == 1) {
-    // ---------------------------------------------------------------- gathering producer
-    if (lane == 0) {
+  if (XM == 1 && (warp == 0 || warp == 3 + L::kNumEpiWarps)) {
+    // ---------------------------------------------------------------- gathering producers
+    // warp 0: weights, the nodes[src] panels (0, 1) and the ef panels (2, 3, by TMA);
+    // the last warp: the nodes[dst] panels (4, 5). Both walk the same panel sequence.
+    const bool src_warp = warp == 0;
+    if (src_warp && lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
-      mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes);
+      if (leader) mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes * CG);
 #pragma unroll 1
       for (int l = 0; l < NL; ++l) {
         const int kl = l == 0 ? K0 : N;
         const uint32_t wbase = smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
         for (int kp = 0; kp < kl / kPanel; ++kp)
           for (int nb = 0; nb < NC / kPanel; ++nb)
-            tma_load_2d_hint(wbase + nb * (kl * 128) + kp * (kPanel * 128), &tm.w[l], smem_u32(w_full),
-                             nb * kPanel, kp * kPanel, keep);
+            tma_load_2d_pair(wbase + nb * (kl * 128) + kp * (kPanel * 128), &tm.w[l], leader_bar(w_full),
+                             static_cast<int>(rank) * NC + nb * kPanel, kp * kPanel, keep);
       }
     }
     const uint64_t stream = l2_policy_evict_first();
     const T* nodes = static_cast<const T*>(args.gnodes);
+    const int64_t* gidx = args.gidx[src_warp ? 0 : 1];
+    // element offsets (node * 128) of this warp's node rows for a tile: lane holds rows
+    // lane + 32 j; 0xFFFFFFFF = outside the rows or an invalid index (a zero row)
+    auto load_offs = [&](int unit, uint32_t (&o)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t r = static_cast<int64_t>(unit) * L::kUnitRows + static_cast<int64_t>(rank) * kBM + lane + 32 * j;
+        o[j] = 0xFFFFFFFFu;
+        if (unit < num_units && r < args.m) {
+          const int64_t v = __ldg(gidx + r);
+          if (v < 0 || v >= args.n_nodes) {
+            atomicCAS(args.status, 0, kDevBadIndex);
+          } else {
+            o[j] = static_cast<uint32_t>(v) * 128u;
+          }
+        }
+      }
+    };
+    uint32_t cur[4], nxt[4];
+    load_offs(unit0, cur);
     int s = 0;
     uint32_t ph = 0;
+    bool live = true;
 #pragma unroll 1
-    for (int unit = unit0; unit < num_units; unit += units_step) {
-      const int64_t row = static_cast<int64_t>(unit) * kBM;
-      // node indices of this tile: lane holds rows lane + 32 j (-1: outside the rows or invalid)
-      int64_t gi[2][4];
-#pragma unroll
-      for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int64_t r = row + lane + 32 * j;
-          int64_t v = -1;
-          if (r < args.m) {
-            v = __ldg(args.gidx[a] + r);
-            if (v < 0 || v >= args.n_nodes) {
-              atomicCAS(args.status, 0, kDevBadIndex);
-              v = -1;
-            }
-          }
-          gi[a][j] = v;
-        }
+    for (int unit = unit0; live && unit < num_units; unit += units_step) {
+      const int row = unit * L::kUnitRows + static_cast<int>(rank) * kBM;
+      load_offs(unit + units_step, nxt);  // the next tile's indices, in flight during this one
 #pragma unroll 1
       for (int p = 0; p < kPanels0; ++p) {
-        int okw = 1;
-        if (lane == 0) okw = mbar_wait(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer) ? 1 : 0;
-        if (__shfl_sync(0xffffffffu, okw, 0) == 0) break;
-        const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
-        if (p == 2 || p == 3) {
-          if (lane == 0) {
-            mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
-            tma_load_2d_hint(dst, &tm.x, smem_u32(&x_full[s]), (p - 2) * kPanel, static_cast<int>(row), stream);
-          }
-        } else {
-          // 4 rows x 8 chunks of 16 B per warp instruction: lanes 8i..8i+7 read one 128-byte row
-          const int a = p < 2 ? 0 : 1;
-          const int col0 = (p & 1) * kPanel;
-          const int chunk = lane & 7;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int r = (lane >> 3) + 4 * i;
-            const int64_t node = __shfl_sync(0xffffffffu, a == 0 ? gi[0][i >> 3] : gi[1][i >> 3], r & 31);
-            const uint32_t d = dst + r * 128 + ((chunk ^ (r & 7)) << 4);
-            if (node >= 0) {
-              cp_async16(d, nodes + node * 128 + col0 + chunk * 8, 16);
-            } else {
-              cp_async16(d, nodes, 0);
+        const bool mine = src_warp ? p < 4 : p >= 4;
+        if (mine) {
+          int okw = 1;
+          if (lane == 0) okw = mbar_wait<kPair>(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer) ? 1 : 0;
+          if (__shfl_sync(0xffffffffu, okw, 0) == 0) { live = false; break; }
+          const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
+          if (p == 2 || p == 3) {
+            if (lane == 0) {
+              // the leader expects both CTAs' bytes; the peer's arrival is the count's second
+              if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
+              tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[s]), (p - 2) * kPanel, row, stream);
+              if (!leader) mbar_arrive_cluster(leader_bar(&x_full[s]));
             }
+          } else {
+            // 4 rows x 8 chunks of 16 B per warp instruction: lanes 8i..8i+7 read one 128-byte row
+            const int col0 = (p & 1) * kPanel;
+            const int chunk = lane & 7;
+            const T* base = nodes + col0 + chunk * 8;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int r = (lane >> 3) + 4 * i;
+              const uint32_t off = __shfl_sync(0xffffffffu, cur[i >> 3], r & 31);
+              const uint32_t d = dst + r * 128 + ((chunk ^ (r & 7)) << 4);
+              if (off != 0xFFFFFFFFu) {
+                cp_async16(d, base + off, 16);
+              } else {
+                cp_async16(d, nodes, 0);
+              }
+            }
+            cp_async_mbar_arrive(smem_u32(&gx_full[s]));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&gx_full[s]));
           }
-          cp_async_mbar_arrive(smem_u32(&x_full[s]));
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&x_full[s]));
         }
         if (++s == kXS) { s = 0; ph ^= 1; }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+    }
+    __syncwarp();
+  } else if (XM == 1 && warp == 2 + L::kNumEpiWarps) {
+    // ---------------------------------------------------------------- gather forwarder
+    if (lane == 0) {
+      int s = 0;
+      uint32_t gpar = 0;  // bit s: parity of gx_full[s]'s next phase
+#pragma unroll 1
+      for (int unit = unit0; unit < num_units; unit += units_step) {
+        bool live = true;
+#pragma unroll 1
+        for (int p = 0; p < kPanels0; ++p) {
+          if (p != 2 && p != 3) {
+            if (!mbar_wait(smem_u32(&gx_full[s]), (gpar >> s) & 1u, wctx, kDevTimeoutProducer)) { live = false; break; }
+            gpar ^= 1u << s;
+            fence_proxy_async_smem();  // the cp.async writes, seen by the tensor core's reads
+            if constexpr (kPair) mbar_arrive_cluster(leader_bar(&x_full[s])); else mbar_arrive(smem_u32(&x_full[s]));
+          }
+          if (++s == kXS) s = 0;
+        }
+        if (!live) break;
       }
     }
     __syncwarp();
@@ -495,9 +542,6 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
             for (int p = 0; p < kPanels0; ++p) {
               if (p > 0 && !mbar_wait<kPair>(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
               tc_fence_after();
-              // gathered panels were written by cp.async (generic proxy); the MMA reads them
-              // through the async proxy
-              if constexpr (XM == 1) fence_proxy_async_smem();
               const uint64_t adesc = make_sdesc_sw128(xsm + s * kPanelBytes, 16, 1024);
 #pragma unroll
               for (int k = 0; k < kPanel / 16; ++k) {
@@ -557,6 +601,16 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     bool ok = true;
 #pragma unroll 1
     for (int unit = unit0 + g * units_step; ok && unit < num_units; unit += NBUF * units_step) {
+      // x mode 1: this row's destination node for the scatter-add (-1: none), loaded before the
+      // layers so that its latency is hidden
+      int64_t snode = -1;
+      if constexpr (XM == 1) {
+        const int64_t rr = static_cast<int64_t>(unit) * L::kUnitRows + static_cast<int64_t>(rank) * kBM + q * 32 + lane;
+        if (args.scatter != nullptr && rr < args.m) {
+          snode = __ldg(args.gidx[1] + rr);
+          if (snode < 0 || snode >= args.n_nodes) snode = -1;  // reported by the producer
+        }
+      }
 #pragma unroll 1
       for (int l = 0; l < NL; ++l) {
         if (!mbar_wait<kPair>(smem_u32(&acc_full[g]), acc_ph, wctx, kDevTimeoutEpilogue)) { ok = false; break; }
@@ -592,15 +646,6 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
           if constexpr (TAIL == kTailLayerNorm) row_stats<N>(v, args.ln_eps, mean, rstd);
           const float nmr = -mean * rstd;
           const int row0 = unit * L::kUnitRows + static_cast<int>(rank) * kBM + q * 32;
-          // x mode 1: this row's destination node for the scatter-add (-1: none)
-          int64_t snode = -1;
-          if constexpr (XM == 1) {
-            const int64_t rr = static_cast<int64_t>(row0) + lane;
-            if (args.scatter != nullptr && rr < args.m) {
-              snode = __ldg(args.gidx[1] + rr);
-              if (snode >= args.n_nodes) snode = -1;  // reported by the producer
-            }
-          }
 #pragma unroll
           for (int c = 0; c < N / 32; ++c) {
             uint32_t pk[16];
@@ -650,14 +695,21 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   }
 }
 
+// threads and dynamic shared memory of a launch in x mode XM (mode 1 adds the forwarder warp, a
+// second gathering warp and the gx_full barriers after the layout's end)
+template <class L, int XM>
+constexpr int resident_threads() { return L::kThreads + (XM == 1 ? 64 : 0); }
+template <class L, int XM>
+constexpr int resident_smem() { return L::kSmemBytes + (XM == 1 ? 128 : 0); }
+
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int XM = 0>
-__global__ void __launch_bounds__(ResidentLayout<K0, N, NL, NBUF, 1>::kThreads, 1)
+__global__ void __launch_bounds__(resident_threads<ResidentLayout<K0, N, NL, NBUF, 1, XM == 1>, XM>(), 1)
     mlp_resident_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
   mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 1, XM>(tm, args);
 }
 
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int XM = 0>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(ResidentLayout<K0, N, NL, NBUF, 2>::kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(resident_threads<ResidentLayout<K0, N, NL, NBUF, 2, XM == 1>, XM>(), 1)
     mlp_resident_pair_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
   mlp_resident_body<T, K0, N, NL, ACTS, TAIL, NBUF, 2, XM>(tm, args);
 }

@@ -12,7 +12,7 @@ namespace gp {
 // 2: c.x = first source [m, 128], c.x2 = second source [m, K0 - 128].
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG, int XM = 0>
 int launch_resident_cg(const LaunchCtx& c) {
-  using L = ResidentLayout<K0, N, NL, NBUF, CG>;
+  using L = ResidentLayout<K0, N, NL, NBUF, CG, XM == 1>;
   const void* kern = nullptr;
   if constexpr (CG == 2) {
     kern = reinterpret_cast<const void*>(&mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>);
@@ -21,7 +21,10 @@ int launch_resident_cg(const LaunchCtx& c) {
   }
   static unsigned long long done_mask = 0;
   static int max_clusters[64] = {0};
-  int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
+  constexpr int kThr = resident_threads<L, XM>();
+  constexpr int kSmem = resident_smem<L, XM>();
+  static_assert(kSmem <= kSmemLimit, "shared memory budget");
+  int rc = ensure_smem_attr(kern, kSmem, &done_mask);
   if (rc != GP_OK) return rc;
   const int dt = c.spec->dtype;
   TensorMaps tm;
@@ -36,7 +39,7 @@ int launch_resident_cg(const LaunchCtx& c) {
   args.num_tiles = static_cast<int>((c.m + L::kUnitRows - 1) / L::kUnitRows);
   if constexpr (CG == 1) {
     const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-    mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+    mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM><<<grid, kThr, kSmem, c.stream>>>(tm, args);
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -44,8 +47,8 @@ int launch_resident_cg(const LaunchCtx& c) {
     if (mc == 0) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (c.sm_count / 2), 1, 1);
-      cfg.blockDim = dim3(L::kThreads, 1, 1);
-      cfg.dynamicSmemBytes = L::kSmemBytes;
+      cfg.blockDim = dim3(kThr, 1, 1);
+      cfg.dynamicSmemBytes = kSmem;
       cudaLaunchAttribute attr;
       attr.id = cudaLaunchAttributeClusterDimension;
       attr.val.clusterDim.x = 2;
@@ -63,7 +66,7 @@ int launch_resident_cg(const LaunchCtx& c) {
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
     mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>
-        <<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+        <<<2 * clusters, kThr, kSmem, c.stream>>>(tm, args);
   }
   return GP_OK;
 }

@@ -20,6 +20,7 @@ import ctypes
 import torch
 
 from . import _lib as L
+from . import workloads as W
 
 _DT = {torch.float16: L.GP_F16, torch.bfloat16: L.GP_BF16}
 
@@ -413,11 +414,37 @@ def dlrm_topmlp(x, *wb) -> torch.Tensor:
     return out
 
 
+_SCRATCH = {}
+
+
+def _scratch_f32(device, n):
+    """A cached fp32 device buffer of at least n elements per device (grown, never shrunk)."""
+    key = (device.type, device.index)
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(n, dtype=torch.float32, device=device)
+        _SCRATCH[key] = buf
+    return buf[:n]
+
+
 def run_workload_out(w, x, weights, ln, out) -> None:
     """Run a workloads.Workload chain through the generic C entry point."""
     if w.block == "dlrm_interaction":
         m = x.shape[0] // 27
         dlrm_interaction_out(x[:m], x[m:].view(m, 26, x.shape[1]), out)
+        return
+    if w.block == "mgn_mp":
+        ef, nf, srcs, dsts = W.split_mgn_input(x)
+        m, n = ef.shape[0], nf.shape[0]
+        o = out.view(-1)
+        agg = _scratch_f32(x.device, n * 128).view(n, 128)
+        agg.zero_()
+        (e1, e2, e3, n1, n2, n3) = weights
+        ge, be, gn, bn = ln
+        mgn_edge_update_out(nf, ef, srcs, dsts, e1[0], e1[1], e2[0], e2[1], e3[0], e3[1], ge, be,
+                            o[:m * 128].view(m, 128), agg=agg)
+        mgn_node_update_out(nf, [agg], n1[0], n1[1], n2[0], n2[1], n3[0], n3[1], gn, bn,
+                            o[m * 128:].view(n, 128))
         return
     if w.block == "nerf_full":
         m = x.numel() // 96

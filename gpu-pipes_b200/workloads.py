@@ -53,7 +53,11 @@ class Workload:
                                   # bottom-output rows, then 26 m embedding rows; no layers);
                                   # "nerf_full" = NeRF with view directions (input: one flat
                                   # tensor, m x-rows of 64 then m d-rows of 32; output [m, 128]
-                                  # holding out_r [m, 64] then out_rgb [m, 64] in memory order)
+                                  # holding out_r [m, 64] then out_rgb [m, 64] in memory order);
+                                  # "mgn_mp" = one MeshGraphNet message-passing step over m edges
+                                  # and m / 16 nodes (input: one flat fp16 buffer [ef | nf | srcs
+                                  # | dsts], indices int64; output [m, 136] holding the edge rows
+                                  # [m, 128] then the node rows [m / 16, 128])
     description: str = ""
 
     @property
@@ -64,6 +68,8 @@ class Workload:
     def n_out(self) -> int:
         if self.block == "nerf_full":
             return 128
+        if self.block == "mgn_mp":
+            return 136
         return 480 if self.block == "dlrm_interaction" else self.layers[-1].n
 
     @property
@@ -82,6 +88,9 @@ class Workload:
     def flop_per_row(self) -> int:
         if self.block == "dlrm_interaction":
             return 351 * 2 * 128  # the dot products below the diagonal
+        if self.block == "mgn_mp":  # edge MLP per edge, node MLP per 16 edges
+            e = sum(2 * l.k_logical * l.n_logical for l in self.layers[:3])
+            return e + sum(2 * l.k_logical * l.n_logical for l in self.layers[3:]) // MGN_EDGES_PER_NODE
         return sum(2 * l.k_logical * l.n_logical for l in self.layers)
 
     @property
@@ -91,6 +100,8 @@ class Workload:
             return 27 * 128
         if self.block.startswith("nerf_full"):
             return 96
+        if self.block == "mgn_mp":
+            return 128 + 8 + 8  # ef, nf / 16, two int64 indices
         return 2 * self.k0 if self.block == "bert_addln" else self.k0
 
     @property
@@ -215,8 +226,22 @@ NERF_FULL = Workload(
     description="NeRF with view directions: trunk 63(64)->256 x8 (skip), alpha 256->64, "
                 "bottleneck 256->256, rgb [256 | d 27(32)] -> 128 ReLU -> 64, fp16")
 
+# One MeshGraphNet message-passing step (graphmodel/mgn_dp.py:28-54, one edge set): edge update
+# [nf[src] | ef | nf[dst]] -> MgnMlp(384) + LN with the gather and the segment sum by destination
+# fused, then the node update [nf | aggregate] -> MgnMlp(256) + LN. 16 edges per node (the ratio of
+# mgn_dp.py's mesh edges to nodes); endpoints uniform over the nodes; features ~N(0, 1).
+MGN_EDGES_PER_NODE = 16
+MGN_MP = Workload(
+    name="mgn_mp", m=2097152, dtype=torch.float16, seed=9, tail=L.TAIL_LAYERNORM, ln_eps=1e-5,
+    input_logical=384, block="mgn_mp",
+    layers=(Layer(384, 128, _R, 384, 128), Layer(128, 128, _R, 128, 128), Layer(128, 128, _N, 128, 128),
+            Layer(256, 128, _R, 256, 128), Layer(128, 128, _R, 128, 128), Layer(128, 128, _N, 128, 128)),
+    description="MeshGraphNet message passing: edges [nf[src] | ef | nf[dst]] 384->128->128->128 + LN "
+                "(gather and segment sum fused), nodes [nf | agg] 256->128->128->128 + LN, 16 edges "
+                "per node, fp16")
+
 WORKLOADS = {w.name: w for w in (MGN_EDGE, MGN_NODE, MGN_LINEARS, TEST_MLP, DLRM_BOT, GC_EDGE, NERF,
-                                 BERT_FFN, DLRM_TOP, BERT_ADDLN, DLRM_INTERACT, NERF_FULL)}
+                                 BERT_FFN, DLRM_TOP, BERT_ADDLN, DLRM_INTERACT, NERF_FULL, MGN_MP)}
 
 
 def rows_of(w: Workload, x: torch.Tensor) -> int:
@@ -225,6 +250,8 @@ def rows_of(w: Workload, x: torch.Tensor) -> int:
         return x.shape[0] // 27
     if w.block == "nerf_full":
         return x.numel() // 96
+    if w.block == "mgn_mp":
+        return x.numel() // w.in_width
     return x.shape[0] // 2 if w.block == "bert_addln" else x.shape[0]
 
 
@@ -273,9 +300,10 @@ def make_weights(w: Workload):
         layers.append((W.to(w.dtype).contiguous(), B.to(w.dtype).contiguous()))
     ln = None
     if w.tail != L.TAIL_NONE:
-        ln = (torch.ones(w.n_out, dtype=w.dtype), torch.zeros(w.n_out, dtype=w.dtype))
-        if w.block == "bert_addln":  # LN0 and LN2
-            ln = ln + (torch.ones(w.n_out, dtype=w.dtype), torch.zeros(w.n_out, dtype=w.dtype))
+        nl = w.layers[-1].n
+        ln = (torch.ones(nl, dtype=w.dtype), torch.zeros(nl, dtype=w.dtype))
+        if w.block in ("bert_addln", "mgn_mp"):  # two LayerNorms (LN0 / LN2, edge / node)
+            ln = ln + (torch.ones(nl, dtype=w.dtype), torch.zeros(nl, dtype=w.dtype))
     return layers, ln
 
 
@@ -283,6 +311,8 @@ def make_input_chunk(w: Workload, chunk: int, rows: int | None = None) -> torch.
     """Rows [chunk*CHUNK_ROWS, chunk*CHUNK_ROWS + rows) of the input, in w.dtype."""
     rows = CHUNK_ROWS if rows is None else rows
     g = _gen(w.seed, 1, chunk)
+    if w.block == "mgn_mp":
+        return mgn_graph_input(w, rows, chunk)
     if w.block == "dlrm_interaction":
         # [bottom-output rows (ReLU of N(0, 0.3^2)); 26 embedding rows per sample, N(0, 0.1^2)]
         bot = torch.relu(torch.randn(rows, w.k0, generator=g)) * 0.3
@@ -331,6 +361,28 @@ def _nerf_posenc(p: torch.Tensor, octaves: int, width: int) -> torch.Tensor:
     return out
 
 
+def mgn_graph_input(w: Workload, edges: int, salt: int) -> torch.Tensor:
+    """A graph of `edges` edges and edges / 16 nodes, packed as one flat fp16 buffer:
+    [ef (edges x 128) | nf (nodes x 128) | srcs (int64) | dsts (int64)]."""
+    assert edges % MGN_EDGES_PER_NODE == 0, "edges must be a multiple of 16"
+    nodes = edges // MGN_EDGES_PER_NODE
+    g = _gen(w.seed, 3, salt)
+    ef = torch.randn(edges, 128, generator=g).to(w.dtype)
+    nf = torch.randn(nodes, 128, generator=g).to(w.dtype)
+    idx = torch.randint(0, nodes, (2, edges), generator=g)
+    return torch.cat([ef.reshape(-1), nf.reshape(-1), idx.reshape(-1).view(w.dtype)])
+
+
+def split_mgn_input(x: torch.Tensor):
+    """Inverse of mgn_graph_input: (ef, nf, srcs, dsts) views of the flat buffer."""
+    edges = x.numel() // 144
+    nodes = edges // MGN_EDGES_PER_NODE
+    ef = x[:edges * 128].view(edges, 128)
+    nf = x[edges * 128:(edges + nodes) * 128].view(nodes, 128)
+    idx = x[(edges + nodes) * 128:].view(torch.int64).view(2, edges)
+    return ef, nf, idx[0], idx[1]
+
+
 def make_input(w: Workload, row0: int = 0, rows: int | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """Rows [row0, row0+rows) of the input (host tensor, optionally written into `out`)."""
@@ -366,6 +418,13 @@ def make_input(w: Workload, row0: int = 0, rows: int | None = None,
             b[r - row0:r - row0 + take] = chunk[need + r - c0:need + r - c0 + take]
             r += take
         res = torch.cat([a, b])
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
+    if w.block == "mgn_mp":
+        # each rank / sample is its own graph (message passing does not split a graph by rows here)
+        res = mgn_graph_input(w, rows, row0 // MGN_EDGES_PER_NODE)
         if out is not None:
             out.copy_(res)
             return out

@@ -190,7 +190,7 @@ GP_API int gp_nerf_out(int64_t m, const void* x, const void* const* w, const voi
  *   agg (optional, fp32 [n_nodes, 128]): agg[dsts[e]] += out[e] (the fp16 values as stored),
  *   accumulated onto the caller's contents (zero it first; several edge sets may share it).
  * An index outside [0, n_nodes) reads a zero row, is left out of agg, and sets device status
- * 0x600 (gp_device_status). The [m, 384] concat never exists in memory. */
+ * 0x600 (gp_device_status). n_nodes <= 2^25. The [m, 384] concat never exists in memory. */
 GP_API int gp_mgn_edge_update_out(int64_t m, int64_t n_nodes, const void* nf, const void* ef,
                            const int64_t* srcs, const int64_t* dsts, const void* const* w,
                            const void* const* b, const void* gamma, const void* beta, void* out,

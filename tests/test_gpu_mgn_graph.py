@@ -154,3 +154,24 @@ def test_shape_errors(cuda_dev):
         cuda_ext.mgn_node_update(nf, [], w1, b1, w2, b2, w3, b3, None, None)
     e = cuda_ext.mgn_edge_update(nf, ef[:0], srcs[:0], dsts[:0], w1, b1, w2, b2, w3, b3, None, None)
     assert e.shape == (0, 128)
+
+
+def test_bench_workload_step(cuda_dev):
+    """The bench's mgn_mp step (edge update with gather and segment sum, then node update) through
+    cuda_ext.run_workload_out, against the oracle on the same packed input."""
+    from gpu_pipes_b200 import workloads as W
+
+    w = W.WORKLOADS["mgn_mp"].with_m(65536)
+    x = W.make_input(w, 0, w.m)
+    layers, ln = W.make_weights(w)
+    out = torch.empty(w.m, w.n_out, dtype=w.dtype, device=cuda_dev)
+    wd = [(a.to(cuda_dev), b.to(cuda_dev)) for a, b in layers]
+    lnd = tuple(t.to(cuda_dev) for t in ln)
+    for _ in range(2):  # the aggregate is re-zeroed on every step
+        cuda_ext.run_workload_out(w, x.to(cuda_dev), wd, lnd, out)
+    torch.cuda.synchronize()
+    ref = O.workload_forward(w, x, layers, ln).reshape(-1)
+    got = out.float().cpu().reshape(-1)
+    m, n = w.m, w.m // 16
+    _check(got[:m * 128].view(m, 128), ref[:m * 128].view(m, 128))
+    _check(got[m * 128:].view(n, 128), ref[m * 128:].view(n, 128))
