@@ -138,7 +138,7 @@ KERNEL_OF = {
     "bert_ffn": "mlp_gemm_pair_kernel", "dlrm_top": "mlp_gemm_pair_kernel",
     "bert_addln": "mlp_stream_kernel", "dlrm_interact": "dlrm_interaction_kernel",
     "nerf_full": "mlp_stream_kernel (trunk, alpha and rgb launches)",
-    "mgn_mp": "mlp_resident_kernel (edge update with gather and segment sum; node update)",
+    "mgn_mp": "mlp_resident_pair_kernel (edge update: gather4 of node rows, segment sum) + mlp_resident_kernel (node update)",
 }
 
 

@@ -186,18 +186,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 16-byte copy global -> shared through the LSU path (cp.async, L1 bypassed). `bytes` = 16 copies,
-// 0 writes 16 zero bytes and reads nothing.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
-}
-
-// Arrive on `bar` once every cp.async this thread issued so far has landed. The pending count is
-// raised by one when this executes, so the phase also needs its ordinary arrivals.
-__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
@@ -231,6 +219,19 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap,
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+// Four rows r0..r3 (any order, any rows; out-of-range rows read zeros) of a 2-D tensor, one
+// box-width of columns from c0, into four consecutive 128-byte rows at dst (tile::gather4; the
+// tensor map's box is one row high). CTA-pair form: completion on the leader's barrier.
+__device__ __forceinline__ void tma_gather4_pair(uint32_t dst, const void* tmap, uint32_t cluster_bar, int c0,
+                                                 int r0, int r1, int r2, int r3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
+      "l"(policy)
       : "memory");
 }
 

@@ -197,13 +197,10 @@ __device__ __forceinline__ void stage_chunk32(uint8_t* stg, int lane, const uint
 // x modes of the resident kernel (the XM template argument):
 //   0  x [M, K0] through one tensor map
 //   1  MeshGraphNet edge update (graphmodel/mgn_dp.py:28-32): x = [nodes[src] | ef | nodes[dst]]
-//      (K0 = 384; nodes and ef 128 wide; CTA pairs, so that half the weights per CTA leave six
-//      x stages to cover the gather latency). The ef panels come by TMA; the node rows are
-//      gathered by each CTA's producer warp, 16-byte cp.async per lane, into the same swizzled
-//      panels (warp 0 the source rows, an extra last warp the destination rows), their completion
-//      counted on a local barrier (gx_full). One more warp (the forwarder) waits for it, fences
-//      the writes into the async proxy and arrives on the leader's x_full, which then expects
-//      one arrival per CTA. With
+//      (K0 = 384; nodes and ef 128 wide; CTA pairs, so that half the weights per CTA leave
+//      seven x stages to cover the gather latency). The ef panels come by TMA; the node rows by
+//      TMA tile::gather4 (four indexed rows per request, written swizzled like any panel) from
+//      tm.x2, warp 0 the source rows and an extra last warp the destination rows. With
 //      args.scatter set, the epilogue also adds each output row into scatter[dst] (fp32).
 //   2  two sources: x panels 0-1 from tm.x (128 wide), the rest from tm.x2
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int CG, int XM = 0>
@@ -211,6 +208,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   using L = ResidentLayout<K0, N, NL, NBUF, CG, XM == 1>;
   static_assert(XM != 1 || (CG == 2 && K0 == 384 && N == 128), "edge gather: CTA pair, 384 -> 128");
   static_assert(XM != 2 || K0 > 128, "two-source x: 128 columns from each source at least");
+  constexpr int kDstWarp = 2 + L::kNumEpiWarps;  // x mode 1: the second gathering warp
   constexpr int kXS = L::kXStages;
   constexpr int kPanels0 = K0 / kPanel;
   constexpr int NC = L::NC;
@@ -228,7 +226,6 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   uint64_t* mma_done = bars + 21;  // [1]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
-  uint64_t* gx_full = reinterpret_cast<uint64_t*>(smem + L::kSmemBytes);  // [kXS], x mode 1 only
   float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
   float* ln_b = ln_g + N;
 
@@ -248,9 +245,8 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXS; ++s) {
-      mbar_init(smem_u32(&x_full[s]), XM == 1 ? CG : 1);
+      mbar_init(smem_u32(&x_full[s]), 1);
       mbar_init(smem_u32(&x_empty[s]), 1);
-      if constexpr (XM == 1) mbar_init(smem_u32(&gx_full[s]), 1);
     }
     mbar_init(smem_u32(w_full), 1);
     for (int b = 0; b < NBUF; ++b) {
@@ -323,10 +319,11 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
   };
 
-  if (XM == 1 && (warp == 0 || warp == 3 + L::kNumEpiWarps)) {
-    // ---------------------------------------------------------------- gathering producers
-    // warp 0: weights, the nodes[src] panels (0, 1) and the ef panels (2, 3, by TMA);
-    // the last warp: the nodes[dst] panels (4, 5). Both walk the same panel sequence.
+  if (XM == 1 && (warp == 0 || warp == kDstWarp)) {
+    // ---------------------------------------------------------------- gathering producers (TMA)
+    // warp 0: weights, the nodes[src] panels (0, 1) and the ef panels (2, 3); the last warp: the
+    // nodes[dst] panels (4, 5). Lane l fetches rows 4l..4l+3 of a gathered panel with one
+    // tile::gather4 request; both CTAs' requests complete on the leader's x_full.
     const bool src_warp = warp == 0;
     if (src_warp && lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
@@ -342,34 +339,34 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
       }
     }
     const uint64_t stream = l2_policy_evict_first();
-    const T* nodes = static_cast<const T*>(args.gnodes);
+    const uint64_t keep_nodes = l2_policy_evict_last();
     const int64_t* gidx = args.gidx[src_warp ? 0 : 1];
-    // element offsets (node * 128) of this warp's node rows for a tile: lane holds rows
-    // lane + 32 j; 0xFFFFFFFF = outside the rows or an invalid index (a zero row)
-    auto load_offs = [&](int unit, uint32_t (&o)[4]) {
+    const int oob = static_cast<int>(args.n_nodes);  // a row past the end: reads zeros
+    // node rows 4 lane + q of a tile (oob for rows past m and for invalid indices)
+    auto load_rows = [&](int unit, int (&o)[4]) {
+      const int64_t r0 = static_cast<int64_t>(unit) * L::kUnitRows + static_cast<int64_t>(rank) * kBM + 4 * lane;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t r = static_cast<int64_t>(unit) * L::kUnitRows + static_cast<int64_t>(rank) * kBM + lane + 32 * j;
-        o[j] = 0xFFFFFFFFu;
-        if (unit < num_units && r < args.m) {
-          const int64_t v = __ldg(gidx + r);
+      for (int q = 0; q < 4; ++q) {
+        o[q] = oob;
+        if (unit < num_units && r0 + q < args.m) {
+          const int64_t v = __ldg(gidx + r0 + q);
           if (v < 0 || v >= args.n_nodes) {
             atomicCAS(args.status, 0, kDevBadIndex);
           } else {
-            o[j] = static_cast<uint32_t>(v) * 128u;
+            o[q] = static_cast<int>(v);
           }
         }
       }
     };
-    uint32_t cur[4], nxt[4];
-    load_offs(unit0, cur);
+    int cur[4], nxt[4];
+    load_rows(unit0, cur);
     int s = 0;
     uint32_t ph = 0;
     bool live = true;
 #pragma unroll 1
     for (int unit = unit0; live && unit < num_units; unit += units_step) {
       const int row = unit * L::kUnitRows + static_cast<int>(rank) * kBM;
-      load_offs(unit + units_step, nxt);  // the next tile's indices, in flight during this one
+      load_rows(unit + units_step, nxt);
 #pragma unroll 1
       for (int p = 0; p < kPanels0; ++p) {
         const bool mine = src_warp ? p < 4 : p >= 4;
@@ -378,60 +375,19 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
           if (lane == 0) okw = mbar_wait<kPair>(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer) ? 1 : 0;
           if (__shfl_sync(0xffffffffu, okw, 0) == 0) { live = false; break; }
           const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
+          if (lane == 0 && leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
+          __syncwarp();
           if (p == 2 || p == 3) {
-            if (lane == 0) {
-              // the leader expects both CTAs' bytes; the peer's arrival is the count's second
-              if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
-              tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[s]), (p - 2) * kPanel, row, stream);
-              if (!leader) mbar_arrive_cluster(leader_bar(&x_full[s]));
-            }
+            if (lane == 0) tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[s]), (p - 2) * kPanel, row, stream);
           } else {
-            // 4 rows x 8 chunks of 16 B per warp instruction: lanes 8i..8i+7 read one 128-byte row
-            const int col0 = (p & 1) * kPanel;
-            const int chunk = lane & 7;
-            const T* base = nodes + col0 + chunk * 8;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int r = (lane >> 3) + 4 * i;
-              const uint32_t off = __shfl_sync(0xffffffffu, cur[i >> 3], r & 31);
-              const uint32_t d = dst + r * 128 + ((chunk ^ (r & 7)) << 4);
-              if (off != 0xFFFFFFFFu) {
-                cp_async16(d, base + off, 16);
-              } else {
-                cp_async16(d, nodes, 0);
-              }
-            }
-            cp_async_mbar_arrive(smem_u32(&gx_full[s]));
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&gx_full[s]));
+            tma_gather4_pair(dst + lane * 512, &tm.x2, leader_bar(&x_full[s]), (p & 1) * kPanel, cur[0], cur[1],
+                             cur[2], cur[3], keep_nodes);
           }
         }
         if (++s == kXS) { s = 0; ph ^= 1; }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
-    }
-    __syncwarp();
-  } else if (XM == 1 && warp == 2 + L::kNumEpiWarps) {
-    // ---------------------------------------------------------------- gather forwarder
-    if (lane == 0) {
-      int s = 0;
-      uint32_t gpar = 0;  // bit s: parity of gx_full[s]'s next phase
-#pragma unroll 1
-      for (int unit = unit0; unit < num_units; unit += units_step) {
-        bool live = true;
-#pragma unroll 1
-        for (int p = 0; p < kPanels0; ++p) {
-          if (p != 2 && p != 3) {
-            if (!mbar_wait(smem_u32(&gx_full[s]), (gpar >> s) & 1u, wctx, kDevTimeoutProducer)) { live = false; break; }
-            gpar ^= 1u << s;
-            fence_proxy_async_smem();  // the cp.async writes, seen by the tensor core's reads
-            if constexpr (kPair) mbar_arrive_cluster(leader_bar(&x_full[s])); else mbar_arrive(smem_u32(&x_full[s]));
-          }
-          if (++s == kXS) s = 0;
-        }
-        if (!live) break;
-      }
+      for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
     }
     __syncwarp();
   } else if (warp == 0) {
@@ -695,12 +651,11 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   }
 }
 
-// threads and dynamic shared memory of a launch in x mode XM (mode 1 adds the forwarder warp, a
-// second gathering warp and the gx_full barriers after the layout's end)
+// threads and dynamic shared memory of a launch in x mode XM (mode 1 adds a second gathering warp)
 template <class L, int XM>
-constexpr int resident_threads() { return L::kThreads + (XM == 1 ? 64 : 0); }
+constexpr int resident_threads() { return L::kThreads + (XM == 1 ? 32 : 0); }
 template <class L, int XM>
-constexpr int resident_smem() { return L::kSmemBytes + (XM == 1 ? 128 : 0); }
+constexpr int resident_smem() { return L::kSmemBytes; }
 
 template <typename T, int K0, int N, int NL, uint32_t ACTS, int TAIL, int NBUF, int XM = 0>
 __global__ void __launch_bounds__(resident_threads<ResidentLayout<K0, N, NL, NBUF, 1, XM == 1>, XM>(), 1)

@@ -31,6 +31,9 @@ int launch_resident_cg(const LaunchCtx& c) {
   std::memset(&tm, 0, sizeof(tm));
   rc = make_tmap_2d(&tm.x, c.x, dt, c.m, XM == 0 ? K0 : 128, kPanel, kBM, 128);
   if (rc == GP_OK && XM == 2) rc = make_tmap_2d(&tm.x2, c.x2, dt, c.m, K0 - 128, kPanel, kBM, 128);
+  // x mode 1: the node rows, one row per box for tile::gather4
+  if (rc == GP_OK && XM == 1)
+    rc = make_tmap_2d(&tm.x2, c.args.gnodes, dt, static_cast<uint64_t>(c.args.n_nodes), 128, kPanel, 1, 128);
   if (rc == GP_OK) rc = make_tmap_2d(&tm.out, c.out, dt, c.m, N, 32, 32, 64);
   for (int l = 0; rc == GP_OK && l < NL; ++l)
     rc = make_tmap_2d(&tm.w[l], c.w[l], dt, l == 0 ? K0 : N, N, kPanel, kPanel, 128);
