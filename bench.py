@@ -47,9 +47,12 @@ from gpu_pipes_b200 import workloads as W  # noqa: E402
 
 L2_BYTES = 126 * 2**20
 # DRAM bytes (read + write) per row of one launch of the fused kernel, from ncu captures
-# (profiles/mlp_resident_mgn_node.md, profiles/mlp_stream_nerf_gc.md); traffic grows with rows.
-NCU_TRAFFIC_PER_ROW = {"mgn_node": 752.7e6 / 1048576, "nerf": 141.4e6 / 1048576,
-                       "gc_edge": 509.8e6 / 131072}
+# (profiles/mlp_resident_mgn_node.md, profiles/mlp_stream_nerf_gc.md,
+# profiles/dlrm_interaction_kernel.md, profiles/mlp_resident_mgn_edge_gather.md: for mgn_mp the
+# edge kernel only); traffic grows with rows.
+NCU_TRAFFIC_PER_ROW = {"mgn_node": 752.7e6 / 1048576, "nerf": 144.1e6 / 1048576,
+                       "gc_edge": 497.7e6 / 131072, "dlrm_interact": 507.5e6 / 65536,
+                       "mgn_mp": 744.5e6 / 1048576}
 
 
 def parse():
