@@ -13,7 +13,9 @@ for the barrier and the max-over-ranks of the timing).
 Reported:
   value       rows/s over all ranks, inputs already resident in HBM, CUDA-event timed
   e2e         same metric through the public API with the host->device copy of x (pinned) and
-              the device->host copy of the output inside every timed step
+              the device->host copy of the output inside every timed step (plain chains through
+              gp_fused_mlp_host, which overlaps the copies of neighbouring row chunks with the
+              kernels; composed blocks copy, run and copy back in sequence)
   roofline    the fused kernel against the measured HBM bandwidth (the path is HBM-bound:
               768 B/row vs 131,072 FLOP/row, arithmetic intensity 171 < ridge 253)
   cpu_baseline the CPU oracle (the reference's PyTorch fp32 model, restated) on a bounded sample
@@ -304,6 +306,11 @@ def main():
     x_dev2 = torch.empty_like(x)
 
     def e2e_step():
+        if not w.block:
+            # plain chains: the pipelined host-buffer entry point (chunked H2D / kernel / D2H on
+            # three streams)
+            cuda_ext.run_workload_host(w, x_host, wd, lnd, out_host)
+            return
         x_dev2.copy_(x_host, non_blocking=True)
         cuda_ext.run_workload_out(w, x_dev2, wd, lnd, out)
         out_host.copy_(out, non_blocking=True)

@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = (
     "gp_nerf_a_out",
     "gp_nerf_out",
     "gp_nerf_full_out",
+    "gp_fused_mlp_host",
     "gp_mgn_edge_update_out",
     "gp_mgn_node_update_out",
     "gp_gc_edges_bf16_noalloc_out",
@@ -117,6 +118,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_bert_ffn_out.restype = _INT
     lib.gp_bert_addln_ffn_out.argtypes = [_I64] + [_P] * 14
     lib.gp_bert_addln_ffn_out.restype = _INT
+    lib.gp_fused_mlp_host.argtypes = [ctypes.POINTER(GpSpec), _I64, _P, ctypes.POINTER(_P),
+                                      ctypes.POINTER(_P), _P, _P, _P, _I64, _P]
+    lib.gp_fused_mlp_host.restype = _INT
     lib.gp_mgn_edge_update_out.argtypes = [_I64, _I64, _P, _P, _P, _P, ctypes.POINTER(_P),
                                            ctypes.POINTER(_P), _P, _P, _P, _P, _P]
     lib.gp_mgn_edge_update_out.restype = _INT

@@ -322,6 +322,112 @@ int fused_mlp(const gp_mlp_spec* spec, int64_t m, const void* x, const void* con
   return finish_launch(stream, 1);
 }
 
+// ------------------------------------------------------------------------------------------------
+// Host-buffer pipeline (gp_fused_mlp_host): per device, an H2D and a D2H stream, double-buffered
+// device staging for x and out chunks (its own allocation, apart from the kernels' workspace, since
+// chains use that inside a call), and the events that order them against the caller's stream.
+// ------------------------------------------------------------------------------------------------
+struct HostPipe {
+  std::mutex mu;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr, x_ready[2] = {}, k_done[2] = {}, out_free[2] = {};
+  void* buf = nullptr;
+  size_t cap = 0;
+  bool used = false;
+};
+static std::vector<HostPipe*> g_pipes;
+
+static int get_host_pipe(HostPipe** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (static_cast<int>(g_pipes.size()) <= dev) g_pipes.resize(dev + 1, nullptr);
+  if (g_pipes[dev] == nullptr) {
+    HostPipe* p = new HostPipe();
+    e = cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking);
+    cudaEvent_t* evs[8] = {&p->start, &p->done, &p->x_ready[0], &p->x_ready[1], &p->k_done[0],
+                           &p->k_done[1], &p->out_free[0], &p->out_free[1]};
+    for (int i = 0; e == cudaSuccess && i < 8; ++i) e = cudaEventCreateWithFlags(evs[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "host pipeline setup: %s", cudaGetErrorString(e));
+    g_pipes[dev] = p;
+  }
+  *out = g_pipes[dev];
+  return GP_OK;
+}
+
+int fused_mlp_host(const gp_mlp_spec* spec, int64_t m, const void* x_host, const void* const* w,
+                   const void* const* b, const void* gamma, const void* beta, void* out_host,
+                   int64_t chunk_rows, cudaStream_t cs) {
+  clear_error();
+  if (spec == nullptr) return set_error(GP_ERR_ARG, "spec is NULL");
+  if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
+  if (m == 0) return GP_OK;
+  if (x_host == nullptr || out_host == nullptr) return set_error(GP_ERR_ARG, "x_host and out_host must not be NULL");
+  if (spec->n_layers < 1 || spec->n_layers > GP_MAX_LAYERS) return set_error(GP_ERR_ARG, "n_layers = %d", spec->n_layers);
+  const size_t xrow = static_cast<size_t>(spec->widths[0]) * 2;
+  const size_t orow = static_cast<size_t>(spec->widths[spec->n_layers]) * 2;
+  if (chunk_rows <= 0) {  // about eight chunks, at least 65,536 rows each, whole tiles
+    chunk_rows = (m + 7) / 8;
+    if (chunk_rows < 65536) chunk_rows = 65536;
+  }
+  chunk_rows = (chunk_rows + 255) / 256 * 256;
+  if (chunk_rows > m) chunk_rows = m;
+  HostPipe* hp = nullptr;
+  int rc = get_host_pipe(&hp);
+  if (rc != GP_OK) return rc;
+  std::lock_guard<std::mutex> lk(hp->mu);
+  const size_t xb = (static_cast<size_t>(chunk_rows) * xrow + 255) / 256 * 256;
+  const size_t ob = (static_cast<size_t>(chunk_rows) * orow + 255) / 256 * 256;
+  cudaError_t e = cudaSuccess;
+  if (2 * (xb + ob) > hp->cap) {
+    if (hp->buf != nullptr) {
+      e = cudaDeviceSynchronize();  // the previous staging may still be in use on any stream
+      if (e == cudaSuccess) e = cudaFree(hp->buf);
+      hp->buf = nullptr;
+      hp->cap = 0;
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&hp->buf, 2 * (xb + ob));
+    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "host pipeline staging (%zu bytes): %s", 2 * (xb + ob), cudaGetErrorString(e));
+    hp->cap = 2 * (xb + ob);
+  }
+  char* base = static_cast<char*>(hp->buf);
+  char* xbuf[2] = {base, base + xb};
+  char* obuf[2] = {base + 2 * xb, base + 2 * xb + ob};
+  auto ck = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
+  // the copies start after the caller's earlier work, and after the previous call's last copy
+  ck(cudaEventRecord(hp->start, cs));
+  ck(cudaStreamWaitEvent(hp->h2d, hp->start, 0));
+  if (hp->used) ck(cudaStreamWaitEvent(hp->h2d, hp->done, 0));
+  const int64_t nchunks = (m + chunk_rows - 1) / chunk_rows;
+  for (int64_t i = 0; rc == GP_OK && e == cudaSuccess && i < nchunks; ++i) {
+    const int s = static_cast<int>(i & 1);
+    const int64_t r0 = i * chunk_rows;
+    const int64_t rows = (m - r0) < chunk_rows ? (m - r0) : chunk_rows;
+    if (i >= 2) ck(cudaStreamWaitEvent(hp->h2d, hp->k_done[s], 0));  // chunk i-2 has read xbuf[s]
+    ck(cudaMemcpyAsync(xbuf[s], static_cast<const char*>(x_host) + r0 * xrow, rows * xrow,
+                       cudaMemcpyHostToDevice, hp->h2d));
+    ck(cudaEventRecord(hp->x_ready[s], hp->h2d));
+    ck(cudaStreamWaitEvent(cs, hp->x_ready[s], 0));
+    if (i >= 2) ck(cudaStreamWaitEvent(cs, hp->out_free[s], 0));  // chunk i-2's D2H has read obuf[s]
+    if (e != cudaSuccess) break;
+    rc = fused_mlp(spec, rows, xbuf[s], w, b, gamma, beta, obuf[s], cs);
+    ck(cudaEventRecord(hp->k_done[s], cs));
+    ck(cudaStreamWaitEvent(hp->d2h, hp->k_done[s], 0));
+    ck(cudaMemcpyAsync(static_cast<char*>(out_host) + r0 * orow, obuf[s], rows * orow,
+                       cudaMemcpyDeviceToHost, hp->d2h));
+    ck(cudaEventRecord(hp->out_free[s], hp->d2h));
+  }
+  // the caller's stream (and the next call) see every copy finished
+  ck(cudaEventRecord(hp->done, hp->d2h));
+  ck(cudaStreamWaitEvent(cs, hp->done, 0));
+  hp->used = true;
+  if (rc != GP_OK) return rc;
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "host pipeline: %s", cudaGetErrorString(e));
+  return GP_OK;
+}
+
 }  // namespace gp
 
 // ================================================================================================
@@ -335,6 +441,13 @@ int gp_fused_mlp_out(const gp_mlp_spec* spec, int64_t m, const void* x, const vo
                      const void* const* b, const void* gamma, const void* beta, void* out,
                      void* stream) {
   return fused_mlp(spec, m, x, w, b, gamma, beta, out, static_cast<cudaStream_t>(stream));
+}
+
+int gp_fused_mlp_host(const gp_mlp_spec* spec, int64_t m, const void* x_host, const void* const* w,
+                      const void* const* b, const void* gamma, const void* beta, void* out_host,
+                      int64_t chunk_rows, void* stream) {
+  return fused_mlp_host(spec, m, x_host, w, b, gamma, beta, out_host, chunk_rows,
+                        static_cast<cudaStream_t>(stream));
 }
 
 static gp_mlp_spec mgn_spec(int k0, int tail, int dtype) {

@@ -80,6 +80,40 @@ def fused_mlp_out(x, weights, biases, out, *, acts, tail=L.TAIL_NONE, gamma=None
                                          _ptr(gamma), _ptr(beta), _ptr(out), _stream(x)))
 
 
+def fused_mlp_host_out(x_host, weights, biases, out_host, *, acts, tail=L.TAIL_NONE, gamma=None,
+                       beta=None, ln_eps=1e-5, skip_layer=0, chunk_rows=0, device=None) -> None:
+    """fused_mlp_out with x and out in HOST memory (pinned for overlap): the rows are streamed in
+    chunks, H2D copies, kernels and D2H copies of neighbouring chunks overlapping. Weights and
+    LayerNorm parameters are device tensors. Enqueued on the current stream of their device;
+    synchronise it before reading out_host."""
+    if x_host.is_cuda or out_host.is_cuda:
+        raise RuntimeError("x_host and out_host must be host tensors")
+    if not x_host.is_contiguous() or not out_host.is_contiguous():
+        raise RuntimeError("x_host and out_host must be contiguous")
+    dt = _DT.get(x_host.dtype)
+    if dt is None or out_host.dtype != x_host.dtype:
+        raise RuntimeError(f"x_host and out_host must both be float16 or bfloat16")
+    dev = device if device is not None else weights[0].device
+    for i, (w, b) in enumerate(zip(weights, biases)):
+        _check_input(f"w{i + 1}", w, x_host.dtype)
+        _check_input(f"b{i + 1}", b, x_host.dtype)
+    _check_input("gamma", gamma, x_host.dtype)
+    _check_input("beta", beta, x_host.dtype)
+    widths = [x_host.shape[1]] + [w.shape[1] for w in weights]
+    if out_host.dim() != 2 or out_host.shape[0] != x_host.shape[0] or out_host.shape[1] != widths[-1]:
+        raise RuntimeError(f"out_host has shape {tuple(out_host.shape)}, expected [{x_host.shape[0]}, {widths[-1]}]")
+    spec = L.make_spec(widths, acts, tail, dt, ln_eps, skip_layer)
+    n = len(weights)
+    wp = (ctypes.c_void_p * n)(*[w.data_ptr() for w in weights])
+    bp = (ctypes.c_void_p * n)(*[(b.data_ptr() if b is not None else None) for b in biases])
+    with torch.cuda.device(dev):
+        L.check(L.lib().gp_fused_mlp_host(ctypes.byref(spec), x_host.shape[0],
+                                          ctypes.c_void_p(x_host.data_ptr()), wp, bp, _ptr(gamma),
+                                          _ptr(beta), ctypes.c_void_p(out_host.data_ptr()),
+                                          int(chunk_rows),
+                                          ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+
+
 # ------------------------------------------------------------------------------------------------
 # MeshGraphNet family (apps/mgn_fullmlp, apps/mgn_linears, apps/test_mlp)
 # ------------------------------------------------------------------------------------------------
@@ -412,6 +446,16 @@ def dlrm_topmlp(x, *wb) -> torch.Tensor:
     out = _out_like(x, 1)
     dlrm_topmlp_out(x, *wb, out)
     return out
+
+
+def run_workload_host(w, x_host, weights, ln, out_host) -> None:
+    """A plain-chain workloads.Workload end to end on host buffers (gp_fused_mlp_host)."""
+    if w.block:
+        raise RuntimeError(f"{w.name}: host pipeline covers plain chains only")
+    gamma, beta = ln if ln is not None else (None, None)
+    fused_mlp_host_out(x_host, [p[0] for p in weights], [p[1] for p in weights], out_host,
+                       acts=w.acts, tail=w.tail, gamma=gamma, beta=beta, ln_eps=w.ln_eps,
+                       skip_layer=w.skip_layer)
 
 
 _SCRATCH = {}

@@ -232,6 +232,18 @@ GP_API int gp_gc_edges_bf16_noalloc_out(int64_t m, int act, const void* x,
                                  const void* w0, const void* b0, const void* w1, const void* b1,
                                  const void* gamma, const void* beta, void* out, void* stream);
 
+/* gp_fused_mlp_out on HOST buffers: x_host [m, widths[0]] in, out_host [m, widths[n_layers]] out
+ * (16-bit; pinned memory for overlap, pageable works but copies synchronously). The rows go in
+ * chunks of chunk_rows (0: about m / 8, at least 65,536) through double-buffered device staging:
+ * the H2D copy of chunk i+1 and the D2H copy of chunk i-1 run on two library streams while chunk
+ * i computes on `stream`, so a call costs about the larger of the two PCIe directions instead of
+ * their sum. Weights, biases, gamma and beta are device pointers as for gp_fused_mlp_out. Returns
+ * after enqueueing; `stream` waits for the last D2H copy, so synchronising `stream` makes
+ * out_host valid. No reference counterpart (the reference takes device tensors only). */
+GP_API int gp_fused_mlp_host(const gp_mlp_spec* spec, int64_t m, const void* x_host,
+                      const void* const* w, const void* const* b, const void* gamma,
+                      const void* beta, void* out_host, int64_t chunk_rows, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Diagnostics and control (no reference counterpart: the reference has no error reporting).
  * ------------------------------------------------------------------------------------------- */
