@@ -68,6 +68,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=8.0)
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--graph", action="store_true",
+                   help="capture one step in a CUDA graph and time its replays")
     p.add_argument("--kernel-only", action="store_true",
                    help="time the kernel only (no e2e, CPU baseline or clock sampling); for ncu")
     return p.parse_args()
@@ -245,6 +247,21 @@ def main():
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
+    graph = None
+    graph_launches = 0
+    if args.graph:
+        # one step captured after the warm-up (workspaces already at size, so the capture
+        # allocates nothing); replays run the same kernels with no host work per step
+        graph = torch.cuda.CUDAGraph()
+        n0 = L.launch_count()
+        with torch.cuda.graph(graph):
+            step()
+        graph_launches = L.launch_count() - n0
+        torch.cuda.synchronize()
+        step = graph.replay  # noqa: F811
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
 
     def barrier():
         torch.cuda.synchronize()
@@ -284,6 +301,8 @@ def main():
         barrier()
         ms = ev0.elapsed_time(ev1)
     launches = L.launch_count() - launches0
+    if graph is not None:  # replays enqueue the captured kernels without calling the library
+        launches = graph_launches * args.steps
     clocks = sampler.stop() if not args.kernel_only else None
     if dist is not None:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -360,7 +379,9 @@ def main():
                               "per GPU < 2 x 126 MB" if flush else
                               "inputs larger than L2 (x %d MB + out %d MB per GPU)") % (
                            w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20),
-                       "parallelism": f"rows sharded over {world} GPU(s), weights replicated"},
+                       "parallelism": f"rows sharded over {world} GPU(s), weights replicated",
+                       "launch": "CUDA graph replay of one captured step" if graph is not None
+                                 else "library calls per step"},
             "tflops": value * w.flop_per_row / 1e12,
             "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak,

@@ -173,6 +173,7 @@ struct Workspace {
   void* ptr = nullptr;
   size_t size = 0;
   cudaEvent_t last_use = nullptr;  // recorded after the latest user's launches
+  bool capturing = false;          // the current holder is recording a CUDA graph
 };
 static Workspace g_ws[64];
 
@@ -189,6 +190,27 @@ int workspace_acquire(size_t bytes, cudaStream_t stream, void** ptr) {
       w.mu.unlock();
       return set_error(GP_ERR_CUDA, "workspace event: %s", cudaGetErrorString(e));
     }
+  }
+  // Under stream capture (a CUDA graph being recorded) the buffer is neither grown nor ordered
+  // through last_use: a captured node may not wait on uncaptured work, and an event recorded in
+  // the capture would not describe the replays. The graph's replays are ordered by the stream they
+  // are launched on; eager calls on other streams must not overlap them.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) {
+    w.mu.unlock();
+    return set_error(GP_ERR_CUDA, "cudaStreamIsCapturing: %s", cudaGetErrorString(e));
+  }
+  w.capturing = cap != cudaStreamCaptureStatusNone;
+  if (w.capturing) {
+    if (w.size < bytes) {
+      w.mu.unlock();
+      return set_error(GP_ERR_UNSUPPORTED,
+                       "workspace of %zu bytes needed during stream capture (have %zu): run the call "
+                       "once outside the capture first", bytes, w.size);
+    }
+    *ptr = w.ptr;
+    return GP_OK;
   }
   if (w.size < bytes) {
     // growing: earlier users must be done with the old buffer
@@ -217,7 +239,8 @@ void workspace_release(cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   Workspace& w = g_ws[dev];
-  cudaEventRecord(w.last_use, stream);
+  if (!w.capturing) cudaEventRecord(w.last_use, stream);
+  w.capturing = false;
   w.mu.unlock();
 }
 
