@@ -184,6 +184,7 @@ def run_reference(args, w, rank: int):
     per_row = (time.perf_counter() - t0) / 4096
     budget = 60.0 / max(1, args.steps + args.warmup)
     rows = int(min(w.m, max(256, budget / max(per_row, 1e-9))))
+    rows = max(256, rows // 256 * 256)  # whole tiles (and whole 16-edge node groups for mgn_mp)
     x = W.make_input(w, 0, rows)
     for _ in range(args.warmup):
         O.workload_forward(w, x, layers, ln)

@@ -3,16 +3,19 @@
 //   out = [bot (128) | Z[a][b] for a > b in row-major order of the strict lower triangle (351) | 0]
 // (480 fp16 values; 128 + 351 = 479, padded to 480 like the reference's top MLP input).
 //
-// Tensor cores on a batched Gram matrix: a 128-row tile holds 4 samples x 32 rows (row i < 26:
-// embedding i, row 26: the bottom output, rows 27..31: zero), K = 128 in two SWIZZLE_128B panels.
-// One M = 128, N = 128, K = 128 MMA of the tile against itself (B = the same K-major tile) gives
-// every sample's 27 x 27 Gram matrix in its 32 x 32 diagonal block; the off-diagonal blocks are
-// discarded. Warp w of the epilogue holds TMEM lanes 32w..32w+31 -- sample w's rows -- and loads
-// its diagonal block (columns 32w..32w+31).
+// Tensor cores on a batched Gram matrix. A 128-row tile holds 4 samples: rows 26 s .. 26 s + 25 are
+// sample s's embeddings (the 104 rows are consecutive rows of sparse viewed as [m * 26, 128]),
+// rows 104 + s its bottom output (consecutive rows of bot), rows 108..127 zero. K = 128 in two
+// SWIZZLE_128B panels, so a tile is 4 TMA requests (2 panels x {104 embedding rows, 4 bottom
+// rows}). One M = 128, N = 128, K = 128 MMA of the tile against itself (B = the same K-major tile)
+// gives every dot product needed: e_i . e_j of sample s at (26 s + i, 26 s + j), bot . e_i at
+// (26 s + i, 104 + s).
 //
-// CTAs of 128 threads each take tiles in turn: the 128 threads load a tile (16-byte loads, manual
-// SW128 swizzle), thread 0 issues the 8 MMAs, everyone waits for the commit, then reads TMEM and
-// writes the rows. Four CTAs per SM (128 TMEM columns each) overlap each other's load latency.
+// Persistent CTAs of 128 threads (three per SM) walk the tiles; the next tile's loads are issued
+// into the second buffer while the current one is computed. Thread r (TMEM lane r) handles
+// embedding row r: it reads its sample's 26-column window of D (within a 64-column load per warp)
+// and the bottom column, and writes its z entries into the sample's output row in shared memory;
+// the rows then leave with 16-byte stores.
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -24,33 +27,50 @@ namespace gp {
 namespace {
 
 constexpr int kIntThreads = 128;
-constexpr int kIntSamples = 4;          // samples per 128-row tile
-constexpr int kIntTileBytes = 2 * 16384;  // two 64-column panels x 128 rows x 128 B
-constexpr int kIntSmem = 56 * 1024;       // sized so that four CTAs fit on an SM (TMEM: 4 x 128 cols)
+constexpr int kIntSamples = 4;           // samples per 128-row tile
+constexpr int kIntPanel = 16384;         // 128 rows x 128 B
+constexpr int kIntTile = 2 * kIntPanel;  // two 64-column panels
+constexpr int kIntBufs = 2;
+constexpr int kIntOutRow = 960;          // 480 fp16
+constexpr int kIntOffOut = kIntBufs * kIntTile;
+constexpr int kIntOffBar = kIntOffOut + kIntSamples * kIntOutRow;
+constexpr int kIntSmem = kIntOffBar + 64;  // three CTAs per SM (TMEM: 3 x 128 columns)
+constexpr uint32_t kIntTx = 2 * (104 + 4) * 128;  // bytes per tile
 
 __global__ void __launch_bounds__(kIntThreads)
-    dlrm_interaction_kernel(const __half* __restrict__ bot, const __half* __restrict__ sparse,
-                            __half* __restrict__ out, int64_t m, int* status,
-                            unsigned long long timeout_ns) {
+    dlrm_interaction_kernel(const __grid_constant__ CUtensorMap tm_e, const __grid_constant__ CUtensorMap tm_b,
+                            __half* __restrict__ out, int64_t m, int* status, unsigned long long timeout_ns) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t* tile = smem;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kIntTileBytes);
-  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + kIntTileBytes + 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kIntTileBytes + 16);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* stage = smem + kIntOffOut;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kIntOffBar);  // [2]
+  uint64_t* mma_bar = full + 2;
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + kIntOffBar + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kIntOffBar + 28);
+  const int tid = threadIdx.x, warp = tid >> 5;
   if ((smem_u32(smem) & 1023u) != 0) {
-    if (threadIdx.x == 0) atomicCAS(status, 0, kDevBadSmemAlign);
+    if (tid == 0) atomicCAS(status, 0, kDevBadSmemAlign);
     return;
   }
-  if (threadIdx.x == 0) {
-    mbar_init(smem_u32(bar), 1);
+  // rows 108..127 of every panel stay zero (no load writes them)
+  for (int q = tid; q < kIntBufs * 2 * 20 * 8; q += kIntThreads) {
+    const int panel = q / 160, rem = q % 160;
+    *reinterpret_cast<uint4*>(smem + panel * kIntPanel + (108 + rem / 8) * 128 + (rem % 8) * 16) =
+        make_uint4(0, 0, 0, 0);
+  }
+  if (tid == 0) {
+    mbar_init(smem_u32(&full[0]), 1);
+    mbar_init(smem_u32(&full[1]), 1);
+    mbar_init(smem_u32(mma_bar), 1);
     *abort_flag = 0;
     fence_mbar_init();
+    prefetch_tmap(&tm_e);
+    prefetch_tmap(&tm_b);
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(holder), 128);
     tmem_relinquish();
   }
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -58,84 +78,84 @@ __global__ void __launch_bounds__(kIntThreads)
   const WaitCtx wctx{status, abort_flag, timeout_ns};
   const uint32_t idesc = make_idesc_f16(128, 128, 0, 0, 0);  // fp16, A and B K-major
   const int64_t tiles = (m + kIntSamples - 1) / kIntSamples;
-  uint32_t phase = 0;
+  auto issue = [&](int64_t t, int b) {  // thread 0
+    uint8_t* buf = smem + b * kIntTile;
+    mbar_arrive_expect_tx(smem_u32(&full[b]), kIntTx);
+    for (int p = 0; p < 2; ++p) {
+      tma_load_2d(smem_u32(buf + p * kIntPanel), &tm_e, smem_u32(&full[b]), p * 64, static_cast<int>(t * 104));
+      tma_load_2d(smem_u32(buf + p * kIntPanel + 104 * 128), &tm_b, smem_u32(&full[b]), p * 64,
+                  static_cast<int>(t * 4));
+    }
+  };
+  // this thread's row: sample s, embedding i (rows >= 104 carry no outputs)
+  const int s = tid < 104 ? tid / 26 : -1;
+  const int i = tid < 104 ? tid % 26 : 0;
+  const int c0 = (26 * ((warp * 32) / 26)) < 64 ? 26 * ((warp * 32) / 26) : 64;  // warp's column window
+  if (tid == 0 && blockIdx.x < tiles) issue(blockIdx.x, 0);
+  uint32_t fph[2] = {0, 0}, mph = 0;
   bool ok = true;
+  int k = 0;
 #pragma unroll 1
-  for (int64_t t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-    // ---- load the tile: row r = 32 s + i, 16 chunks of 16 B per row; all 16 loads of a thread
-    // are issued before any store, so a CTA keeps its whole tile in flight
-    {
-      uint4 v[16];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int q = threadIdx.x + u * kIntThreads;
-        const int r = q >> 4, c = q & 15;
-        const int s = r >> 5, i = r & 31;
-        const int64_t g = t * kIntSamples + s;
-        v[u] = make_uint4(0, 0, 0, 0);
-        if (g < m && i <= 26) {
-          const __half* src = i < 26 ? sparse + (g * 26 + i) * 128 : bot + g * 128;
-          v[u] = __ldg(reinterpret_cast<const uint4*>(src) + c);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int q = threadIdx.x + u * kIntThreads;
-        const int r = q >> 4, c = q & 15;
-        const int panel = c >> 3, cp = c & 7;
-        *reinterpret_cast<uint4*>(tile + panel * 16384 + r * 128 + ((cp ^ (r & 7)) * 16)) = v[u];
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
+  for (int64_t t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++k) {
+    const int b = k & 1;
+    // the next tile into the other buffer: freed by the barrier that ended the last iteration
+    if (tid == 0 && t + gridDim.x < tiles) issue(t + gridDim.x, b ^ 1);
+    if (!mbar_wait(smem_u32(&full[b]), fph[b], wctx, kDevTimeoutProducer)) ok = false;
+    fph[b] ^= 1;
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
     tc_fence_after();
-    if (threadIdx.x == 0) {
+    const uint8_t* buf = smem + b * kIntTile;
+    if (tid == 0) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const uint64_t d = make_sdesc_sw128(smem_u32(tile) + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
-        mma_ss(tmem, d, d, idesc, k > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t d = make_sdesc_sw128(smem_u32(buf) + (kk >> 2) * kIntPanel + (kk & 3) * 32, 16, 1024);
+        mma_ss(tmem, d, d, idesc, kk > 0 ? 1u : 0u);
       }
-      mma_commit(smem_u32(bar));
+      mma_commit(smem_u32(mma_bar));
     }
     __syncwarp();
-    if (!mbar_wait(smem_u32(bar), phase, wctx, kDevTimeoutEpilogue)) ok = false;
-    phase ^= 1;
+    if (!mbar_wait(smem_u32(mma_bar), mph, wctx, kDevTimeoutEpilogue)) ok = false;
+    mph ^= 1;
     tc_fence_after();
-    // ---- epilogue: warp w = sample w of the tile; lane i = row i of its Gram block. The output
-    // row (480 halves, 960 B) is assembled in shared memory, then written with 16-byte stores. It
-    // goes to bytes [4096 w, 4096 w + 960): sample w's own tile rows 0..7 of the first panel, no
-    // longer read by the (complete) MMAs nor by any other warp, and disjoint from its row 26.
-    const int64_t g = t * kIntSamples + warp;
-    uint32_t v[32];
-    tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + warp * 32, v);
+    uint32_t v[64], vb[32];
+    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    tmem_ld32(trow + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
+    tmem_ld32(trow + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+    tmem_ld32(trow + 96, vb);
     tmem_wait_ld();
-    __half* srow = reinterpret_cast<__half*>(tile + warp * 4096);
-    if (lane < 16) {  // the bottom output, from its tile row 32 w + 26 (un-swizzled)
-      const int r = warp * 32 + 26;
-      const int panel = lane >> 3, cp = lane & 7;
-      reinterpret_cast<uint4*>(srow)[lane] =
-          *reinterpret_cast<const uint4*>(tile + panel * 16384 + r * 128 + ((cp ^ (r & 7)) * 16));
+    // bottom rows into the staged output rows: 16 chunks of 16 B per sample, un-swizzled
+    if (tid < 64) {
+      const int ss = tid >> 4, c = tid & 15;
+      const int row = 104 + ss, panel = c >> 3, cp = c & 7;
+      *reinterpret_cast<uint4*>(stage + ss * kIntOutRow + c * 16) =
+          *reinterpret_cast<const uint4*>(buf + panel * kIntPanel + row * 128 + ((cp ^ (row & 7)) << 4));
+    } else if (tid < 68) {
+      reinterpret_cast<__half*>(stage + (tid - 64) * kIntOutRow)[479] = __float2half_rn(0.0f);
     }
-    if (lane < 26) {
-      // tile row `lane` is embedding lane = feature a = lane + 1 of F = [bot; e_0 .. e_25]; its
-      // pairs (a, b < a) start at a (a - 1) / 2: b = 0 is the bottom output (tile row 26),
-      // b = j + 1 is embedding j (tile row j)
-      const int a = lane + 1;
-      __half* z = srow + 128 + a * (a - 1) / 2;
-      z[0] = __float2half_rn(__uint_as_float(v[26]));
-      for (int j = 0; j < lane; ++j) z[j + 1] = __float2half_rn(__uint_as_float(v[j]));
+    if (s >= 0) {
+      // z entries of feature a = i + 1 (after the bottom output, feature 0): pairs (a, 0) .. (a, a - 1)
+      const int a = i + 1;
+      __half* z = reinterpret_cast<__half*>(stage + s * kIntOutRow) + 128 + a * (a - 1) / 2;
+      const float bd = __uint_as_float(s == 0 ? vb[8] : s == 1 ? vb[9] : s == 2 ? vb[10] : vb[11]);
+      z[0] = __float2half_rn(bd);
+      const int j0 = c0 - 26 * s;  // embedding index of window column 0
+#pragma unroll
+      for (int jj = 0; jj < 64; ++jj) {
+        const int j = j0 + jj;
+        if (j >= 0 && j < i) z[j + 1] = __float2half_rn(__uint_as_float(v[jj]));
+      }
     }
-    if (lane == 31) srow[479] = __float2half_rn(0.0f);
-    __syncwarp();
-    if (ok && g < m) {
-      const uint4* src = reinterpret_cast<const uint4*>(srow);
-      uint4* dst = reinterpret_cast<uint4*>(out + g * 480);
-      for (int c = lane; c < 60; c += 32) dst[c] = src[c];
+    __syncthreads();
+    for (int q = tid; q < kIntSamples * 60; q += kIntThreads) {
+      const int ss = q / 60, c = q % 60;
+      const int64_t g = t * kIntSamples + ss;
+      if (g < m)
+        reinterpret_cast<uint4*>(out + g * 480)[c] = *reinterpret_cast<const uint4*>(stage + ss * kIntOutRow + c * 16);
     }
     tc_fence_before();
-    // TMEM and the tile are reused by the next tile; a wait that ran out anywhere ends the loop
-    // in every thread at the same point
+    // TMEM, the staged rows and this buffer are reused; a wait that ran out ends the loop in every
+    // thread at the same point
     ok = __syncthreads_and(ok) != 0;
     tc_fence_after();
   }
@@ -150,12 +170,15 @@ int launch_dlrm_interaction(int64_t m, const void* bot, const void* sparse, void
   static unsigned long long done_mask = 0;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(&dlrm_interaction_kernel), kIntSmem, &done_mask);
   if (rc != GP_OK) return rc;
+  CUtensorMap tm_e, tm_b;
+  rc = make_tmap_2d(&tm_e, sparse, GP_F16, static_cast<uint64_t>(m) * 26, 128, 64, 104, 128);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm_b, bot, GP_F16, static_cast<uint64_t>(m), 128, 64, 4, 128);
+  if (rc != GP_OK) return rc;
   const int64_t tiles = (m + kIntSamples - 1) / kIntSamples;
-  const int64_t want = static_cast<int64_t>(4) * sm_count;
+  const int64_t want = static_cast<int64_t>(3) * sm_count;
   const int grid = static_cast<int>(tiles < want ? tiles : want);
-  dlrm_interaction_kernel<<<grid, kIntThreads, kIntSmem, stream>>>(
-      static_cast<const __half*>(bot), static_cast<const __half*>(sparse), static_cast<__half*>(out), m,
-      status, timeout_ns);
+  dlrm_interaction_kernel<<<grid, kIntThreads, kIntSmem, stream>>>(tm_e, tm_b, static_cast<__half*>(out), m,
+                                                                    status, timeout_ns);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "interaction launch: %s", cudaGetErrorString(e));
 }
