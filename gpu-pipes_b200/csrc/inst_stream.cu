@@ -16,6 +16,7 @@ struct ChainDlrmBot {
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 2;
   static constexpr bool SPLIT_ACT = false;
+  static constexpr bool EPI_PAIRS = false;
 };
 
 // GraphCast-style edge / node MLP (apps/gc_edges/torch/model.py:4-14): K0 -> 512 act -> 512, LN.
