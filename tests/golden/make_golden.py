@@ -1,6 +1,7 @@
 """Generate the golden fixtures in this directory from the REFERENCE's own PyTorch models.
 
-Run in a checkout that has the reference source tree (default /root/reference, or $GP_REFERENCE):
+Run where the reference source tree is available ($GP_REFERENCE, default: a directory named
+`reference` beside this repository):
     python tests/golden/make_golden.py
 It imports the reference's model classes straight from its sources
 (common/mlps.py MgnMlp/DlrmMlp, apps/bert_ffn/torch/model.py BertFfn,
@@ -73,7 +74,7 @@ def _save(name: str, **arrays):
 
 
 def main() -> None:
-    ref = Path(os.environ.get("GP_REFERENCE", "/root/reference"))
+    ref = Path(os.environ.get("GP_REFERENCE", ROOT.parent / "reference"))
     mlps = _load(ref, "common/mlps.py", "ref_mlps")
     torch.manual_seed(0)
     rows = 48
