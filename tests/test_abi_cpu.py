@@ -91,3 +91,84 @@ def test_knobs():
     with pytest.raises(L.GpError):
         L.set_fault_injection(7)
     assert L.launch_count() >= 0
+
+
+P = ctypes.c_void_p
+
+
+def _arr(vals):
+    return (ctypes.c_void_p * len(vals))(*vals)
+
+
+def _edge(m=256, n=100, nf=0x10000, ef=0x20000, src=0x30000, dst=0x38000, w=(0x40000, 0x50000, 0x60000),
+          b=None, agg=None, out=0x70000):
+    return L.lib().gp_mgn_edge_update_out(m, n, P(nf), P(ef), P(src), P(dst), _arr(list(w)),
+                                          None if b is None else _arr(list(b)), None, None, P(out),
+                                          None if agg is None else P(agg), None)
+
+
+def test_mgn_edge_update_argument_checks():
+    assert _edge(m=0) == L.GP_OK  # nothing to do, no device touched
+    assert _edge(m=-1) == L.GP_ERR_ARG
+    assert _edge(m=2**31) == L.GP_ERR_SHAPE
+    assert _edge(n=0) == L.GP_ERR_ARG
+    assert _edge(n=2**25 + 1) == L.GP_ERR_SHAPE  # 32-bit node row offsets in the kernel
+    assert _edge(nf=0) == L.GP_ERR_ARG
+    assert _edge(dst=0) == L.GP_ERR_ARG
+    assert _edge(ef=0x20008) == L.GP_ERR_ALIGN
+    assert _edge(src=0x30004) == L.GP_ERR_ALIGN
+    assert _edge(agg=0x80004) == L.GP_ERR_ALIGN
+    assert _edge(w=(0x40000, 0x50002, 0x60000)) == L.GP_ERR_ALIGN
+    assert _edge(b=(0x90000, 0x90002, None)) == L.GP_ERR_ALIGN
+
+
+def _node(n=256, n_sets=1, nf=0x10000, aggs=(0x20000, 0x28000), w=(0x40000, 0x50000, 0x60000),
+          out=0x70000):
+    return L.lib().gp_mgn_node_update_out(n, n_sets, P(nf), _arr(list(aggs)), _arr(list(w)), None,
+                                          None, None, P(out), None)
+
+
+def test_mgn_node_update_argument_checks():
+    assert _node(n=0) == L.GP_OK
+    assert _node(n=-5) == L.GP_ERR_ARG
+    assert _node(n_sets=3) == L.GP_ERR_UNSUPPORTED
+    assert _node(n_sets=0) == L.GP_ERR_UNSUPPORTED
+    assert _node(nf=0) == L.GP_ERR_ARG
+    assert _node(n_sets=2, aggs=(0x20000, 0x28004)) == L.GP_ERR_ALIGN
+    assert _node(out=0x70002) == L.GP_ERR_ALIGN
+
+
+def _nerf_full(m=256, x=0x10000, d=0x18000, w=None, out_r=0x70000, out_rgb=0x78000):
+    w = list(w) if w is not None else [0x100000 + 0x10000 * i for i in range(12)]
+    return L.lib().gp_nerf_full_out(m, P(x), P(d), _arr(w), None, P(out_r), P(out_rgb), None)
+
+
+def test_nerf_full_argument_checks():
+    assert _nerf_full(m=0) == L.GP_OK
+    assert _nerf_full(m=-1) == L.GP_ERR_ARG
+    assert _nerf_full(d=0) == L.GP_ERR_ARG
+    assert _nerf_full(out_rgb=0) == L.GP_ERR_ARG
+    w = [0x100000 + 0x10000 * i for i in range(12)]
+    w[9] = 0
+    assert _nerf_full(w=w) == L.GP_ERR_ARG and "w[9]" in L.last_error()
+    w[9] = 0x190008
+    assert _nerf_full(w=w) == L.GP_ERR_ALIGN
+    assert _nerf_full(x=0x10002) == L.GP_ERR_ALIGN
+
+
+def test_dlrm_interaction_argument_checks():
+    f = L.lib().gp_dlrm_interaction_out
+    assert f(0, P(0x10000), P(0x20000), P(0x30000), None) == L.GP_OK
+    assert f(-1, P(0x10000), P(0x20000), P(0x30000), None) == L.GP_ERR_ARG
+    assert f(64, None, P(0x20000), P(0x30000), None) == L.GP_ERR_ARG
+    assert f(64, P(0x10000), P(0x20008), P(0x30000), None) == L.GP_ERR_ALIGN
+
+
+def test_fused_mlp_host_argument_checks():
+    f = L.lib().gp_fused_mlp_host
+    s = mgn(256)
+    w = _arr([0x30000, 0x31000, 0x32000])
+    assert f(None, 16, P(0x1000), w, None, None, None, P(0x2000), 0, None) == L.GP_ERR_ARG
+    assert f(ctypes.byref(s), -1, P(0x1000), w, None, None, None, P(0x2000), 0, None) == L.GP_ERR_ARG
+    assert f(ctypes.byref(s), 0, P(0x1000), w, None, None, None, P(0x2000), 0, None) == L.GP_OK
+    assert f(ctypes.byref(s), 16, None, w, None, None, None, P(0x2000), 0, None) == L.GP_ERR_ARG
