@@ -83,3 +83,14 @@ def test_nerf_full_input_layout():
     norms = d_full[:, :3].float().norm(dim=1)
     assert torch.allclose(norms, torch.ones_like(norms), atol=2e-3)
     assert torch.all(d_full[:, 27:] == 0) and torch.all(x_full[:, 63:] == 0)
+
+
+def test_mgn_mp_rank_graphs_distinct_and_reproducible():
+    """Under weak scaling each rank builds its own graph from its row offset: the same rank gets
+    the same bytes, different ranks different graphs."""
+    w = W.WORKLOADS["mgn_mp"].with_m(4096)
+    g0 = W.make_input(w.with_m(4096), 0, 4096)
+    g1 = W.make_input(w.with_m(2 * 4096), 4096, 4096)
+    assert torch.equal(g0, W.make_input(w.with_m(4096), 0, 4096))
+    assert torch.equal(g1, W.make_input(w.with_m(2 * 4096), 4096, 4096))
+    assert not torch.equal(g0, g1)
