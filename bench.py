@@ -6,9 +6,11 @@ A step is one pass of the fused MLP over one batch: M rows of the configured wor
 `mgn_node`: MeshGraphNet node MLP, 1,048,576 rows, 256->128->128->128 + LayerNorm, fp16 -- the
 second benchmark config, the one the headline metric is quoted on that fits one GPU).
 
-Multi-GPU (torchrun, one process per GPU): rows are independent, so each rank runs its own
-M-row slice of an N*M-row job (weak scaling, no collective on the data path; NCCL is used only
-for the barrier and the max-over-ranks of the timing).
+Multi-GPU (torchrun, one process per GPU): rows are independent, so the M rows of the config are
+split into contiguous, tile-aligned row ranges, one per rank (strong scaling, the default for
+N > 1: global M fixed, as the benchmark configs specify). `--split weak` instead gives every rank
+its own M-row slice of an N*M-row job. There is no collective on the data path; NCCL is used only
+for the barrier and the max-over-ranks of the timing.
 
 Reported:
   value       rows/s over all ranks, inputs already resident in HBM, CUDA-event timed
@@ -48,10 +50,10 @@ from gpu_pipes_b200 import _lib as L  # noqa: E402
 from gpu_pipes_b200 import workloads as W  # noqa: E402
 
 L2_BYTES = 126 * 2**20
-# DRAM bytes (read + write) per row of one launch of the fused kernel, from ncu captures
-# (profiles/mlp_resident_mgn_node.md, profiles/mlp_stream_nerf_gc.md,
-# profiles/dlrm_interaction_kernel.md, profiles/mlp_resident_mgn_edge_gather.md: for mgn_mp the
-# edge kernel only); traffic grows with rows.
+# DRAM bytes (read + write) per row of one launch of the dominant kernel: constants taken from
+# ncu captures of that kernel (dram__bytes_read.sum + dram__bytes_write.sum over the captured
+# launch, divided by its rows; for mgn_mp the edge kernel only). Not measured by this script:
+# the line marks them as such. Traffic grows in proportion to the rows.
 NCU_TRAFFIC_PER_ROW = {"mgn_node": 752.7e6 / 1048576, "nerf": 144.1e6 / 1048576,
                        "gc_edge": 497.7e6 / 131072, "dlrm_interact": 507.5e6 / 65536,
                        "mgn_mp": 744.5e6 / 1048576}
@@ -64,6 +66,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--config", default="mgn_node", choices=sorted(W.WORKLOADS))
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--split", default=None, choices=["strong", "weak"],
+                   help="multi-GPU row split: strong (default; the config's M rows shared by the "
+                        "ranks) or weak (M rows per rank)")
     p.add_argument("--m", type=int, default=0, help="override rows per GPU (testing only)")
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=8.0)
@@ -164,9 +169,14 @@ def cpu_oracle_rate(w, seconds: float) -> dict:
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": rows / dt, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": rows / dt, "unit": "rows/s", "cores": torch.get_num_threads(),
+            "cpu_count": os.cpu_count(), "kind": "port",
             "sample": f"{rows} rows of {w.name} in {rows // W.CHUNK_ROWS} x 65,536-row chunks, "
                       f"fp32 PyTorch on the host ({dt:.1f} s)"}
+
+
+def split_mode(args, world: int) -> str:
+    return args.split or "strong"  # at N = 1 both modes run the config's M rows
 
 
 def run_reference(args, w, rank: int):
@@ -177,14 +187,17 @@ def run_reference(args, w, rank: int):
 
     torch.set_num_threads(os.cpu_count() or 1)
     layers, ln = W.make_weights(w)
-    # size each step so the whole run takes about a minute
+    # every step runs the config's full M rows (the same work as one step of the GPU arm) unless
+    # that would take the whole run past about three minutes; then a bounded sample
     x_cal = W.make_input(w, 0, 4096)
+    O.workload_forward(w, x_cal, layers, ln)
     t0 = time.perf_counter()
     O.workload_forward(w, x_cal, layers, ln)
     per_row = (time.perf_counter() - t0) / 4096
-    budget = 60.0 / max(1, args.steps + args.warmup)
+    budget = 180.0 / max(1, args.steps + args.warmup)
     rows = int(min(w.m, max(256, budget / max(per_row, 1e-9))))
-    rows = max(256, rows // 256 * 256)  # whole tiles (and whole 16-edge node groups for mgn_mp)
+    if rows < w.m:
+        rows = max(256, rows // 256 * 256)  # whole tiles (and whole 16-edge node groups for mgn_mp)
     x = W.make_input(w, 0, rows)
     for _ in range(args.warmup):
         O.workload_forward(w, x, layers, ln)
@@ -196,14 +209,16 @@ def run_reference(args, w, rank: int):
     line = {
         "impl": "reference", "metric": "fused-MLP rows/s", "value": val, "unit": "rows/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "rows_per_step_sampled": rows, "rows_per_gpu": w.m,
-                   "chain": w.widths, "description": w.description},
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": split_mode(args, args.gpus), "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "rows_per_step": rows, "global_rows": w.m,
+                   "same_rows_as_gpu_arm": rows == w.m, "chain": w.widths,
+                   "description": w.description},
         "tflops": val * w.flop_per_row / 1e12,
         "cpu_baseline": {"value": val, "unit": "rows/s", "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"{rows} rows per step of {w.name}, PyTorch fp32 on the host"},
+                         "cpu_count": os.cpu_count(), "kind": "port",
+                         "sample": f"{rows} rows per step of {w.name} ({'all' if rows == w.m else 'a sample'} "
+                                   f"of the config's {w.m}), PyTorch fp32 on the host"},
         "e2e": {"value": val, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -232,9 +247,17 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
     from gpu_pipes_b200 import cuda_ext
 
-    # ---- data: rank r owns rows [r*M, (r+1)*M) of the N*M-row job
-    row0 = rank * w.m
-    x_host = W.make_input(w.with_m(row0 + w.m), row0, w.m).pin_memory()
+    # ---- data. strong: the config's M rows in contiguous 256-row-aligned ranges, one per rank
+    # (weights replicated); weak: rank r owns rows [r*M, (r+1)*M) of an N*M-row job
+    split = split_mode(args, world)
+    if split == "strong":
+        row0, n_rows = W.shard_rows(w.m, world, rank, tile=256)
+        rows_total = w.m
+    else:
+        row0, n_rows = rank * w.m, w.m
+        rows_total = w.m * world
+    x_host = W.make_input(w.with_m(row0 + n_rows), row0, n_rows).pin_memory()
+    w = w.with_m(n_rows)
     layers, ln = W.make_weights(w)
     x = x_host.to(dev)
     wd = [(a.to(dev), b.to(dev)) for a, b in layers]
@@ -310,7 +333,6 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    rows_total = w.m * world
     value = rows_total / (ms_step / 1e3)
 
     if args.kernel_only:
@@ -371,7 +393,7 @@ def main():
         line = {
             "metric": "fused-MLP rows/s", "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": split, "vs_baseline": None,
             "dtype": "f16" if w.dtype == torch.float16 else "bf16", "data": "synthetic",
             "config": {"workload": w.name, "rows_per_gpu": w.m, "global_rows": rows_total,
                        "chain": w.widths, "tail": ["none", "layernorm", "residual+layernorm"][w.tail],
@@ -387,6 +409,8 @@ def main():
             "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak,
                          "traffic": None if tr is None else tr * w.m,
+                         "traffic_source": None if tr is None else
+                             "constant per row from an ncu capture of this kernel (not measured by this run)",
                          "peak_source": f"{peak_note} (MEASURED_PEAKS.json)",
                          "kernel": KERNEL_OF.get(w.name, "mlp_stream_kernel"),
                          "algorithmic_bytes_per_launch": alg_bytes,

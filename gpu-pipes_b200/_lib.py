@@ -106,7 +106,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_mgn_linears_out.restype = _INT
     lib.gp_testmlp_out.argtypes = [_I64] + [_P] * 9
     lib.gp_testmlp_out.restype = _INT
-    lib.gp_dlrm_botmlp_out.argtypes = [_I64] + [_P] * 9
+    lib.gp_dlrm_botmlp_out.argtypes = [_I64, _INT] + [_P] * 9
     lib.gp_dlrm_botmlp_out.restype = _INT
     for name in ("gp_gc_edges_out", "gp_gc_nodes_out"):
         getattr(lib, name).argtypes = [_I64, _INT, _INT] + [_P] * 9
@@ -131,7 +131,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_nerf_full_out.restype = _INT
     lib.gp_dlrm_interaction_out.argtypes = [_I64, _P, _P, _P, _P]
     lib.gp_dlrm_interaction_out.restype = _INT
-    lib.gp_dlrm_topmlp_out.argtypes = [_I64, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P]
+    lib.gp_dlrm_topmlp_out.argtypes = [_I64, _INT, _INT, _P, ctypes.POINTER(_P), ctypes.POINTER(_P), _P, _P]
     lib.gp_dlrm_topmlp_out.restype = _INT
     lib.gp_gc_edges_bf16_noalloc_out.argtypes = [_I64, _INT] + [_P] * 9
     lib.gp_gc_edges_bf16_noalloc_out.restype = _INT

@@ -23,6 +23,7 @@ GP_DECLARE(launch_mgn_ln_bf16_k384_pair)
 GP_DECLARE(launch_mgn_ln_bf16_k256_single)
 GP_DECLARE(launch_mgn_ln_bf16_k128_single)
 GP_DECLARE(launch_dlrm_bot_f16)
+GP_DECLARE(launch_dlrm_bot_f16_k32)
 GP_DECLARE(launch_addln0_f16_h128)
 GP_DECLARE(launch_ffn_resln_f16_h128)
 GP_DECLARE(launch_ffn_resln_bf16_h128)
@@ -34,6 +35,7 @@ GP_DECLARE(launch_nerf_f16)
 GP_DECLARE(launch_nerf_trunk_f16)
 GP_DECLARE(launch_bert_ffn_bf16)
 GP_DECLARE(launch_dlrm_top_f16)
+GP_DECLARE(launch_dlrm_top_f16_ref)
 #undef GP_DECLARE2
 #undef GP_DECLARE
 
@@ -66,6 +68,8 @@ static const ChainEntry kChains[] = {
     {"probe_2l_f16_k128_single", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_single, 1},
     // weight-streaming chains (wide layers)
     {"dlrm_bot_f16", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16, 0},
+    // the reference app's own bottom MLP input width (apps/dlrm_botmlp/pipelined/val.py:11-12)
+    {"dlrm_bot_f16_k32", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32, 0},
     {"gc_silu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {GP_ACT_SILU, NO}, GP_TAIL_LAYERNORM, launch_gc_silu_bf16_k1536, 0},
     {"gc_relu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_bf16_k1536, 0},
     {"gc_relu_f16_k1536", GP_F16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_f16_k1536, 0},
@@ -85,6 +89,9 @@ static const ChainEntry kChains[] = {
      launch_bert_ffn_bf16, 0},
     {"dlrm_top_f16", GP_F16, 5, {480, 1024, 1024, 512, 256, 1}, {R, R, R, R, GP_ACT_SIGMOID},
      GP_TAIL_NONE, launch_dlrm_top_f16, 0},
+    // the reference app's own top MLP (apps/dlrm_topmlp/pipelined/val.py:11-12): ReLU everywhere
+    {"dlrm_top_f16_ref", GP_F16, 5, {512, 1024, 1024, 512, 256, 64}, {R, R, R, R, R},
+     GP_TAIL_NONE, launch_dlrm_top_f16_ref, 0},
 };
 #undef MGN
 #undef R

@@ -42,6 +42,7 @@ void set_kernel_variant(int v);
 
 // helpers implemented in gp_abi.cu
 int set_error(int code, const char* fmt, ...);
+void clear_error();
 // swizzle_bytes: 128, 64, 32 or 0 (none)
 // ld: row stride in elements (0 = cols, a contiguous matrix)
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
@@ -76,6 +77,15 @@ int make_tmap_w3d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, 
 // want the workspace of this device wait.
 int workspace_acquire(size_t bytes, cudaStream_t stream, void** ptr);
 void workspace_release(cudaStream_t stream);
+
+// Library-wide knobs set through the C ABI (gp_abi.cu): the device wait budget, the host-side
+// fault injection mode, and the launch counter behind gp_launch_count.
+unsigned long long current_timeout_ns();
+int current_fault_injection();
+void count_launches(int n);
+// Status word of the allocation-free entry point on the current device (noalloc.cu); clears it
+// when `clear` is set. The caller synchronises the device first.
+int noalloc_status(bool clear, int* status);
 
 // Sets the dynamic shared memory attribute of `kern` once per device.
 int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask);

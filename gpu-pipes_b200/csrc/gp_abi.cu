@@ -50,6 +50,10 @@ static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_inject{0};
 static std::atomic<uint64_t> g_launches{0};
 
+unsigned long long current_timeout_ns() { return g_timeout_ns.load(); }
+int current_fault_injection() { return g_inject.load(); }
+void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+
 static bool sync_check_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("GP_SYNC_CHECK");
@@ -505,11 +509,12 @@ int gp_mgn_linears_out(int64_t m, int k0, const void* x, const void* w1, const v
   return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
 }
 
-int gp_dlrm_botmlp_out(int64_t m, const void* x, const void* w1, const void* b1, const void* w2,
-                       const void* b2, const void* w3, const void* b3, void* out, void* stream) {
+int gp_dlrm_botmlp_out(int64_t m, int k0, const void* x, const void* w1, const void* b1,
+                       const void* w2, const void* b2, const void* w3, const void* b3, void* out,
+                       void* stream) {
   gp_mlp_spec s{};
   s.n_layers = 3;
-  const int wd[4] = {16, 512, 256, 128};
+  const int wd[4] = {k0, 512, 256, 128};
   for (int i = 0; i < 4; ++i) s.widths[i] = wd[i];
   for (int i = 0; i < 3; ++i) s.act[i] = GP_ACT_RELU;
   s.tail = GP_TAIL_NONE;
@@ -566,15 +571,17 @@ int gp_bert_ffn_out(int64_t m, const void* x, const void* w1, const void* b1, co
   return fused_mlp(&s, m, x, w, b, gamma, beta, out, static_cast<cudaStream_t>(stream));
 }
 
-int gp_dlrm_topmlp_out(int64_t m, const void* x, const void* const* w, const void* const* b,
-                       void* out, void* stream) {
+int gp_dlrm_topmlp_out(int64_t m, int k0, int n_out, const void* x, const void* const* w,
+                       const void* const* b, void* out, void* stream) {
   if (w == nullptr) return set_error(GP_ERR_ARG, "w is NULL");
   gp_mlp_spec s{};
   s.n_layers = 5;
-  const int wd[6] = {480, 1024, 1024, 512, 256, 1};
+  const int wd[6] = {k0, 1024, 1024, 512, 256, n_out};
   for (int i = 0; i < 6; ++i) s.widths[i] = wd[i];
   for (int i = 0; i < 4; ++i) s.act[i] = GP_ACT_RELU;
-  s.act[4] = GP_ACT_SIGMOID;
+  // a single output is the click probability (sigmoid); the reference app's 64-wide output is
+  // followed by DlrmMlp's ReLU
+  s.act[4] = n_out == 1 ? GP_ACT_SIGMOID : GP_ACT_RELU;
   s.tail = GP_TAIL_NONE;
   s.dtype = GP_F16;
   return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
@@ -808,6 +815,12 @@ int gp_device_status(int device, int clear, int* status_out) {
     if (e == cudaSuccess && clear) e = cudaMemset(st->status, 0, sizeof(int));
     if (e == cudaSuccess && clear) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "status: %s", cudaGetErrorString(e));
+  }
+  if (rc == GP_OK) {
+    // the allocation-free entry point keeps its own status word (a file-scope device variable)
+    int h_na = 0;
+    rc = noalloc_status(clear != 0, &h_na);
+    if (h == 0) h = h_na;
   }
   cudaSetDevice(prev);
   if (status_out != nullptr) *status_out = h;

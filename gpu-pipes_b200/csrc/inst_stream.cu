@@ -5,11 +5,14 @@
 
 namespace gp {
 
-// DLRM bottom MLP (common/mlps.py:23-35 DlrmMlp([13, 512, 256, 128])), input padded 13 -> 16.
+// DLRM bottom MLP (common/mlps.py:23-35 DlrmMlp([K0, 512, 256, 128])): K0 = 16 is BASELINE's
+// 13 dense features padded to 16; K0 = 32 is the reference app's own width
+// (apps/dlrm_botmlp/pipelined/val.py:11-12, DlrmMlp([13 + 19, 512, 256, 128]), x [M, 32]).
+template <int K0_>
 struct ChainDlrmBot {
   using T = __half;
   static constexpr int NL = 3;
-  __host__ __device__ static constexpr int K(int l) { return l == 0 ? 16 : (l == 1 ? 512 : 256); }
+  __host__ __device__ static constexpr int K(int l) { return l == 0 ? K0_ : (l == 1 ? 512 : 256); }
   __host__ __device__ static constexpr int N(int l) { return l == 0 ? 512 : (l == 1 ? 256 : 128); }
   __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
   static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
@@ -221,7 +224,8 @@ int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void
   return rc;
 }
 
-int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot>(c); }
+int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot<16>>(c); }
+int launch_dlrm_bot_f16_k32(const LaunchCtx& c) { return launch_stream<ChainDlrmBot<32>>(c); }
 int launch_gc_silu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActSilu>, 2>(c); }
 int launch_gc_relu_bf16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__nv_bfloat16, 1536, kActRelu>, 2>(c); }
 int launch_gc_relu_f16_k1536(const LaunchCtx& c) { return launch_stream<ChainGc<__half, 1536, kActRelu>, 2>(c); }

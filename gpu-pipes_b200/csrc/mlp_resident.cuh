@@ -116,28 +116,38 @@ __device__ __forceinline__ void epi_hidden(const uint32_t (&v)[N / 32][32], uint
   }
 }
 
-// Mean and rstd of one row (one-pass sum / sum of squares in fp32, four f32x2 chains).
+// Mean and rstd of one row, in two passes over the registers as common/layer_norm_v2.cuh:34-62
+// does: the mean first, then the biased variance as the mean of (v - mean)^2. A one-pass
+// E[v^2] - mean^2 cancels catastrophically when |mean| is large against the row's spread.
+// Packed f32x2 arithmetic, four independent chains per pass.
 template <int N>
 __device__ __forceinline__ void row_stats(const uint32_t (&v)[N / 32][32], float eps, float& mean,
                                           float& rstd) {
-  float2 s[4], q[4];
+  float2 s[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    s[i] = make_float2(0.f, 0.f);
-    q[i] = make_float2(0.f, 0.f);
-  }
+  for (int i = 0; i < 4; ++i) s[i] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < N / 32; ++c)
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      s[j & 3] = __fadd2_rn(s[j & 3],
+                            make_float2(__uint_as_float(v[c][2 * j]), __uint_as_float(v[c][2 * j + 1])));
+  const float2 s01 = __fadd2_rn(__fadd2_rn(s[0], s[1]), __fadd2_rn(s[2], s[3]));
+  mean = (s01.x + s01.y) * (1.0f / N);
+  const float2 nm = make_float2(-mean, -mean);
+  float2 q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < N / 32; ++c)
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const float2 p = make_float2(__uint_as_float(v[c][2 * j]), __uint_as_float(v[c][2 * j + 1]));
-      s[j & 3] = __fadd2_rn(s[j & 3], p);
-      q[j & 3] = __ffma2_rn(p, p, q[j & 3]);
+      const float2 d = __fadd2_rn(
+          make_float2(__uint_as_float(v[c][2 * j]), __uint_as_float(v[c][2 * j + 1])), nm);
+      q[j & 3] = __ffma2_rn(d, d, q[j & 3]);
     }
-  const float2 s01 = __fadd2_rn(__fadd2_rn(s[0], s[1]), __fadd2_rn(s[2], s[3]));
   const float2 q01 = __fadd2_rn(__fadd2_rn(q[0], q[1]), __fadd2_rn(q[2], q[3]));
-  mean = (s01.x + s01.y) * (1.0f / N);
-  const float var = fmaxf((q01.x + q01.y) * (1.0f / N) - mean * mean, 0.0f);
+  const float var = (q01.x + q01.y) * (1.0f / N);
   rstd = rsqrtf(var + eps);
 }
 

@@ -741,9 +741,15 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
           float mean = 0.f, rstd = 1.f;
           if constexpr (L::kLN) {
             if (!wait_acc(0) || (NH == 2 && !wait_acc(1))) { ok = false; break; }
-            float s = 0.f, sq = 0.f;
+            // Row statistics without the cancellation of E[y^2] - mean^2: each warp of the pair
+            // accumulates sum and sum of squares of (y - k), k = its first value of the row, so
+            // its partial mean and M2 = sum (y - mean_w)^2 are exact to rounding; the two
+            // halves are combined with the parallel-variance formula (Chan et al., 1979). The
+            // result equals the two-pass mean / biased variance of common/layer_norm_v2.cuh:34-62.
+            float s = 0.f, sq = 0.f, k = 0.f;
+            constexpr int kChunks = C::N(NL - 1) / 32;
 #pragma unroll 1
-            for (int c = eg; c < C::N(l) / 32; c += 2) {
+            for (int c = eg; c < kChunks; c += 2) {
               uint32_t v[32];
               tmem_ld32(t_lane + dcol + c * 32, v);
               tmem_wait_ld();
@@ -751,21 +757,31 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
 #pragma unroll
               for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(v[i]) + bl[c * 32 + i];
               resid_add(c, y);
+              if (c == eg) k = y[0];
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                s += y[i];
-                sq = fmaf(y[i], y[i], sq);
+                const float d = y[i] - k;
+                s += d;
+                sq = fmaf(d, d, sq);
               }
             }
+            const float n_me = 32.0f * ((kChunks - eg + 1) / 2);
+            const float mean_me = k + s / n_me;
+            const float m2_me = fmaxf(sq - s * (s / n_me), 0.0f);
             float2* xs = reinterpret_cast<float2*>(xchg);
-            xs[eg * kBM + r] = make_float2(s, sq);
+            xs[eg * kBM + r] = make_float2(mean_me, m2_me);
             if (!pair_sync()) { ok = false; break; }
             const float2 other = xs[(eg ^ 1) * kBM + r];
             if (!pair_sync()) { ok = false; break; }  // the exchange slots are free again
-            s += other.x;
-            sq += other.y;
-            mean = s * (1.0f / C::N(l));
-            rstd = rsqrtf(fmaxf(sq * (1.0f / C::N(l)) - mean * mean, 0.0f) + args.ln_eps);
+            // evaluate in warp order (even half first) so that both warps get identical bits
+            const float2 h0 = eg == 0 ? make_float2(mean_me, m2_me) : other;
+            const float2 h1 = eg == 0 ? other : make_float2(mean_me, m2_me);
+            const float n0 = 32.0f * ((kChunks + 1) / 2), n1 = 32.0f * (kChunks / 2);
+            const float inv_n = 1.0f / C::N(l);
+            mean = (h0.x * n0 + h1.x * n1) * inv_n;
+            const float delta = h1.x - h0.x;
+            const float var = (h0.y + h1.y + delta * delta * (n0 * n1 * inv_n)) * inv_n;
+            rstd = rsqrtf(var + args.ln_eps);
           }
 #pragma unroll 1
           for (int hf = 0; hf < NH; ++hf) {

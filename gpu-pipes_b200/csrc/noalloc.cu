@@ -17,8 +17,14 @@
 //     needs to start at zero). Calls whose kernels overlap on the GPU -- on different streams
 //     without ordering between them -- race on the buffer; order them (one stream, or events).
 //   * Chains whose converted weights exceed the buffer are rejected with GP_ERR_SHAPE.
-//   * Device-side timeouts are recorded in a status word of this file (not the one
-//     gp_device_status reads); the kernel still exits cleanly.
+//   * Device waits are bounded by the library's wait budget (gp_set_timeout_ns) and honour the
+//     host-side fault injection (gp_set_fault_injection). A wait that runs out records its code in
+//     a status word of this file -- also a file-scope __device__ variable, so reporting needs no
+//     allocation either -- and the kernel exits cleanly; gp_device_status reads and clears that
+//     word together with the library's own.
+//   * The kernel is the single-CTA form of the weight-streaming chain kernel (the regular bf16
+//     GraphCast entry point runs the CTA-pair form), so timings differ; both meet the same
+//     tolerance against the fp32 model.
 //
 // Nothing here calls cudaMalloc, cudaMallocAsync, cudaFree or any other allocating routine.
 #include <cuda_runtime.h>
@@ -66,7 +72,7 @@ struct NoAllocDevice {
   void* scratch = nullptr;   // device address of g_noalloc_scratch
   int* status = nullptr;     // device address of g_noalloc_status
   int sm_count = 0;
-  bool attr_relu = false, attr_silu = false;
+  bool attr_relu = false, attr_silu = false;  // guarded by g_na_mu
 };
 
 std::mutex g_na_mu;
@@ -135,11 +141,14 @@ int na_launch(NoAllocDevice& d, int64_t m, const void* x, const void* w0, const 
               cudaStream_t stream, bool* attr_done) {
   using C = ChainGcNoAlloc<ACT0>;
   using Lay = StreamLayout<C>;
-  if (!*attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(&mlp_stream_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Lay::kSmemBytes);
-    if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    *attr_done = true;
+  {
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    if (!*attr_done) {
+      cudaError_t e = cudaFuncSetAttribute(&mlp_stream_kernel<C>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kSmemBytes);
+      if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      *attr_done = true;
+    }
   }
   // fp16 copy of the second layer's weights into the fixed buffer
   const int64_t n1 = static_cast<int64_t>(C::K(1)) * C::N(1);
@@ -169,16 +178,32 @@ int na_launch(NoAllocDevice& d, int64_t m, const void* x, const void* w0, const 
   args.out = out;
   args.ln_eps = 1e-5f;
   args.status = d.status;
-  args.timeout_ns = 2000000000ull;
+  args.timeout_ns = current_timeout_ns();
+  args.inject = current_fault_injection();
   const int grid = args.num_tiles < d.sm_count ? args.num_tiles : d.sm_count;
   mlp_stream_kernel<C><<<grid, Lay::kThreads, Lay::kSmemBytes, stream>>>(tm, args);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "launch: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "launch: %s", cudaGetErrorString(e));
+  count_launches(2);  // the weight conversion and the chain kernel
+  return GP_OK;
 }
 
 bool na_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 }  // namespace
+
+int noalloc_status(bool clear, int* status) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&h, g_noalloc_status, sizeof(int));
+  if (e == cudaSuccess && clear && h != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_noalloc_status, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "no-alloc status: %s", cudaGetErrorString(e));
+  *status = h;
+  return GP_OK;
+}
+
 }  // namespace gp
 
 using namespace gp;
@@ -187,6 +212,7 @@ extern "C" int gp_gc_edges_bf16_noalloc_out(int64_t m, int act, const void* x, c
                                             const void* b0, const void* w1, const void* b1,
                                             const void* gamma, const void* beta, void* out,
                                             void* stream) {
+  clear_error();
   if (m < 0) return set_error(GP_ERR_ARG, "m = %lld is negative", (long long)m);
   if (m >= (int64_t(1) << 31)) return set_error(GP_ERR_SHAPE, "m = %lld exceeds 2^31-1", (long long)m);
   if (act != GP_ACT_RELU && act != GP_ACT_SILU)

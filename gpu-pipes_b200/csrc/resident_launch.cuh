@@ -1,6 +1,7 @@
 // Host launchers for the weight-resident chain kernel (single CTA and CTA pair).
 #pragma once
 
+#include <atomic>
 #include <cstring>
 
 #include "chain_registry.h"
@@ -20,7 +21,7 @@ int launch_resident_cg(const LaunchCtx& c) {
     kern = reinterpret_cast<const void*>(&mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>);
   }
   static unsigned long long done_mask = 0;
-  static int max_clusters[64] = {0};
+  static std::atomic<int> max_clusters[64];
   constexpr int kThr = resident_threads<L, XM>();
   constexpr int kSmem = resident_smem<L, XM>();
   static_assert(kSmem <= kSmemLimit, "shared memory budget");
@@ -46,7 +47,8 @@ int launch_resident_cg(const LaunchCtx& c) {
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
-    int& mc = max_clusters[dev & 63];
+    std::atomic<int>& mc_slot = max_clusters[dev & 63];  // filled once per device; racing first calls store the same value
+    int mc = mc_slot.load(std::memory_order_relaxed);
     if (mc == 0) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (c.sm_count / 2), 1, 1);
@@ -66,6 +68,7 @@ int launch_resident_cg(const LaunchCtx& c) {
         n = c.sm_count / 2;
       }
       mc = n;
+      mc_slot.store(n, std::memory_order_relaxed);
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
     mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>

@@ -2,6 +2,7 @@
 // (CTA pairs over 256-row units, each CTA staging half of every weight stage).
 #pragma once
 
+#include <atomic>
 #include <cstring>
 
 #include "chain_registry.h"
@@ -27,7 +28,7 @@ int launch_stream(const LaunchCtx& c) {
     kern = reinterpret_cast<const void*>(&mlp_stream_kernel<C>);
   }
   static unsigned long long done_mask = 0;
-  static int max_clusters[64] = {0};
+  static std::atomic<int> max_clusters[64];
   int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
   if (rc != GP_OK) return rc;
   const int dt = c.spec->dtype;
@@ -77,7 +78,8 @@ int launch_stream(const LaunchCtx& c) {
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
-    int& mc = max_clusters[dev & 63];
+    std::atomic<int>& mc_slot = max_clusters[dev & 63];  // filled once per device; racing first calls store the same value
+    int mc = mc_slot.load(std::memory_order_relaxed);
     if (mc == 0) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (c.sm_count / 2), 1, 1);
@@ -97,6 +99,7 @@ int launch_stream(const LaunchCtx& c) {
         n = c.sm_count / 2;
       }
       mc = n;
+      mc_slot.store(n, std::memory_order_relaxed);
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
     mlp_stream_pair_kernel<C><<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);

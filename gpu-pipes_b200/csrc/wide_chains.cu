@@ -2,12 +2,16 @@
 //   BERT-large FFN  ln(x + W2 gelu(W1 x + b1) + b2), 1024 -> 4096 -> 1024, bf16
 //                   (apps/bert_ffn/torch/model.py:4-15 at BERT-large widths, GELU(tanh))
 //   DLRM top MLP    480 -> 1024 -> 1024 -> 512 -> 256 -> 1, ReLU, sigmoid at the end, fp16
-//                   (common/mlps.py:23-35 DlrmMlp([479, 1024, 1024, 512, 256, 1], sigmoid_i=4))
+//                   (common/mlps.py:23-35 DlrmMlp([479, 1024, 1024, 512, 256, 1], sigmoid_i=4)),
+//                   and the reference app's own widths 512 -> 1024 -> 1024 -> 512 -> 256 -> 64
+//                   with ReLU after every layer (apps/dlrm_topmlp/pipelined/val.py:11-12,
+//                   DlrmMlp([479 + 33, 1024, 1024, 512, 256, 64]); dlrm_topmlp_pl_ext.cu:34-40)
 // Each chain runs over large row chunks whose intermediates live in the per-device workspace
 // (measured faster than L2-sized chunks: fewer launches and partial waves, and the HBM traffic of
 // the intermediates overlaps the GEMMs); each wide layer is one mlp_gemm_pair_kernel launch; the
 // tail (LayerNorm, or the last two DLRM layers with the sigmoid head) is a row kernel / the
 // weight-streaming chain kernel.
+#include <atomic>
 #include <cstring>
 
 #include "chain_registry.h"
@@ -22,13 +26,14 @@ template <int ACT, bool OUT_F32>
 int gemm_launch_t(cudaStream_t s, int sm_count, const TensorMaps& tm, const GemmArgs& g, int a_bf16) {
   using L = GemmLayoutT<2>;
   static unsigned long long done_mask = 0;
-  static int max_clusters[64] = {0};
+  static std::atomic<int> max_clusters[64];
   const void* kern = reinterpret_cast<const void*>(&mlp_gemm_pair_kernel<ACT, OUT_F32>);
   int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
   if (rc != GP_OK) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
-  int& mc = max_clusters[dev & 63];
+  std::atomic<int>& mc_slot = max_clusters[dev & 63];  // filled once per device; racing first calls store the same value
+  int mc = mc_slot.load(std::memory_order_relaxed);
   if (mc == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (sm_count / 2), 1, 1);
@@ -48,6 +53,7 @@ int gemm_launch_t(cudaStream_t s, int sm_count, const TensorMaps& tm, const Gemm
       n = sm_count / 2;
     }
     mc = n;
+    mc_slot.store(n, std::memory_order_relaxed);
   }
   const int clusters = g.num_tiles < mc ? g.num_tiles : mc;
   mlp_gemm_pair_kernel<ACT, OUT_F32><<<2 * clusters, L::kThreads, L::kSmemBytes, s>>>(tm, g, a_bf16);
@@ -117,6 +123,19 @@ struct ChainDlrmTail {
   static constexpr bool SPLIT_ACT = false;
 };
 
+// The reference app's tail: 512 -> 256 (ReLU) -> 64 (ReLU), stored as [M, 64].
+struct ChainDlrmTailRef {
+  using T = __half;
+  static constexpr int NL = 2;
+  __host__ __device__ static constexpr int K(int l) { return l == 0 ? 512 : 256; }
+  __host__ __device__ static constexpr int N(int l) { return l == 0 ? 256 : 64; }
+  __host__ __device__ static constexpr int ACT(int) { return kActRelu; }
+  static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr bool HIDDEN_F16 = false;
+  static constexpr int HALVES = 1;
+  static constexpr bool SPLIT_ACT = false;
+};
+
 }  // namespace
 
 // BERT-large FFN (bf16): hidden activations kept in fp16 (as the other bf16 chains), the second
@@ -162,10 +181,13 @@ int launch_bert_ffn_bf16(const LaunchCtx& c) {
   return rc;
 }
 
-// DLRM top MLP (fp16): three wide layers on mlp_gemm_kernel, then 512 -> 256 -> 1 on the
-// streaming chain kernel. The tail runs once per two row chunks (h3 holds both), so each of its
-// launches has two 128-row tiles per SM to pipeline instead of one.
-int launch_dlrm_top_f16(const LaunchCtx& c) {
+// DLRM top MLP (fp16): three wide layers on mlp_gemm_kernel, then the last two layers (512 -> 256
+// -> 1 sigmoid head, or 512 -> 256 -> 64) on the streaming chain kernel. The tail runs once per two
+// row chunks (h3 holds both), so each of its launches has two 128-row tiles per SM to pipeline
+// instead of one.
+template <class Tail>
+int launch_dlrm_top_t(const LaunchCtx& c) {
+  const int n_out = c.spec->widths[5];
   // Chunks of up to 262,144 rows: the intermediates (h1 + h2 + 2 x h3 = 1.5 GB at full size) go
   // through HBM, but the traffic overlaps the GEMMs and large launches lose little to partial
   // last waves. Measured at M = 262,144: 1.44 ms with 16,384-row (L2-sized) chunks, 1.28 with
@@ -207,7 +229,7 @@ int launch_dlrm_top_f16(const LaunchCtx& c) {
       t.spec = &tail_spec;
       t.m = tail_rows;
       t.x = h3;
-      t.out = static_cast<char*>(c.out) + r0 * 2;
+      t.out = static_cast<char*>(c.out) + r0 * n_out * 2;
       t.w[0] = c.w[3];
       t.w[1] = c.w[4];
       t.args.bias[0] = c.args.bias[3];
@@ -215,11 +237,14 @@ int launch_dlrm_top_f16(const LaunchCtx& c) {
       t.args.m = tail_rows;
       t.args.num_tiles = static_cast<int>((tail_rows + kBM - 1) / kBM);
       t.args.out = t.out;
-      rc = launch_stream<ChainDlrmTail>(t);
+      rc = launch_stream<Tail>(t);
     }
   }
   workspace_release(c.stream);
   return rc;
 }
+
+int launch_dlrm_top_f16(const LaunchCtx& c) { return launch_dlrm_top_t<ChainDlrmTail>(c); }
+int launch_dlrm_top_f16_ref(const LaunchCtx& c) { return launch_dlrm_top_t<ChainDlrmTailRef>(c); }
 
 }  // namespace gp

@@ -188,9 +188,35 @@ def _out_like(x, n):
     return torch.zeros(x.shape[0], n, dtype=x.dtype, device=x.device)
 
 
+def _check_chain(x, ws, bs, out, widths, dtype=torch.float16):
+    """Shapes of a plain chain call: x [M, widths[0]], w_i [widths[i], widths[i+1]], b_i
+    [widths[i+1]] (or None), out [M, widths[-1]]."""
+    _check_input("x", x, dtype)
+    _check_input("out", out, dtype)
+    if x.dim() != 2 or x.shape[1] != widths[0]:
+        raise RuntimeError(f"x has shape {tuple(x.shape)}, expected [M, {widths[0]}]")
+    for i, (w, b) in enumerate(zip(ws, bs)):
+        _check_input(f"w{i + 1}", w, dtype)
+        _check_input(f"b{i + 1}", b, dtype)
+        if w is None or tuple(w.shape) != (widths[i], widths[i + 1]):
+            raise RuntimeError(f"w{i + 1} has shape {None if w is None else tuple(w.shape)}, "
+                               f"expected {(widths[i], widths[i + 1])}")
+        if b is not None and tuple(b.shape) != (widths[i + 1],):
+            raise RuntimeError(f"b{i + 1} has shape {tuple(b.shape)}, expected ({widths[i + 1]},)")
+    if out.dim() != 2 or tuple(out.shape) != (x.shape[0], widths[-1]):
+        raise RuntimeError(f"out has shape {tuple(out.shape)}, expected [{x.shape[0]}, {widths[-1]}]")
+
+
 def dlrm_botmlp_out(x, w1, b1, w2, b2, w3, b3, out) -> None:
-    """x [M, 16] (13 features zero padded) -> 512 -> 256 -> 128, ReLU after every layer."""
-    fused_mlp_out(x, [w1, w2, w3], [b1, b2, b3], out, acts=[L.ACT_RELU] * 3)
+    """x [M, K0] -> 512 -> 256 -> 128, ReLU after every layer. K0 = 32 is the reference app's own
+    input (apps/dlrm_botmlp/pipelined/val.py:11-12, DlrmMlp([13 + 19, 512, 256, 128])); K0 = 16 is
+    13 dense features zero padded (the benchmark config). Calls gp_dlrm_botmlp_out."""
+    _check_input("x", x, torch.float16)
+    k0 = x.shape[1] if x.dim() == 2 else -1
+    _check_chain(x, [w1, w2, w3], [b1, b2, b3], out, [k0, 512, 256, 128])
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_dlrm_botmlp_out(x.shape[0], k0, _ptr(x), _ptr(w1), _ptr(b1), _ptr(w2),
+                                           _ptr(b2), _ptr(w3), _ptr(b3), _ptr(out), _stream(x)))
 
 
 def dlrm_botmlp(x, w1, b1, w2, b2, w3, b3) -> torch.Tensor:
@@ -437,13 +463,26 @@ def dlrm_interaction(bot, sparse) -> torch.Tensor:
 
 
 def dlrm_topmlp_out(x, w1, b1, w2, b2, w3, b3, w4, b4, w5, b5, out) -> None:
-    """x [M, 480] -> 1024 -> 1024 -> 512 -> 256 (ReLU) -> 1 (sigmoid)."""
-    fused_mlp_out(x, [w1, w2, w3, w4, w5], [b1, b2, b3, b4, b5], out,
-                  acts=[L.ACT_RELU] * 4 + [L.ACT_SIGMOID])
+    """Two width sets (gp_dlrm_topmlp_out):
+      * x [M, 512] -> 1024 -> 1024 -> 512 -> 256 -> 64, ReLU after every layer: the reference
+        app's own DlrmMlp([479 + 33, 1024, 1024, 512, 256, 64]) (apps/dlrm_topmlp/pipelined/val.py:11-12);
+      * x [M, 480] -> 1024 -> 1024 -> 512 -> 256 (ReLU) -> 1 (sigmoid): DlrmMlp(..., sigmoid_i=4),
+        the benchmark config."""
+    _check_input("x", x, torch.float16)
+    _check_input("w5", w5, torch.float16)
+    k0 = x.shape[1] if x.dim() == 2 else -1
+    n_out = w5.shape[1] if w5.dim() == 2 else -1
+    ws, bs = [w1, w2, w3, w4, w5], [b1, b2, b3, b4, b5]
+    _check_chain(x, ws, bs, out, [k0, 1024, 1024, 512, 256, n_out])
+    wp = (ctypes.c_void_p * 5)(*[w.data_ptr() for w in ws])
+    bp = (ctypes.c_void_p * 5)(*[(b.data_ptr() if b is not None else None) for b in bs])
+    with torch.cuda.device(x.device):
+        L.check(L.lib().gp_dlrm_topmlp_out(x.shape[0], k0, n_out, _ptr(x), wp, bp, _ptr(out),
+                                           _stream(x)))
 
 
 def dlrm_topmlp(x, *wb) -> torch.Tensor:
-    out = _out_like(x, 1)
+    out = _out_like(x, wb[8].shape[1])
     dlrm_topmlp_out(x, *wb, out)
     return out
 

@@ -112,10 +112,13 @@ GP_API int gp_testmlp_out(int64_t m, const void* x,
                    const void* w1, const void* b1, const void* w2, const void* b2,
                    const void* w3, const void* b3, void* out, void* stream);
 
-/* DLRM bottom MLP, fp16: x [m, 16] (13 dense features, zero padded), 16 -> 512 -> 256 -> 128,
- * ReLU after every layer. w1 is [16, 512] (rows 13..15 multiply the zero padding).
- * Replaces dlrm_botmlp_out (apps/dlrm_botmlp/pipelined/dlrm_botmlp_pl_ext.cu:24-66). */
-GP_API int gp_dlrm_botmlp_out(int64_t m, const void* x,
+/* DLRM bottom MLP, fp16: x [m, k0] -> 512 -> 256 -> 128, ReLU after every layer; w1 is [k0, 512].
+ * k0 = 32 is the reference app's input (apps/dlrm_botmlp/pipelined/val.py:11-12,
+ * DlrmMlp([13 + 19, 512, 256, 128])); k0 = 16 is 13 dense features zero padded to 16 (rows
+ * 13..15 of w1 multiply the padding). Other widths return GP_ERR_UNSUPPORTED.
+ * Replaces dlrm_botmlp_out (apps/dlrm_botmlp/pipelined/dlrm_botmlp_pl_ext.cu:24-66), whose
+ * widths are compile-time; here k0 is an argument, as in gp_mgn_fullmlp_out. */
+GP_API int gp_dlrm_botmlp_out(int64_t m, int k0, const void* x,
                        const void* w1, const void* b1, const void* w2, const void* b2,
                        const void* w3, const void* b3, void* out, void* stream);
 
@@ -159,11 +162,15 @@ GP_API int gp_bert_addln_ffn_out(int64_t m, const void* attn_out, const void* x,
                                  const void* b2, const void* ga0, const void* be0, const void* ga2,
                                  const void* be2, void* out, void* stream);
 
-/* DLRM top MLP, fp16: x [m, 480] (479 interaction features, zero padded) -> 1024 -> 1024 -> 512
- * -> 256 (ReLU) -> 1 (sigmoid); w[5], b[5]; w1 is [480, 1024]; out [m, 1].
- * Replaces dlrm_topmlp_out (apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl_ext.cu:24-71), which pads
- * the output to 64 columns and applies ReLU instead of the model's sigmoid on the last layer. */
-GP_API int gp_dlrm_topmlp_out(int64_t m, const void* x, const void* const* w,
+/* DLRM top MLP, fp16, w[5], b[5], two compiled width sets:
+ *   k0 = 512, n_out = 64: the reference app's own model (apps/dlrm_topmlp/pipelined/val.py:11-12,
+ *     DlrmMlp([479 + 33, 1024, 1024, 512, 256, 64])): 512 -> 1024 -> 1024 -> 512 -> 256 -> 64,
+ *     ReLU after every layer, out [m, 64];
+ *   k0 = 480, n_out = 1: 479 interaction features zero padded to 480, 480 -> 1024 -> 1024 -> 512
+ *     -> 256 (ReLU) -> 1 with a sigmoid (DlrmMlp(..., sigmoid_i=4)), out [m, 1].
+ * Other widths return GP_ERR_UNSUPPORTED.
+ * Replaces dlrm_topmlp_out (apps/dlrm_topmlp/pipelined/dlrm_topmlp_pl_ext.cu:24-71). */
+GP_API int gp_dlrm_topmlp_out(int64_t m, int k0, int n_out, const void* x, const void* const* w,
                        const void* const* b, void* out, void* stream);
 
 /* NeRF trunk, fp16: x [m, 64] (63 positional-encoding features, zero padded); layers 1-5
@@ -226,8 +233,10 @@ GP_API int gp_nerf_full_out(int64_t m, const void* x, const void* d, const void*
  * nothing; the fp16 copy of the second layer's weights goes to a fixed 1 MiB buffer compiled
  * into the library (held by every GPU that loads it, until exit). The first call on a device
  * looks that buffer up (cudaGetSymbolAddress) and should come before any stream capture. Calls
- * share the buffer: calls that overlap on the GPU race and must be ordered. Device-side timeouts
- * are not reported through gp_device_status. No counterpart in the reference. */
+ * share the buffer: calls that overlap on the GPU race and must be ordered. Its device waits use
+ * the gp_set_timeout_ns budget and honour gp_set_fault_injection; a wait that runs out is
+ * reported by gp_device_status like any other. It runs the single-CTA form of the kernel (the
+ * regular bf16 entry point runs the CTA-pair form). No counterpart in the reference. */
 GP_API int gp_gc_edges_bf16_noalloc_out(int64_t m, int act, const void* x,
                                  const void* w0, const void* b0, const void* w1, const void* b1,
                                  const void* gamma, const void* beta, void* out, void* stream);

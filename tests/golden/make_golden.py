@@ -169,6 +169,7 @@ def main() -> None:
     gen_bert_addln(ref, rows)
     gen_nerf_full(ref, rows)
     gen_mgn_graph(ref)
+    gen_val_replay(ref)
 
     # ---- known-answer LayerNorm row from misc_tests/layer_norm/torch_val.py:87-116
     src = (ref / "misc_tests/layer_norm/torch_val.py").read_text()
@@ -269,6 +270,51 @@ def gen_mgn_graph(ref: Path, n_nodes: int = 40, n_edges: int = 96) -> None:
     _save("mgn_graph_step", seed=np.int64(seed), nf=_u16(nf), ef=_u16(ef), srcs=srcs.numpy(),
           dsts=dsts.numpy(), y_edge=y_edge.numpy().astype(np.float32), agg=agg.numpy(),
           y_node=y_node.numpy().astype(np.float32), **out)
+
+
+def gen_val_replay(ref: Path, rows: int = 16) -> None:
+    """The eleven apps' models built exactly as their apps/<app>/pipelined/val.py builds them
+    (torch.manual_seed(0), the reference's model class, .eval().half()). Stores, per app, the
+    parameter checksum (which pins tests/_val_apps.build() to the reference's construction order)
+    and the reference model's fp32 output on `rows` input rows."""
+    from tests import _val_apps as V
+
+    mlps = _load(ref, "common/mlps.py", "ref_mlps_val")
+    mods = {a: _load(ref, f"apps/{a}/torch/model.py", f"ref_val_{a}")
+            for a in ("bert_ffn", "bert_addln_ffn", "gc_edges", "gc_nodes", "nerf_a", "nerf_full")}
+    ctor = {
+        "mgn_fullmlp": lambda: mlps.MgnMlp(384, [128, 128, 128], layernorm=True),
+        "mgn_linears": lambda: mlps.MgnMlp(384, [128, 128, 128], layernorm=False),
+        "test_mlp": lambda: mlps.MgnMlp(128, [128, 128, 128], layernorm=False),
+        "dlrm_botmlp": lambda: mlps.DlrmMlp([13 + 19, 512, 256, 128]),
+        "dlrm_topmlp": lambda: mlps.DlrmMlp([479 + 33, 1024, 1024, 512, 256, 64]),
+        "bert_ffn": lambda: mods["bert_ffn"].BertFfn(),
+        "bert_addln_ffn": lambda: mods["bert_addln_ffn"].BertFfn(),
+        "gc_edges": lambda: mods["gc_edges"].GraphCastEdges(),
+        "gc_nodes": lambda: mods["gc_nodes"].GraphCastNodes(),
+        "nerf_a": lambda: mods["nerf_a"].NerfA(64),
+        "nerf_full": lambda: mods["nerf_full"].Nerf(64, 32, radiance_dim=64, rgb_dim=64),
+    }
+    out = {}
+    for app, make in ctor.items():
+        torch.manual_seed(0)
+        net = make().eval().half()
+        lins = [m for m in net.modules() if isinstance(m, torch.nn.Linear)]
+        ref_sum = float(sum(m.weight.detach().double().sum() + m.bias.detach().double().sum() for m in lins))
+        ws, bs, _ = V.build(app)
+        assert abs(ref_sum - V.checksum(ws, bs)) < 1e-9, (app, ref_sum, V.checksum(ws, bs))
+        xs = V.inputs(app, rows)
+        with torch.no_grad():
+            y = net.float()(*[x.float() for x in xs])
+        out[f"{app}_wsum"] = np.float64(ref_sum)
+        for i, x in enumerate(xs):
+            out[f"{app}_x{i}"] = _u16(x)
+        if isinstance(y, tuple):   # Nerf with view directions returns (rgb, alpha)
+            out[f"{app}_rgb"] = y[0].numpy().astype(np.float32)
+            out[f"{app}_alpha"] = y[1].numpy().astype(np.float32)
+        else:
+            out[f"{app}_y"] = y.numpy().astype(np.float32)
+    _save("val_replay", **out)
 
 
 if __name__ == "__main__":

@@ -172,3 +172,33 @@ def test_fused_mlp_host_argument_checks():
     assert f(ctypes.byref(s), -1, P(0x1000), w, None, None, None, P(0x2000), 0, None) == L.GP_ERR_ARG
     assert f(ctypes.byref(s), 0, P(0x1000), w, None, None, None, P(0x2000), 0, None) == L.GP_OK
     assert f(ctypes.byref(s), 16, None, w, None, None, None, P(0x2000), 0, None) == L.GP_ERR_ARG
+
+
+def _noalloc(m=256, act=L.ACT_SILU, x=0x10000, w0=0x30000, w1=0x40000, out=0x20000):
+    return L.lib().gp_gc_edges_bf16_noalloc_out(m, act, _fake(x), _fake(w0), None, _fake(w1), None,
+                                                None, None, _fake(out), None)
+
+
+def test_noalloc_rejects_bad_arguments():
+    """The allocation-free entry point checks its arguments before any CUDA call."""
+    assert _noalloc(act=L.ACT_GELU_TANH) == L.GP_ERR_UNSUPPORTED
+    assert "act" in L.last_error()
+    assert _noalloc(act=L.ACT_NONE) == L.GP_ERR_UNSUPPORTED
+    assert _noalloc(x=0x10008) == L.GP_ERR_ALIGN
+    assert _noalloc(out=0x20002) == L.GP_ERR_ALIGN
+    assert _noalloc(w1=0x40004) == L.GP_ERR_ALIGN
+    assert _noalloc(x=0) == L.GP_ERR_ARG
+    assert _noalloc(m=-1) == L.GP_ERR_ARG
+    assert _noalloc(m=2**31) == L.GP_ERR_SHAPE
+    assert _noalloc(m=0) == L.GP_OK
+    assert L.last_error() == ""  # a successful call clears the previous message
+
+
+def test_dlrm_entry_points_reject_uncompiled_widths():
+    """Only the compiled width sets are accepted: bottom k0 16 / 32, top (480, 1) / (512, 64)."""
+    lib = L.lib()
+    w = (ctypes.c_void_p * 5)(*[0x30000 + 0x1000 * i for i in range(5)])
+    assert lib.gp_dlrm_botmlp_out(256, 48, _fake(0x10000), _fake(0x30000), None, _fake(0x31000),
+                                  None, _fake(0x32000), None, _fake(0x20000), None) == L.GP_ERR_UNSUPPORTED
+    assert lib.gp_dlrm_topmlp_out(256, 512, 1, _fake(0x10000), w, None, _fake(0x20000), None) == L.GP_ERR_UNSUPPORTED
+    assert lib.gp_dlrm_topmlp_out(256, 480, 64, _fake(0x10000), w, None, _fake(0x20000), None) == L.GP_ERR_UNSUPPORTED

@@ -47,7 +47,9 @@ def _worker(rank, world, port, m, q):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         if rank == 0:
             full = torch.cat([p[:int(s.item())] for p, s in zip(parts, sizes)])
-            q.put((full, float(t.item())))
+            # a numpy array is pickled by value; a torch tensor would be shared through a file
+            # descriptor owned by this process, which exits before the parent unpickles it
+            q.put((full.numpy(), float(t.item())))
     finally:
         dist.destroy_process_group()
 
@@ -69,6 +71,7 @@ def test_two_rank_sharding_reassembles():
             assert all(p.is_alive() or p.exitcode == 0 for p in procs), "a worker died"
     assert got is not None, "no result from rank 0"
     full, tmax = got
+    full = torch.from_numpy(full)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
