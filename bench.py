@@ -149,7 +149,7 @@ KERNEL_OF = {
     "dlrm_bot": "mlp_stream_kernel", "nerf": "mlp_stream_kernel", "gc_edge": "mlp_stream_pair_kernel",
     "bert_ffn": "mlp_gemm_pair_kernel", "dlrm_top": "mlp_gemm_pair_kernel",
     "bert_addln": "mlp_stream_kernel", "dlrm_interact": "dlrm_interaction_kernel",
-    "nerf_full": "mlp_stream_kernel (trunk, alpha and rgb launches)",
+    "nerf_full": "mlp_stream_kernel (one fused chain: trunk, alpha side output, rgb branch)",
     "mgn_mp": "mlp_resident_pair_kernel (edge update: gather4 of node rows, segment sum) + mlp_resident_kernel (node update)",
 }
 

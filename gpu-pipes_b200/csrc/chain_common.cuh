@@ -9,7 +9,7 @@ namespace gp {
 constexpr int kBM = 128;            // rows per tile: one TMEM lane (and one epilogue thread) per row
 constexpr int kPanel = 64;          // 16-bit elements per 128-byte swizzled K panel
 constexpr int kPanelBytes = kBM * kPanel * 2;  // one x panel: 128 rows x 128 B = 16 KB
-constexpr int kMaxLayers = 10;
+constexpr int kMaxLayers = 12;     // kernels; the public spec (GP_MAX_LAYERS) allows 10
 constexpr int kSmemLimit = 232448;  // sm_100 opt-in dynamic shared memory per CTA
 
 // Tail applied after the last GEMM (+bias, +activation) of a chain.
@@ -46,6 +46,7 @@ struct ChainArgs {
   const int64_t* gidx[2];             // per row: source and destination node
   int64_t n_nodes;
   float* scatter;                     // [n_nodes, N_last] fp32, += out row at gidx[1] (or null)
+  void* out2;                         // side output rows [M, N(SIDE)] (stream kernel, SIDE chains)
 };
 
 }  // namespace gp

@@ -679,7 +679,8 @@ int gp_nerf_out(int64_t m, const void* x, const void* const* w, const void* cons
   return fused_mlp(&s, m, x, w, b, nullptr, nullptr, out, static_cast<cudaStream_t>(stream));
 }
 
-// NeRF with view directions (apps/nerf_full/pipelined/nerf_full_pl_ext.cu:22-95): x [m, 64],
+// NeRF with view directions (apps/nerf_full/pipelined/nerf_full_pl_ext.cu:22-95), one fused chain
+// kernel (trunk, alpha side output, bottleneck, [bottleneck | d] -> rgb): x [m, 64],
 // d [m, 32] -> out_r [m, 64] = encoded w9 + b9, out_rgb [m, 64] = ReLU([encoded w10 + b10 | d]
 // w11 + b11) w12 + b12. fp16. w[0..11] / b[0..11] are the reference's w1..w12 / b1..b12 (b may
 // be NULL, or hold NULL entries).
@@ -710,9 +711,8 @@ int gp_nerf_full_out(int64_t m, const void* x, const void* d, const void* const*
   c.args.status = st->status;
   c.args.timeout_ns = g_timeout_ns.load();
   c.args.inject = g_inject.load();
-  rc = launch_nerf_full(c, m, x, d, w, bb, out_r, out_rgb);
+  rc = launch_nerf_full(c, m, x, d, w, bb, out_r, out_rgb);  // one fused chain kernel
   if (rc != GP_OK) return rc;
-  g_launches.fetch_add(4, std::memory_order_relaxed);  // identity, staging, trunk, alpha, rgb
   return finish_launch(s, 1);
 }
 

@@ -91,137 +91,59 @@ int launch_ffn_resln_bf16_h128(const LaunchCtx& c) {
   return launch_stream<ChainFfnResLn<__nv_bfloat16>>(c);
 }
 
-// NeRF with view directions (apps/nerf_full, model.py:40-64 with use_viewdirs=True; the
-// reference's pipelined shapes, nerf_full_pl_ext.cu:24-68): x [M, 64], d [M, 32]; trunk w1..w8
-// (w6 [320, 256] reads [h | x]); alpha w9 [256, 64]; bottleneck w10 [256, 256];
-// rgb w11 [288, 128] reads [bottleneck | d], w12 [128, 64]. Three chain launches:
-//   trunk  x -> encoded, stored in columns 0..255 of a [M, 384] buffer E
-//   alpha  encoded (E, row stride 384) -> out_r [M, 64]
-//   rgb    E = [encoded | d | 0] (384) -> 384 -> 128 (ReLU) -> 128, of which the first 64
-//          columns are stored to out_rgb
-// The rgb chain's first layer carries the bottleneck in its first 256 columns and a 32 x 32
-// identity that passes d through unchanged (x 1.0, exact) to columns 256..287, so the concat
-// [bottleneck | d] is simply its output; w11 is zero-padded to 384 rows, w12 to 128 columns.
-struct ChainNerfAlpha {
+// NeRF with view directions (apps/nerf_full/torch/model.py:40-64 with use_viewdirs=True; the
+// reference's pipelined shapes, nerf_full_pl_ext.cu:24-68): x [M, 64], d [M, 32]; one fused
+// chain of twelve tensor-core layers per 128-row tile:
+//   0..7   the trunk (w1..w8; w6 [320, 256] reads [h | x])                      -> encoded
+//   8      alpha = encoded w9 + b9 ([256, 64]), a side output stored to out_r; the activation
+//          buffer keeps `encoded`
+//   9      bottleneck = encoded w10 + b10 ([256, 256])
+//   10     ReLU([bottleneck | d] w11 + b11): w11 [288, 128] read as 320 rows (rows 288..319 are
+//          past the tensor and read as zeros), d the second input, zero filled to 64 columns
+//   11     w12 + b12 ([128, 64])                                                  -> out_rgb
+// No intermediate leaves the SM: `encoded`, the bottleneck and the rgb hidden layer stay in
+// the activation buffer, and d is loaded into the resident x buffer after the skip layer.
+struct ChainNerfFull {
   using T = __half;
-  static constexpr int NL = 1;
-  __host__ __device__ static constexpr int K(int) { return 256; }
-  __host__ __device__ static constexpr int N(int) { return 64; }
-  __host__ __device__ static constexpr int ACT(int) { return kActNone; }
-  static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr int NL = 12;
+  __host__ __device__ static constexpr int K(int l) {
+    return l == 0 ? 64 : (l == 5 || l == 10) ? 320 : (l == 11 ? 128 : 256);
+  }
+  __host__ __device__ static constexpr int N(int l) {
+    return l < 8 ? 256 : (l == 8 || l == 11) ? 64 : (l == 9 ? 256 : 128);
+  }
+  __host__ __device__ static constexpr int ACT(int l) {
+    return (l < 8 || l == 10) ? kActRelu : kActNone;
+  }
+  __host__ __device__ static constexpr int WROWS(int l) { return l == 10 ? 288 : K(l); }
+  static constexpr int SKIP = 5, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
+  static constexpr int SIDE = 8, SKIP2 = 10, X2_COLS = 32;
   static constexpr bool HIDDEN_F16 = false;
   static constexpr int HALVES = 1;
-  static constexpr bool SPLIT_ACT = false;
+  static constexpr bool SPLIT_ACT = true;
 };
-
-struct ChainNerfRgb {
-  using T = __half;
-  static constexpr int NL = 3;
-  __host__ __device__ static constexpr int K(int l) { return l == 2 ? 128 : 384; }
-  __host__ __device__ static constexpr int N(int l) { return l == 0 ? 384 : 128; }
-  __host__ __device__ static constexpr int ACT(int l) { return l == 1 ? kActRelu : kActNone; }
-  static constexpr int SKIP = 0, TAIL = kTailNone, HEAD_N = 0, HEAD_ACT = kActNone;
-  static constexpr bool HIDDEN_F16 = false;
-  static constexpr int HALVES = 2;
-  static constexpr bool SPLIT_ACT = false;
-  static constexpr int OUT_N = 64;
-};
-
-// E[:, 256:384] = [d | 0] with 16-byte loads and stores (16 per row: 4 carry d, 12 zeros).
-__global__ void nerf_stage_d_kernel(const uint4* __restrict__ d, uint4* __restrict__ e, int64_t m) {
-  const int64_t n = m * 16;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i >> 4;
-    const int c = static_cast<int>(i & 15);
-    e[row * 48 + 32 + c] = c < 4 ? __ldg(d + row * 4 + c) : make_uint4(0, 0, 0, 0);
-  }
-}
-
-__global__ void nerf_identity_block_kernel(__half* w0p) {  // w0p [384, 384]: 1.0 at (256 + i, 256 + i)
-  const int i = threadIdx.x;
-  if (i < 32) w0p[(256 + i) * 384 + 256 + i] = __float2half_rn(1.0f);
-}
 
 int launch_nerf_full(const LaunchCtx& base, int64_t m, const void* x, const void* d,
                      const void* const* w, const void* const* b, void* out_r, void* out_rgb) {
-  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
-  const size_t e_bytes = al(size_t(m) * 384 * 2), w0_bytes = al(384 * 384 * 2), b0_bytes = al(384 * 2);
-  const size_t w1_bytes = al(384 * 128 * 2), w2_bytes = al(128 * 128 * 2), b2_bytes = al(128 * 2);
-  void* ws = nullptr;
-  const cudaStream_t s = base.stream;
-  int rc = workspace_acquire(e_bytes + w0_bytes + b0_bytes + w1_bytes + w2_bytes + b2_bytes, s, &ws);
-  if (rc != GP_OK) return rc;
-  char* p = static_cast<char*>(ws);
-  __half* E = reinterpret_cast<__half*>(p);
-  char* w0p = p + e_bytes;
-  char* b0p = w0p + w0_bytes;
-  char* w1p = b0p + b0_bytes;
-  char* w2p = w1p + w1_bytes;
-  char* b2p = w2p + w2_bytes;
-  cudaError_t e = cudaSuccess;
-  auto ck = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
-  // augmented weights of the rgb chain
-  ck(cudaMemsetAsync(w0p, 0, w0_bytes + b0_bytes + w1_bytes + w2_bytes + b2_bytes, s));
-  ck(cudaMemcpy2DAsync(w0p, 384 * 2, w[9], 256 * 2, 256 * 2, 256, cudaMemcpyDeviceToDevice, s));
-  nerf_identity_block_kernel<<<1, 32, 0, s>>>(reinterpret_cast<__half*>(w0p));
-  if (b[9] != nullptr) ck(cudaMemcpyAsync(b0p, b[9], 256 * 2, cudaMemcpyDeviceToDevice, s));
-  ck(cudaMemcpyAsync(w1p, w[10], 288 * 128 * 2, cudaMemcpyDeviceToDevice, s));
-  ck(cudaMemcpy2DAsync(w2p, 128 * 2, w[11], 64 * 2, 64 * 2, 128, cudaMemcpyDeviceToDevice, s));
-  if (b[11] != nullptr) ck(cudaMemcpyAsync(b2p, b[11], 64 * 2, cudaMemcpyDeviceToDevice, s));
-  // E = [encoded | d | 0]: d into columns 256..287, zeros into 288..383 (encoded by the trunk)
-  {
-    const int64_t want = (m * 16 + 255) / 256;
-    const int blocks = static_cast<int>(want < 8 * base.sm_count ? want : 8 * base.sm_count);
-    nerf_stage_d_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(d), reinterpret_cast<uint4*>(E), m);
-  }
-  if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "nerf_full staging: %s", cudaGetErrorString(e));
-
   gp_mlp_spec spec{};
   spec.dtype = GP_F16;
   LaunchCtx t = base;
   t.spec = &spec;
   t.m = m;
+  t.x = x;
+  t.x2 = d;
+  t.x_ld = 0;
+  t.out = out_rgb;
+  t.out_ld = 0;
+  for (int l = 0; l < ChainNerfFull::NL; ++l) {
+    t.w[l] = w[l];
+    t.args.bias[l] = b[l];
+  }
   t.args.m = m;
   t.args.num_tiles = static_cast<int>((m + kBM - 1) / kBM);
-  for (int l = 0; l < kMaxLayers; ++l) t.args.bias[l] = nullptr;
-  if (rc == GP_OK) {  // trunk: x -> E[:, 0:256]
-    t.x = x;
-    t.x_ld = 0;
-    t.out = E;
-    t.out_ld = 384;
-    for (int l = 0; l < 8; ++l) {
-      t.w[l] = w[l];
-      t.args.bias[l] = b[l];
-    }
-    t.args.out = t.out;
-    rc = launch_stream<ChainNerfTrunk>(t);
-  }
-  if (rc == GP_OK) {  // alpha: encoded -> out_r
-    t.x = E;
-    t.x_ld = 384;
-    t.out = out_r;
-    t.out_ld = 0;
-    t.w[0] = w[8];
-    t.args.bias[0] = b[8];
-    t.args.out = t.out;
-    rc = launch_stream<ChainNerfAlpha>(t);
-  }
-  if (rc == GP_OK) {  // rgb: [encoded | d | 0] -> out_rgb
-    t.x = E;
-    t.x_ld = 0;
-    t.out = out_rgb;
-    t.w[0] = w0p;
-    t.w[1] = w1p;
-    t.w[2] = w2p;
-    t.args.bias[0] = b0p;
-    t.args.bias[1] = b[10];
-    t.args.bias[2] = b2p;
-    t.args.out = t.out;
-    rc = launch_stream<ChainNerfRgb>(t);
-  }
-  workspace_release(s);
-  return rc;
+  t.args.out = out_rgb;
+  t.args.out2 = out_r;
+  return launch_stream<ChainNerfFull>(t);
 }
 
 int launch_dlrm_bot_f16(const LaunchCtx& c) { return launch_stream<ChainDlrmBot<16>>(c); }

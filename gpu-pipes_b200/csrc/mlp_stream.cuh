@@ -69,6 +69,44 @@ struct EpiPairs<C, std::void_t<decltype(C::EPI_PAIRS)>> {
   static constexpr bool value = C::EPI_PAIRS;
 };
 
+//   SIDE (optional, default -1): a hidden layer whose output (bias + activation) is a second
+//   result, stored straight from registers to args.out2 ([M, N(SIDE)] rows) instead of the
+//   activation buffer; the layer after it reads the same activation as SIDE did (a branch off the
+//   chain, e.g. NeRF's alpha head off the trunk). Needs SPLIT_ACT.
+template <class C, class = void>
+struct SideLayer {
+  static constexpr int value = -1;
+};
+template <class C>
+struct SideLayer<C, std::void_t<decltype(C::SIDE)>> {
+  static constexpr int value = C::SIDE;
+};
+
+//   SKIP2 (optional, default 0): a layer whose last 64-column A panel is the second input
+//   (args x2 through tm.x2, [M, <= 64] rows, zero filled to 64 columns), e.g. NeRF's view
+//   directions concatenated to the bottleneck. The panel is loaded into the resident x buffer
+//   once x's last reader (layer 0 or SKIP) is done, so it costs no shared memory.
+template <class C, class = void>
+struct Skip2Layer {
+  static constexpr int value = 0;
+};
+template <class C>
+struct Skip2Layer<C, std::void_t<decltype(C::SKIP2)>> {
+  static constexpr int value = C::SKIP2;
+};
+
+//   WROWS(l) (optional, default K(l)): rows of weight l present in memory; the rows from WROWS(l)
+//   to K(l) are read as zeros (the TMA box reaches past the tensor), which pads a K that is not a
+//   whole number of 16-row steps without a copy.
+template <class C, class = void>
+struct WeightRows {
+  static constexpr int get(int l) { return C::K(l); }
+};
+template <class C>
+struct WeightRows<C, std::void_t<decltype(C::WROWS(0))>> {
+  static constexpr int get(int l) { return C::WROWS(l); }
+};
+
 template <class C, int CG = 1>
 struct StreamLayout {
   static constexpr int NL = C::NL;
@@ -152,6 +190,14 @@ struct StreamLayout {
   // stages are used whenever three of them fit, 32-row stages otherwise.
   static constexpr int kXStages = kXRes ? 0 : 2;
   static constexpr int kXSlots = kXRes ? 1 : kXStages;  // x buffers cycled by xs
+  static constexpr int kSide = SideLayer<C>::value;
+  static constexpr int kSkip2 = Skip2Layer<C>::value;
+  static constexpr int kLastXLayer = C::SKIP != 0 ? C::SKIP : 0;  // x's last reader
+  // the second input is loaded two layers ahead of its reader (never before x's last reader)
+  static constexpr int kLoadX2Layer = kSkip2 - 2 > kLastXLayer + 1 ? kSkip2 - 2 : kLastXLayer + 1;
+  static_assert(kSide < 0 || (kSplit && kSide > 0 && kSide + 1 < NL), "SIDE: a hidden layer of a SPLIT_ACT chain");
+  static_assert(kSkip2 == 0 || (kXRes && CG == 1 && kSkip2 > kLastXLayer + 1 && kSkip2 < NL),
+                "SKIP2: a resident-x chain, after x's last reader");
   static constexpr int kRingBytes = kSmemLimit - kFixed - kXStages * kPanelBytes;
   // Stage rows: 128 (two K panels per request; only where x is resident, since a streamed x
   // panel is consumed with its own weight rows), else 64, else 32 -- the largest of which two
@@ -348,6 +394,18 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
         }
 #pragma unroll 1
         for (int l = 0; ok && l < NL; ++l) {
+          if constexpr (L::kSkip2 != 0) {
+            if (l == L::kLoadX2Layer) {
+              // the second input into the resident x buffer, once x's last reader is done
+              if (!mbar_wait<kPair>(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
+              if (args.inject != 1) {
+                mbar_arrive_expect_tx(smem_u32(&x_full[xs]), kPanelBytes);
+                tma_load_2d_hint(smem_u32(smem + L::kOffX + xs * kPanelBytes), &tm.x2,
+                                 smem_u32(&x_full[xs]), 0, row_base, stream);
+              }
+              if (++xs == L::kXSlots) { xs = 0; xph ^= 1; }
+            }
+          }
           const int panels = (C::K(l) + kPanel - 1) / kPanel;
           if (!L::kXRes && l == 0) {
 #pragma unroll 1
@@ -416,7 +474,8 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
           const bool p_outer = !L::kXRes && l == 0;
           // A operand of panel p (waits for x where needed); 0 on timeout
           auto a_panel = [&](int p) -> uint32_t {
-            const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1);
+            const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1) ||
+                                (L::kSkip2 != 0 && l == L::kSkip2 && p == panels - 1);
             if (!from_x) return act_sm + p * kPanelBytes;
             if constexpr (L::kXRes) {
               return x_sm + xcur * kPanelBytes;
@@ -451,6 +510,12 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
             return true;
           };
           if (L::kXRes && l == 0) {
+            if (!mbar_wait<kPair>(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            tc_fence_after();
+          }
+          if (L::kSkip2 != 0 && l == L::kSkip2) {
+            // the second input took the x buffer's next phase
+            xph ^= 1;
             if (!mbar_wait<kPair>(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) { ok = false; break; }
             tc_fence_after();
           }
@@ -504,7 +569,8 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
                   const int p = kg >> 2;
                   const uint64_t bdesc = bdesc0 + static_cast<uint64_t>(k * 128);
                   const uint32_t acc = (r0 | k) != 0 ? 1u : 0u;
-                  const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1);
+                  const bool from_x = (l == 0) || (C::SKIP != 0 && l == C::SKIP && p == panels - 1) ||
+                                      (L::kSkip2 != 0 && l == L::kSkip2 && p == panels - 1);
                   const uint64_t adesc = from_x ? x_desc + static_cast<uint64_t>((kg & 3) * 2)
                                                 : act_desc + static_cast<uint64_t>(kg * 2 + p * (1024 - 8));
                   if constexpr (kPair) {
@@ -521,8 +587,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
             if (!ok) break;
           }
           if constexpr (L::kXRes) {
-            const int last_x_layer = C::SKIP != 0 ? C::SKIP : 0;
-            if (l == last_x_layer) commit_any(&x_empty[xcur]);
+            if (l == L::kLastXLayer || (L::kSkip2 != 0 && l == L::kSkip2)) commit_any(&x_empty[xcur]);
           }
           // with SPLIT_ACT every epilogue releases both halves: consume the second one once per
           // layer even where no K panel needed it, so the barrier phases stay in step
@@ -607,7 +672,32 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
         const float* bl = bias_s + L::biasOff(l);
         const int act_id = C::ACT(l);
         const int hc = C::N(l) / 32 / NH;  // 32-column chunks per half (even)
-        if (l + 1 < NL) {
+        if (l == L::kSide) {
+          // side output: bias + activation, stored from registers (16-byte stores of this row's
+          // 32-column chunks); the activation buffer keeps the previous layer's output
+          if (!wait_acc(0)) { ok = false; break; }
+#pragma unroll 1
+          for (int c = eg; c < C::N(l) / 32; c += 2) {
+            uint32_t v[32];
+            tmem_ld32(t_lane + dcol + c * 32, v);
+            tmem_wait_ld();
+            uint32_t pk[16];
+            act_dispatch(act_id, [&](auto actc) {
+              constexpr int A = decltype(actc)::value;
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                pk[i] = Elem<T>::pack(act_t<A>(__uint_as_float(v[2 * i]) + bl[c * 32 + 2 * i]),
+                                      act_t<A>(__uint_as_float(v[2 * i + 1]) + bl[c * 32 + 2 * i + 1]));
+            });
+            if (row < args.m) {
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(args.out2) + row * C::N(l) + c * 32);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            }
+          }
+          release(0);
+          release(1);
+        } else if (l + 1 < NL) {
           // hidden layer: bias + activation -> 16-bit A operand of the next layer (K-major SW128)
           // Layers >= 1 read their A operand from this same activation buffer: the second half's
           // MMAs of layer l still read layer l-1's activations, so writing layer l's activations

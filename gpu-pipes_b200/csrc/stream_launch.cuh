@@ -37,6 +37,10 @@ int launch_stream(const LaunchCtx& c) {
   rc = make_tmap_2d(&tm.x, c.x, dt, c.m, C::K(0), kPanel, kBM, 128, c.x_ld);
   if (rc == GP_OK && C::TAIL != kTailHead)
     rc = make_tmap_2d(&tm.out, c.out, dt, c.m, L::kOutN, 32, 32, 64, c.out_ld);
+  if constexpr (L::kSkip2 != 0) {
+    // second input [m, X2_COLS] as one 64-column panel per tile (columns past X2_COLS read zero)
+    if (rc == GP_OK) rc = make_tmap_2d(&tm.x2, c.x2, dt, c.m, C::X2_COLS, kPanel, kBM, 128);
+  }
   // fp16 copies of the weights of layers >= 1 (HIDDEN_F16), in the per-device workspace
   void* scratch = nullptr;
   size_t offs[kMaxLayers] = {0};
@@ -59,7 +63,7 @@ int launch_stream(const LaunchCtx& c) {
     const bool conv = C::HIDDEN_F16 && l > 0;
     const void* wl = conv ? static_cast<const void*>(static_cast<char*>(scratch) + offs[l]) : c.w[l];
     // one stage = kBK rows of this CTA's columns of one output half
-    rc = make_tmap_w3d(&tm.w[l], wl, conv ? GP_F16 : dt, C::K(l), C::N(l), L::kBK,
+    rc = make_tmap_w3d(&tm.w[l], wl, conv ? GP_F16 : dt, WeightRows<C>::get(l), C::N(l), L::kBK,
                        C::N(l) / L::NH / CG / 64);
   }
   if (rc != GP_OK) {

@@ -9,8 +9,8 @@ fused kernels' statistics shows up against the fp32 oracle.
 Covered tails:
   * the weight-resident kernel's LayerNorm (MeshGraphNet edge and node MLPs, both kernel forms),
   * the weight-streaming kernel's LayerNorm (GraphCast, CTA pair, bf16),
-  * the residual LayerNorm tails (the reference's BERT FFN 128 -> 512 -> 128 and the BERT
-    attention-output block), where the offset comes from the residual x,
+  * the residual LayerNorm tails: the reference's BERT FFN 128 -> 512 -> 128 (offset from the
+    FFN output) and the BERT attention-output block (offset from the residual x),
   * the BERT-large GEMM chain's row LayerNorm.
 Tolerance: the north-star max |err| <= 2e-2 and relative L2 <= 5e-3 against the fp32 oracle.
 """
@@ -81,7 +81,7 @@ def _check_ratio(pre, lo=50.0):
     mean = pre.mean(-1)
     std = pre.std(-1, unbiased=False)
     assert float((mean.abs() / std).min()) > lo, float((mean.abs() / std).min())
-    assert float(mean.std()) > 5.0  # the offset differs between rows
+    assert float(mean.std()) > 1.0  # the offset differs between rows
 
 
 def _close(out, ref, what):
@@ -116,12 +116,24 @@ def test_stream_layernorm_offset_rows(cuda_dev):
     _close(out, O.gc_edges(x, layers, (ga, be), O.ACT_SILU, 1e-5), "gc_edges")
 
 
+def ffn_offset_case(g, m, h, f, dtype, w1_scale, per_row):
+    """Residual-tail FFN case whose pre-LayerNorm rows x + FFN(x) sit at a large, per-row mean.
+    The mean comes from the second layer: W2 = per_row + 0.002 N(0,1) adds per_row * sum(h) (h >=
+    0 after ReLU/GELU, different for every row) to every column, so the rows keep the spread of x
+    (0.3) while bf16 inputs stay finely resolved (a large offset in x itself would quantise a
+    bf16 row to a few distinct values)."""
+    x = (0.3 * torch.randn(m, h, generator=g)).to(dtype)
+    w1 = (torch.randn(h, f, generator=g) * w1_scale).to(dtype)
+    b1 = (torch.randn(f, generator=g) * 0.01).to(dtype)
+    w2 = (torch.randn(f, h, generator=g) * 0.002 + per_row).to(dtype)
+    b2 = torch.zeros(h).to(dtype)
+    return x, [(w1, b1), (w2, b2)]
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_residual_layernorm_offset_rows_bert128(cuda_dev, dtype):
     g = torch.Generator().manual_seed(13)
-    m = 30_000
-    x = resid_offset_x(g, m, 128, dtype)
-    layers = [_lin(g, 128, 512, 0.002, dtype), _lin(g, 512, 128, 0.01, dtype)]
+    x, layers = ffn_offset_case(g, 30_000, 128, 512, dtype, 0.09, 1.5)
     ga, be = ln_params(g, 128, dtype)
     _check_ratio(_pre_ln(x[:4096], layers, [O.ACT_RELU], resid=True))
     (w1, b1), (w2, b2) = layers
@@ -151,9 +163,7 @@ def test_residual_layernorm_offset_rows_addln(cuda_dev):
 
 def test_gemm_chain_layernorm_offset_rows_bert_large(cuda_dev):
     g = torch.Generator().manual_seed(15)
-    m = 2_048
-    x = resid_offset_x(g, m, 1024, torch.bfloat16)
-    layers = [_lin(g, 1024, 4096, 0.0005, torch.bfloat16), _lin(g, 4096, 1024, 0.002, torch.bfloat16)]
+    x, layers = ffn_offset_case(g, 2_048, 1024, 4096, torch.bfloat16, 0.03, 0.6)
     ga, be = ln_params(g, 1024, torch.bfloat16)
     _check_ratio(_pre_ln(x[:1024], layers, [O.ACT_GELU_TANH], resid=True))
     (w1, b1), (w2, b2) = layers
