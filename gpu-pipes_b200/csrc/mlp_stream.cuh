@@ -728,6 +728,10 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
                 }
               });
             };
+            // SPLIT_ACT: the first half of the activation panels is released by each warp right
+            // after it has written its last chunk of that half (before any chunk if it has none)
+            const int last0 = (hc / 2 - 1 - eg) >= 0 ? (hc / 2 - 1) - ((hc / 2 - 1 - eg) & 1) : -1;
+            if (L::kSplit && last0 < 0) release(0);
             // this warp's chunks two at a time (EPI_PAIRS): both TMEM loads behind one wait
 #pragma unroll 1
             for (int c = hf * hc + eg; c < (hf + 1) * hc; c += EpiPairs<C>::value ? 4 : 2) {
@@ -738,8 +742,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               tmem_wait_ld();
               put_chunk(c, v[0]);
               if (two) put_chunk(c + 2, v[1]);
-              const int cl = two ? c + 2 : c;  // last chunk written
-              if (L::kSplit && cl < hc / 2 && cl + 2 >= hc / 2) {  // first half of the panels written
+              if (L::kSplit && (c == last0 || (two && c + 2 == last0))) {  // first half written
                 fence_proxy_async_smem();
                 release(0);
               }
