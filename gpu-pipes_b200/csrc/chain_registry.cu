@@ -24,6 +24,10 @@ GP_DECLARE(launch_mgn_ln_bf16_k256_single)
 GP_DECLARE(launch_mgn_ln_bf16_k128_single)
 GP_DECLARE(launch_dlrm_bot_f16)
 GP_DECLARE(launch_dlrm_bot_f16_k32)
+GP_DECLARE(launch_dlrm_bot_f16_tmem)
+GP_DECLARE(launch_dlrm_bot_f16_k32_tmem)
+GP_DECLARE(launch_ffn_resln_f16_h128_tmem)
+GP_DECLARE(launch_ffn_resln_bf16_h128_tmem)
 GP_DECLARE(launch_addln0_f16_h128)
 GP_DECLARE(launch_ffn_resln_f16_h128)
 GP_DECLARE(launch_ffn_resln_bf16_h128)
@@ -67,9 +71,13 @@ static const ChainEntry kChains[] = {
     {"probe_2l_f16_k128", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_pair, 0},
     {"probe_2l_f16_k128_single", GP_F16, 2, {128, 128, 128}, {NO, NO}, GP_TAIL_NONE, launch_probe_2l_f16_k128_single, 1},
     // weight-streaming chains (wide layers)
-    {"dlrm_bot_f16", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16, 0},
+    // chains with one wide first layer: hidden activations in TMEM (variant 0), or in shared
+    // memory on the weight-streaming kernel (variant 1)
+    {"dlrm_bot_f16_tmem", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_tmem, 0},
+    {"dlrm_bot_f16", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16, 1},
     // the reference app's own bottom MLP input width (apps/dlrm_botmlp/pipelined/val.py:11-12)
-    {"dlrm_bot_f16_k32", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32, 0},
+    {"dlrm_bot_f16_k32_tmem", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32_tmem, 0},
+    {"dlrm_bot_f16_k32", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32, 1},
     {"gc_silu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {GP_ACT_SILU, NO}, GP_TAIL_LAYERNORM, launch_gc_silu_bf16_k1536, 0},
     {"gc_relu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_bf16_k1536, 0},
     {"gc_relu_f16_k1536", GP_F16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_f16_k1536, 0},
@@ -82,8 +90,10 @@ static const ChainEntry kChains[] = {
     // residual + LN0, then 128 -> 512 ReLU -> 128 with residual + LN2 (the latter is also the
     // reference's small BERT FFN, apps/bert_ffn)
     {"addln0_f16_h128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_RESIDUAL_LN, launch_addln0_f16_h128, 0},
-    {"ffn_resln_f16_h128", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128, 0},
-    {"ffn_resln_bf16_h128", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128, 0},
+    {"ffn_resln_f16_h128_tmem", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128_tmem, 0},
+    {"ffn_resln_f16_h128", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128, 1},
+    {"ffn_resln_bf16_h128_tmem", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128_tmem, 0},
+    {"ffn_resln_bf16_h128", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128, 1},
     // chains with activations too wide for one SM: per-layer GEMMs over large row chunks
     {"bert_ffn_bf16", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
      launch_bert_ffn_bf16, 0},
