@@ -28,6 +28,10 @@ GP_DECLARE(launch_dlrm_bot_f16_tmem)
 GP_DECLARE(launch_dlrm_bot_f16_k32_tmem)
 GP_DECLARE(launch_ffn_resln_f16_h128_tmem)
 GP_DECLARE(launch_ffn_resln_bf16_h128_tmem)
+GP_DECLARE(launch_dlrm_bot_f16_tmem_pair)
+GP_DECLARE(launch_dlrm_bot_f16_k32_tmem_pair)
+GP_DECLARE(launch_ffn_resln_f16_h128_tmem_pair)
+GP_DECLARE(launch_ffn_resln_bf16_h128_tmem_pair)
 GP_DECLARE(launch_addln0_f16_h128)
 GP_DECLARE(launch_ffn_resln_f16_h128)
 GP_DECLARE(launch_ffn_resln_bf16_h128)
@@ -75,9 +79,11 @@ static const ChainEntry kChains[] = {
     // memory on the weight-streaming kernel (variant 1)
     {"dlrm_bot_f16_tmem", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_tmem, 0},
     {"dlrm_bot_f16", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16, 1},
+    {"dlrm_bot_f16_tmem_pair", GP_F16, 3, {16, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_tmem_pair, 2},
     // the reference app's own bottom MLP input width (apps/dlrm_botmlp/pipelined/val.py:11-12)
     {"dlrm_bot_f16_k32_tmem", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32_tmem, 0},
     {"dlrm_bot_f16_k32", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32, 1},
+    {"dlrm_bot_f16_k32_tmem_pair", GP_F16, 3, {32, 512, 256, 128}, {R, R, R}, GP_TAIL_NONE, launch_dlrm_bot_f16_k32_tmem_pair, 2},
     {"gc_silu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {GP_ACT_SILU, NO}, GP_TAIL_LAYERNORM, launch_gc_silu_bf16_k1536, 0},
     {"gc_relu_bf16_k1536", GP_BF16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_bf16_k1536, 0},
     {"gc_relu_f16_k1536", GP_F16, 2, {1536, 512, 512}, {R, NO}, GP_TAIL_LAYERNORM, launch_gc_relu_f16_k1536, 0},
@@ -92,8 +98,10 @@ static const ChainEntry kChains[] = {
     {"addln0_f16_h128", GP_F16, 1, {128, 128}, {NO}, GP_TAIL_RESIDUAL_LN, launch_addln0_f16_h128, 0},
     {"ffn_resln_f16_h128_tmem", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128_tmem, 0},
     {"ffn_resln_f16_h128", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128, 1},
+    {"ffn_resln_f16_h128_tmem_pair", GP_F16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_f16_h128_tmem_pair, 2},
     {"ffn_resln_bf16_h128_tmem", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128_tmem, 0},
     {"ffn_resln_bf16_h128", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128, 1},
+    {"ffn_resln_bf16_h128_tmem_pair", GP_BF16, 2, {128, 512, 128}, {R, NO}, GP_TAIL_RESIDUAL_LN, launch_ffn_resln_bf16_h128_tmem_pair, 2},
     // chains with activations too wide for one SM: per-layer GEMMs over large row chunks
     {"bert_ffn_bf16", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
      launch_bert_ffn_bf16, 0},

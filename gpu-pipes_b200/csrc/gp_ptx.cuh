@@ -163,13 +163,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     return kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
   };
   if (probe()) return true;
-  const uint64_t t0 = globaltimer_ns();
+  // the clock is first read after 64 unsuccessful probes, so a wait that ends soon pays no
+  // %globaltimer read; the budget then runs from that first read
+  uint64_t t0 = 0;
   uint32_t spins = 0;
   while (true) {
     if (probe()) return true;
     if ((++spins & 63u) == 0) {
       if (*w.abort_flag) return false;
-      if (globaltimer_ns() - t0 > w.timeout_ns) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > w.timeout_ns) {
         atomicCAS(w.status, 0, code);
         *w.abort_flag = 1;
         return false;

@@ -35,11 +35,13 @@ struct TmemFfnResLn {
   static constexpr bool HIDDEN_F16 = std::is_same<TT, __nv_bfloat16>::value;
 };
 
-template <class C>
+template <class C, int CG = 1>
 int launch_tmem(const LaunchCtx& c) {
-  using L = TmemLayout<C>;
-  const void* kern = reinterpret_cast<const void*>(&mlp_tmem_kernel<C>);
+  using L = TmemLayout<C, CG>;
+  const void* kern = CG == 2 ? reinterpret_cast<const void*>(&mlp_tmem_pair_kernel<C>)
+                             : reinterpret_cast<const void*>(&mlp_tmem_kernel<C>);
   static unsigned long long done_mask = 0;
+  static std::atomic<int> max_clusters[64];
   int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
   if (rc != GP_OK) return rc;
   const int dt = c.spec->dtype;
@@ -65,21 +67,51 @@ int launch_tmem(const LaunchCtx& c) {
           reinterpret_cast<__half*>(static_cast<char*>(scratch) + offs[l]), n);
     }
   }
-  // first layer: stages of kBK0 rows x one 128-column chunk (two 64-column blocks);
-  // later layers: stages of kBK rows x all N columns
-  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], c.w[0], dt, C::K(0), C::N(0), L::kBK0, 2);
+  // first layer: stages of kBK0 rows x one 128-column chunk (two 64-column blocks, one per CTA
+  // of a pair); later layers: stages of kBK rows x all N columns (half per CTA of a pair)
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], c.w[0], dt, C::K(0), C::N(0), L::kBK0, 2 / CG);
   for (int l = 1; rc == GP_OK && l < C::NL; ++l) {
     const void* wl = C::HIDDEN_F16 ? static_cast<const void*>(static_cast<char*>(scratch) + offs[l]) : c.w[l];
-    rc = make_tmap_w3d(&tm.w[l], wl, C::HIDDEN_F16 ? GP_F16 : dt, C::K(l), C::N(l), L::kBK, C::N(l) / 64);
+    rc = make_tmap_w3d(&tm.w[l], wl, C::HIDDEN_F16 ? GP_F16 : dt, C::K(l), C::N(l), L::kBK, C::N(l) / 64 / CG);
   }
   if (rc != GP_OK) {
     if (scratch != nullptr) workspace_release(c.stream);
     return rc;
   }
   ChainArgs args = c.args;
-  args.num_tiles = static_cast<int>((c.m + kBM - 1) / kBM);
-  const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-  mlp_tmem_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  args.num_tiles = static_cast<int>((c.m + L::kUnitRows - 1) / L::kUnitRows);
+  if constexpr (CG == 1) {
+    const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
+    mlp_tmem_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  } else {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::atomic<int>& mc_slot = max_clusters[dev & 63];  // filled once per device; racing first calls store the same value
+    int mc = mc_slot.load(std::memory_order_relaxed);
+    if (mc == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (c.sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(L::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = L::kSmemBytes;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = c.sm_count / 2;
+      }
+      mc = n;
+      mc_slot.store(n, std::memory_order_relaxed);
+    }
+    const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
+    mlp_tmem_pair_kernel<C><<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+  }
   if (scratch != nullptr) workspace_release(c.stream);
   return GP_OK;
 }
@@ -88,6 +120,8 @@ int launch_tmem(const LaunchCtx& c) {
 
 int launch_dlrm_bot_f16_tmem(const LaunchCtx& c) { return launch_tmem<TmemDlrmBot<16>>(c); }
 int launch_dlrm_bot_f16_k32_tmem(const LaunchCtx& c) { return launch_tmem<TmemDlrmBot<32>>(c); }
+int launch_dlrm_bot_f16_tmem_pair(const LaunchCtx& c) { return launch_tmem<TmemDlrmBot<16>, 2>(c); }
+int launch_dlrm_bot_f16_k32_tmem_pair(const LaunchCtx& c) { return launch_tmem<TmemDlrmBot<32>, 2>(c); }
 
 // The residual of this kernel is x itself (read from the resident x tile); a chain whose residual
 // rows are another tensor (the attention-output block's first stage) runs on the streaming kernel.
@@ -100,6 +134,14 @@ int launch_ffn_resln_f16_h128_tmem(const LaunchCtx& c) {
 int launch_ffn_resln_bf16_h128_tmem(const LaunchCtx& c) {
   if (c.args.resid != c.x) return launch_ffn_resln_bf16_h128(c);
   return launch_tmem<TmemFfnResLn<__nv_bfloat16>>(c);
+}
+int launch_ffn_resln_f16_h128_tmem_pair(const LaunchCtx& c) {
+  if (c.args.resid != c.x) return launch_ffn_resln_f16_h128(c);
+  return launch_tmem<TmemFfnResLn<__half>, 2>(c);
+}
+int launch_ffn_resln_bf16_h128_tmem_pair(const LaunchCtx& c) {
+  if (c.args.resid != c.x) return launch_ffn_resln_bf16_h128(c);
+  return launch_tmem<TmemFfnResLn<__nv_bfloat16>, 2>(c);
 }
 
 }  // namespace gp

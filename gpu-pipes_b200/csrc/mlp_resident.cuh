@@ -482,6 +482,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
       for (int b = 0; b < NBUF; ++b) { jt[b] = b; jl[b] = 0; ready_ph[b] = 0; first[b] = true; }
       int next_l0 = 0;  // local unit whose layer 0 consumes the x ring next (ring order)
       uint64_t idle_since = 0;
+      uint32_t idle_spins = 0;
       int prefer = 0;
 #pragma unroll 1
       while (ok) {
@@ -536,7 +537,10 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
         if (!any_left) break;
         if (issued) {
           idle_since = 0;
-        } else {
+          idle_spins = 0;
+        } else if ((++idle_spins & 63u) == 0) {
+          // the wait budget is checked every 64 idle polls: reading %globaltimer on every poll
+          // would put its latency between a buffer's release and the next MMA
           const uint64_t now = globaltimer_ns();
           if (idle_since == 0) {
             idle_since = now;

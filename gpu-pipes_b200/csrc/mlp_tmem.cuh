@@ -36,7 +36,7 @@
 
 namespace gp {
 
-template <class C>
+template <class C, int CG = 1>
 struct TmemLayout {
   static constexpr int NL = C::NL;
   static constexpr int K0 = C::K(0);
@@ -53,6 +53,12 @@ struct TmemLayout {
     return true;
   }
   static_assert(laterOk(), "layers >= 1: K = previous N, N a multiple of 64 up to 256");
+  __host__ __device__ static constexpr bool pairOk() {
+    for (int l = 1; l < NL; ++l)
+      if (C::N(l) % 128 != 0) return false;
+    return true;
+  }
+  static_assert(CG == 1 || (CG == 2 && pairOk()), "CTA pairs stage half of every N: N a multiple of 128");
   static constexpr bool kLN = C::TAIL == kTailLayerNorm || C::TAIL == kTailResidualLN;
   static constexpr bool kResid = C::TAIL == kTailResidualLN;
   static_assert(!kResid || K0 == NLast, "residual tail: the residual is x itself");
@@ -75,8 +81,9 @@ struct TmemLayout {
     for (int i = 0; i < l; ++i) s += C::N(i);
     return s;
   }
+  // bytes of one stage in this CTA (a CTA pair stages half of the columns in each CTA)
   static constexpr int kStageBytesMax =
-      (kBK * maxLaterN() * 2 > kBK0 * 128 * 2) ? kBK * maxLaterN() * 2 : kBK0 * 128 * 2;
+      ((kBK * maxLaterN() * 2 > kBK0 * 128 * 2) ? kBK * maxLaterN() * 2 : kBK0 * 128 * 2) / CG;
   static constexpr int kXBytes = kXPanels * kPanelBytes;  // one x slot
   static constexpr int kEpiWarps = 8;
   static constexpr int kStgBytes = kEpiWarps * 2 * 2048;  // two 32 x 32 output tiles per warp
@@ -98,15 +105,16 @@ struct TmemLayout {
   static constexpr int kSmemBytes = kOffBar + kBarBytes;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
   static_assert(kOffB % 1024 == 0 && kStageBytesMax % 1024 == 0 && kOffStg % 1024 == 0, "alignment");
+  static constexpr int kUnitRows = kBM * CG;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr uint32_t kACol = 256;  // TMEM column of the packed activation
 };
 
-template <class C>
-__global__ void __launch_bounds__(320, 1)
-    mlp_tmem_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+template <class C, int CG>
+__device__ __forceinline__ void mlp_tmem_body(const TensorMaps& tm, const ChainArgs& args) {
   using T = typename C::T;
-  using L = TmemLayout<C>;
+  using L = TmemLayout<C, CG>;
+  constexpr bool kPair = CG == 2;
   using H = typename std::conditional<C::HIDDEN_F16, __half, T>::type;  // hidden activation type
   constexpr int NL = C::NL;
   constexpr int kBS = L::kBStages;
@@ -130,7 +138,11 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_units = args.num_tiles;
+  const int num_units = args.num_tiles;  // in units of kUnitRows rows
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if ((smem_u32(smem) & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
@@ -143,12 +155,13 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&x_full[s]), 1);
-      // the residual tail reads x in the epilogue: then every epilogue warp releases the slot
+      // the residual tail reads x in the epilogue: then this CTA's epilogue warps release the
+      // slot; otherwise the (pair leader's) MMA commit does
       mbar_init(smem_u32(&x_empty[s]), L::kResid ? L::kEpiWarps : 1);
       mbar_init(smem_u32(&acc_full[s]), 1);
-      mbar_init(smem_u32(&s_free[s]), L::kEpiWarps);
+      mbar_init(smem_u32(&s_free[s]), L::kEpiWarps * CG);  // the leader's count both CTAs
     }
-    mbar_init(smem_u32(act_ready), L::kEpiWarps);
+    mbar_init(smem_u32(act_ready), L::kEpiWarps * CG);
     mbar_init(smem_u32(mma_done), 1);
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&pair_bar[i]), 64);
     *abort_flag = 0;
@@ -159,8 +172,13 @@ __global__ void __launch_bounds__(320, 1)
     prefetch_tmap(&tm.out);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_holder), 512);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_holder), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), 512);
+      tmem_relinquish();
+    }
   }
   for (int l = 0; l < NL; ++l) {
     const T* b = reinterpret_cast<const T*>(args.bias[l]);
@@ -176,10 +194,21 @@ __global__ void __launch_bounds__(320, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrival
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
+  // barrier address as seen by the loads / arrivals of this CTA (the leader's in a pair)
+  auto leader_bar = [&](const uint64_t* b) -> uint32_t {
+    return kPair ? mapa_shared(smem_u32(b), 0) : smem_u32(b);
+  };
+  auto commit_any = [&](uint64_t* bar) {
+    if constexpr (kPair) mma_commit_pair(smem_u32(bar), 0x3); else mma_commit(smem_u32(bar));
+  };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -189,37 +218,49 @@ __global__ void __launch_bounds__(320, 1)
       int bs = 0, xs = 0;
       uint32_t bph = 0, xph = 0;
       bool ok = true;
+      // bytes: the whole stage (both CTAs of a pair); this CTA loads its half of the columns
       auto stage = [&](const CUtensorMap* map, int row, int blk, uint32_t bytes) -> bool {
-        if (!mbar_wait(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) return false;
-        mbar_arrive_expect_tx(smem_u32(&b_full[bs]), bytes);
-        tma_load_3d_hint(smem_u32(smem + L::kOffB + bs * L::kStageBytesMax), map,
-                         smem_u32(&b_full[bs]), 0, row, blk, keep);
+        if (!mbar_wait<kPair>(smem_u32(&b_empty[bs]), bph ^ 1, wctx, kDevTimeoutProducer)) return false;
+        if (leader) mbar_arrive_expect_tx(smem_u32(&b_full[bs]), bytes);
+        const uint32_t dst = smem_u32(smem + L::kOffB + bs * L::kStageBytesMax);
+        if constexpr (kPair) {
+          tma_load_3d_pair(dst, map, leader_bar(&b_full[bs]), 0, row, blk, keep);
+        } else {
+          tma_load_3d_hint(dst, map, smem_u32(&b_full[bs]), 0, row, blk, keep);
+        }
         if (++bs == kBS) { bs = 0; bph ^= 1; }
         return true;
       };
 #pragma unroll 1
-      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
-        if (!mbar_wait(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
+      for (int unit = unit0; ok && unit < num_units; unit += units_step) {
+        const int row_base = unit * L::kUnitRows + static_cast<int>(rank) * kBM;
+        if (!mbar_wait<kPair>(smem_u32(&x_empty[xs]), xph ^ 1, wctx, kDevTimeoutProducer)) break;
         if (args.inject != 1) {
-          mbar_arrive_expect_tx(smem_u32(&x_full[xs]), L::kXBytes);
-          for (int p = 0; p < L::kXPanels; ++p)
-            tma_load_2d_hint(smem_u32(smem + L::kOffX + xs * L::kXBytes + p * kPanelBytes), &tm.x,
-                             smem_u32(&x_full[xs]), p * kPanel, unit * kBM, stream);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[xs]), L::kXBytes * CG);
+          for (int p = 0; p < L::kXPanels; ++p) {
+            const uint32_t dst = smem_u32(smem + L::kOffX + xs * L::kXBytes + p * kPanelBytes);
+            if constexpr (kPair) {
+              tma_load_2d_pair(dst, &tm.x, leader_bar(&x_full[xs]), p * kPanel, row_base, stream);
+            } else {
+              tma_load_2d_hint(dst, &tm.x, smem_u32(&x_full[xs]), p * kPanel, row_base, stream);
+            }
+          }
         }
         if (++xs == 2) { xs = 0; xph ^= 1; }
-        // first layer: per 128-column chunk, kBK0-row stages of two 64-column blocks
+        // first layer: per 128-column chunk, kBK0-row stages of two 64-column blocks (one per
+        // CTA of a pair)
         for (int j = 0; ok && j < L::kChunks0; ++j)
           for (int r0 = 0; ok && r0 < L::K0; r0 += L::kBK0)
-            ok = stage(&tm.w[0], r0, 2 * j, L::kBK0 * 128 * 2);
+            ok = stage(&tm.w[0], r0, 2 * j + static_cast<int>(rank), L::kBK0 * 128 * 2);
         for (int l = 1; ok && l < NL; ++l)
           for (int r0 = 0; ok && r0 < C::K(l); r0 += L::kBK)
-            ok = stage(&tm.w[l], r0, 0, L::kBK * C::N(l) * 2);
+            ok = stage(&tm.w[l], r0, static_cast<int>(rank) * (C::N(l) / CG / 64), L::kBK * C::N(l) * 2);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       const uint32_t b_sm = smem_u32(smem + L::kOffB);
       const uint32_t x_sm = smem_u32(smem + L::kOffX);
       int bs = 0, xs = 0;
@@ -228,15 +269,21 @@ __global__ void __launch_bounds__(320, 1)
       int job = 0;
       bool ok = true;
       auto take_s = [&](int h) -> bool {  // S half h is free (the epilogue has read it)
-        if (!mbar_wait(smem_u32(&s_free[h]), sph[h] ^ 1, wctx, kDevTimeoutMma)) return false;
+        if (!mbar_wait<kPair>(smem_u32(&s_free[h]), sph[h] ^ 1, wctx, kDevTimeoutMma)) return false;
         sph[h] ^= 1;
         return true;
       };
-      constexpr uint32_t kIdesc0 = make_idesc_f16(kBM, 128, Elem<T>::kIsBf16, 0, 1);
+      auto mma_ss_any = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+        if constexpr (kPair) mma_ss_pair(d, a, b, idesc, acc); else mma_ss(d, a, b, idesc, acc);
+      };
+      auto mma_ts_any = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+        if constexpr (kPair) mma_ts_pair(d, a, b, idesc, acc); else mma_ts(d, a, b, idesc, acc);
+      };
+      constexpr uint32_t kIdesc0 = make_idesc_f16(L::kUnitRows, 128, Elem<T>::kIsBf16, 0, 1);
 #pragma unroll 1
-      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+      for (int unit = unit0; ok && unit < num_units; unit += units_step) {
         const int xcur = xs;
-        if (!mbar_wait(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) break;
+        if (!mbar_wait<kPair>(smem_u32(&x_full[xcur]), xph, wctx, kDevTimeoutMma)) break;
         tc_fence_after();
         // first layer: SS MMAs (x panels x W0 chunk stages) into alternating S halves
 #pragma unroll 1
@@ -246,56 +293,56 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
 #pragma unroll 1
           for (int r0 = 0; r0 < L::K0; r0 += L::kBK0) {
-            if (!mbar_wait(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            if (!mbar_wait<kPair>(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
             tc_fence_after();
             const uint32_t bst = b_sm + bs * L::kStageBytesMax;
             const uint32_t xp = x_sm + xcur * L::kXBytes + (r0 / kPanel) * kPanelBytes;
             for (int k = 0; k < L::kBK0 / 16; ++k) {
               const uint64_t adesc = make_sdesc_sw128(xp + ((r0 % kPanel) / 16 + k) * 32, 16, 1024);
               const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK0 * 128, 1024);
-              mma_ss(tmem_base + h * 128, adesc, bdesc, kIdesc0, (r0 | k) != 0 ? 1u : 0u);
+              mma_ss_any(tmem_base + h * 128, adesc, bdesc, kIdesc0, (r0 | k) != 0 ? 1u : 0u);
             }
-            mma_commit(smem_u32(&b_empty[bs]));
+            commit_any(&b_empty[bs]);
             if (++bs == kBS) { bs = 0; bph ^= 1; }
           }
           if (!ok) break;
-          mma_commit(smem_u32(&acc_full[job & 1]));
+          commit_any(&acc_full[job & 1]);
           ++job;
         }
         if (!ok) break;
-        if constexpr (!L::kResid) mma_commit(smem_u32(&x_empty[xcur]));  // x read by layer 0 only
+        if constexpr (!L::kResid) commit_any(&x_empty[xcur]);  // x is read by layer 0 only
         // later layers: TS MMAs, A = the packed activation in TMEM columns [256, ...)
 #pragma unroll 1
         for (int l = 1; ok && l < NL; ++l) {
-          if (!mbar_wait(smem_u32(act_ready), aph, wctx, kDevTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait<kPair>(smem_u32(act_ready), aph, wctx, kDevTimeoutMma)) { ok = false; break; }
           aph ^= 1;
           if (!take_s(0) || (C::N(l) > 128 && !take_s(1))) { ok = false; break; }
           tc_fence_after();
-          const uint32_t idesc = make_idesc_f16(kBM, C::N(l), (C::HIDDEN_F16 ? 0 : Elem<T>::kIsBf16), 0, 1);
+          const uint32_t idesc = make_idesc_f16(L::kUnitRows, C::N(l), (C::HIDDEN_F16 ? 0 : Elem<T>::kIsBf16), 0, 1);
 #pragma unroll 1
           for (int r0 = 0; r0 < C::K(l); r0 += L::kBK) {
-            if (!mbar_wait(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            if (!mbar_wait<kPair>(smem_u32(&b_full[bs]), bph, wctx, kDevTimeoutMma)) { ok = false; break; }
             tc_fence_after();
             const uint32_t bst = b_sm + bs * L::kStageBytesMax;
             for (int k = 0; k < L::kBK / 16; ++k) {
               const uint64_t bdesc = make_sdesc_sw128(bst + k * 2048, L::kBK * 128, 1024);
-              mma_ts(tmem_base, tmem_base + L::kACol + (r0 / 16 + k) * 8, bdesc, idesc, (r0 | k) != 0 ? 1u : 0u);
+              mma_ts_any(tmem_base, tmem_base + L::kACol + (r0 / 16 + k) * 8, bdesc, idesc, (r0 | k) != 0 ? 1u : 0u);
             }
-            mma_commit(smem_u32(&b_empty[bs]));
+            commit_any(&b_empty[bs]);
             if (++bs == kBS) { bs = 0; bph ^= 1; }
           }
           if (!ok) break;
-          mma_commit(smem_u32(&acc_full[job & 1]));
+          commit_any(&acc_full[job & 1]);
           ++job;
         }
         if (++xs == 2) { xs = 0; xph ^= 1; }
       }
-      mma_commit(smem_u32(mma_done));  // every issued MMA has completed before TMEM is released
+      commit_any(mma_done);  // every issued MMA has completed before TMEM is released
     }
     if (lane == 0) {
       volatile int no_abort = 0;
       WaitCtx drain{args.status, &no_abort, args.timeout_ns};
-      mbar_wait(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
+      mbar_wait<kPair>(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
@@ -312,14 +359,22 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     auto wait_job = [&]() -> bool {
       const int i = job & 1;
-      if (!mbar_wait(smem_u32(&acc_full[i]), acc_ph[i], wctx, kDevTimeoutEpilogue)) return false;
+      if (!mbar_wait<kPair>(smem_u32(&acc_full[i]), acc_ph[i], wctx, kDevTimeoutEpilogue)) return false;
       acc_ph[i] ^= 1;
       ++job;
       tc_fence_after();
       return true;
     };
+    // a hand-off the (pair leader's) MMA issuer waits on
     auto arrive = [&](uint64_t* bar) {
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (kPair) mbar_arrive_cluster(leader_bar(bar)); else mbar_arrive(smem_u32(bar));
+      }
+    };
+    // a hand-off to this CTA's own producer
+    auto arrive_local = [&](uint64_t* bar) {
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(bar));
     };
@@ -340,9 +395,8 @@ __global__ void __launch_bounds__(320, 1)
       });
     };
 #pragma unroll 1
-    for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
-      const int64_t row = static_cast<int64_t>(unit) * kBM + r;
-      const int row0 = unit * kBM + q * 32;
+    for (int unit = unit0; ok && unit < num_units; unit += units_step) {
+      const int row0 = unit * L::kUnitRows + static_cast<int>(rank) * kBM + q * 32;
       // ---- first layer: each warp converts 64 columns of every 128-column chunk
 #pragma unroll 1
       for (int j = 0; ok && j < L::kChunks0; ++j) {
@@ -468,7 +522,7 @@ __global__ void __launch_bounds__(320, 1)
           // every accumulator column of this warp is read: S may take the next tile's chunks
           arrive(&s_free[0]);
           if (NLast > 128) arrive(&s_free[1]);
-          if constexpr (L::kResid) arrive(&x_empty[xs]);
+          if constexpr (L::kResid) arrive_local(&x_empty[xs]);
         }
         if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
@@ -481,18 +535,35 @@ __global__ void __launch_bounds__(320, 1)
         }
         sb ^= 1;
       }
-      (void)row;
       if (++xs == 2) xs = 0;
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair) {
+    cluster_sync_all();  // no CTA leaves while the pair's MMAs may still read its memory
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if constexpr (kPair) tmem_dealloc_pair(tmem_base, 512); else tmem_dealloc(tmem_base, 512);
   }
+}
+
+template <class C>
+__global__ void __launch_bounds__(320, 1)
+    mlp_tmem_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  mlp_tmem_body<C, 1>(tm, args);
+}
+
+// CTA-pair form: 256-row units, 256-row MMAs issued by the leader over both CTAs' TMEM
+// activations, each CTA staging half of the columns of every weight stage.
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    mlp_tmem_pair_kernel(const __grid_constant__ TensorMaps tm, const ChainArgs args) {
+  mlp_tmem_body<C, 2>(tm, args);
 }
 
 }  // namespace gp
