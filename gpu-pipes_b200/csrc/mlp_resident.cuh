@@ -219,6 +219,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   static_assert(XM != 1 || (CG == 2 && K0 == 384 && N == 128), "edge gather: CTA pair, 384 -> 128");
   static_assert(XM != 2 || K0 > 128, "two-source x: 128 columns from each source at least");
   constexpr int kDstWarp = 2 + L::kNumEpiWarps;  // x mode 1: the second gathering warp
+  constexpr int kIssWarp1 = 2 + L::kNumEpiWarps + (XM == 1 ? 1 : 0);  // the second MMA issuer
   constexpr int kXS = L::kXStages;
   constexpr int kPanels0 = K0 / kPanel;
   constexpr int NC = L::NC;
@@ -234,6 +235,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   uint64_t* acc_full = bars + 17;  // [NBUF]
   uint64_t* act_ready = bars + 19; // [NBUF]  (leader's count both CTAs' epilogue warps)
   uint64_t* mma_done = bars + 21;  // [1]
+  uint64_t* l0_turn = bars + 22;   // [2]  issuer of buffer b may start waiting for its x panels
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
   float* ln_g = reinterpret_cast<float*>(smem + L::kOffLn);
@@ -263,7 +265,8 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&act_ready[b]), 4 * CG);
     }
-    mbar_init(smem_u32(mma_done), 1);
+    mbar_init(smem_u32(mma_done), NBUF);  // one drain commit per issuing thread
+    for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&l0_turn[b]), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -451,63 +454,64 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     producer_done:;
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer (pair leader)
-    if (lane == 0 && leader) {
+  } else if (warp == 1 || warp == kIssWarp1) {
+    // ---------------------------------------------------------------- MMA issuers (pair leader)
+    // One issuing thread per accumulator buffer (warp 1: buffer 0, the last warp: buffer 1), so
+    // that a buffer whose epilogue has released it gets its next MMAs queued while the other
+    // buffer's job still runs: a single issuer measured ~650 cycles between a job's commit and
+    // its next barrier test (clock64 traces), and the two buffers' jobs then alternated with a
+    // gap each instead of overlapping. tcgen05.commit tracks the MMAs of the issuing thread, so
+    // each buffer's commits stay its own.
+    const int b = warp == 1 ? 0 : 1;
+    if (lane == 0 && leader && b < NBUF) {
       bool ok = mbar_wait<kPair>(smem_u32(w_full), 0, wctx, kDevTimeoutWeights);
       tc_fence_after();
       const uint32_t wsm = smem_u32(smem + L::kOffW);
       const uint32_t xsm = smem_u32(smem + L::kOffX);
       const uint32_t bsm = smem_u32(smem + L::kOffBias);
       const uint32_t ones = tmem_base + L::kOnesCol;
-      auto mma_ss_any = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-        if constexpr (kPair) mma_ss_pair(d, a, b, kIdesc, acc); else mma_ss(d, a, b, kIdesc, acc);
+      auto mma_ss_any = [&](uint32_t d, uint64_t a, uint64_t bd, uint32_t acc) {
+        if constexpr (kPair) mma_ss_pair(d, a, bd, kIdesc, acc); else mma_ss(d, a, bd, kIdesc, acc);
       };
-      auto mma_ts_any = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t acc) {
-        if constexpr (kPair) mma_ts_pair(d, a, b, kIdesc, acc); else mma_ts(d, a, b, kIdesc, acc);
+      auto mma_ts_any = [&](uint32_t d, uint32_t a, uint64_t bd, uint32_t acc) {
+        if constexpr (kPair) mma_ts_pair(d, a, bd, kIdesc, acc); else mma_ts(d, a, bd, kIdesc, acc);
       };
       auto commit_any = [&](uint64_t* bar) {
         if constexpr (kPair) mma_commit_pair(smem_u32(bar), 0x3); else mma_commit(smem_u32(bar));
       };
-      auto test_any = [&](uint64_t* bar, uint32_t parity) {
-        return kPair ? mbar_test_wait_cluster(smem_u32(bar), parity)
-                     : mbar_test_wait(smem_u32(bar), parity);
-      };
-      int s = 0;
-      uint32_t ph = 0;
-      // per-buffer job cursor: local unit index (units j with j % NBUF == b) and layer
-      int jt[NBUF], jl[NBUF];
-      uint32_t ready_ph[NBUF];
-      bool first[NBUF];
-      for (int b = 0; b < NBUF; ++b) { jt[b] = b; jl[b] = 0; ready_ph[b] = 0; first[b] = true; }
-      int next_l0 = 0;  // local unit whose layer 0 consumes the x ring next (ring order)
-      uint64_t idle_since = 0;
-      uint32_t idle_spins = 0;
-      int prefer = 0;
+      const uint32_t d_tmem = tmem_base + b * L::kBufCols;
+      const uint32_t a_tmem = tmem_base + b * L::kBufCols + L::kActCol;
+      uint32_t ready_ph = 0, turn_ph = 0;
+      bool first = true;
+      // local units j = b, b + NBUF, ...; the x panels are consumed in ring order over all units
 #pragma unroll 1
-      while (ok) {
-        bool any_left = false, issued = false;
+      for (int j = b; ok && unit0 + j * units_step < num_units; j += NBUF) {
 #pragma unroll 1
-        for (int bi = 0; bi < NBUF && !issued; ++bi) {
-          const int b = (prefer + bi) % NBUF;
-          const int unit = unit0 + jt[b] * units_step;
-          if (unit >= num_units) continue;
-          any_left = true;
-          const int l = jl[b];
-          // dependency: this buffer's previous epilogue step is done (in both CTAs)
-          if (!first[b] && !test_any(&act_ready[b], ready_ph[b])) continue;
-          // layer 0 takes x panels in ring order and needs the first panel present
-          if (l == 0 && (jt[b] != next_l0 || !test_any(&x_full[s], ph))) continue;
-          if (!first[b]) ready_ph[b] ^= 1;
-          first[b] = false;
+        for (int l = 0; ok && l < NL; ++l) {
+          // this buffer's previous epilogue step is done (in both CTAs)
+          if (!first) {
+            if (!mbar_wait<kPair>(smem_u32(&act_ready[b]), ready_ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+            ready_ph ^= 1;
+          }
+          first = false;
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + b * L::kBufCols;
           const uint32_t bias_l = bsm + l * (NC / 64) * 1024;
           // acc = 1 x bias (initialises the accumulator)
           mma_ts_any(d_tmem, ones, make_sdesc_sw128(bias_l, 1024, 1024), 0u);
           if (l == 0) {
+            // The x ring is consumed in unit order across both issuers. A parity wait cannot tell
+            // a stage's use k from use k - 2, so this unit waits for its panels only once the
+            // previous unit's issuer has passed its own waits (its l0_turn arrival).
+            if (j > 0) {
+              if (!mbar_wait<kPair>(smem_u32(&l0_turn[b]), turn_ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+              turn_ph ^= 1;
+            }
+#pragma unroll 1
             for (int p = 0; p < kPanels0; ++p) {
-              if (p > 0 && !mbar_wait<kPair>(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
+              const int g = j * kPanels0 + p;  // position in the x ring's sequence
+              const int s = g % kXS;
+              const uint32_t ph = static_cast<uint32_t>(g / kXS) & 1u;
+              if (!mbar_wait<kPair>(smem_u32(&x_full[s]), ph, wctx, kDevTimeoutMma)) { ok = false; break; }
               tc_fence_after();
               const uint64_t adesc = make_sdesc_sw128(xsm + s * kPanelBytes, 16, 1024);
 #pragma unroll
@@ -517,12 +521,11 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
                 mma_ss_any(d_tmem, adesc + static_cast<uint64_t>(k * 2), bdesc, 1u);
               }
               commit_any(&x_empty[s]);
-              if (++s == kXS) { s = 0; ph ^= 1; }
             }
-            next_l0 += 1;
+            if (!ok) break;
+            mbar_arrive(smem_u32(&l0_turn[(b + 1) % NBUF]));  // the next unit's issuer may wait
           } else {
             const uint32_t wl = wsm + w_layer_offset(l, L::kW0Bytes, L::kWhBytes);
-            const uint32_t a_tmem = tmem_base + b * L::kBufCols + L::kActCol;
 #pragma unroll
             for (int k = 0; k < N / 16; ++k) {
               const uint64_t bdesc = make_sdesc_sw128(wl + k * 2048, N * 128, 1024);
@@ -530,30 +533,12 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
             }
           }
           commit_any(&acc_full[b]);
-          if (++jl[b] == NL) { jl[b] = 0; jt[b] += NBUF; }
-          issued = true;
-          prefer = (b + 1) % NBUF;
-        }
-        if (!any_left) break;
-        if (issued) {
-          idle_since = 0;
-          idle_spins = 0;
-        } else if ((++idle_spins & 63u) == 0) {
-          // the wait budget is checked every 64 idle polls: reading %globaltimer on every poll
-          // would put its latency between a buffer's release and the next MMA
-          const uint64_t now = globaltimer_ns();
-          if (idle_since == 0) {
-            idle_since = now;
-          } else if (now - idle_since > args.timeout_ns || *abort_flag) {
-            if (!*abort_flag) { atomicCAS(args.status, 0, kDevTimeoutMma); *abort_flag = 1; }
-            ok = false;
-          }
         }
       }
-      // drain: every issued MMA has completed before TMEM can be released
+      // drain: every MMA this thread issued has completed before TMEM can be released
       commit_any(mma_done);
     }
-    if (lane == 0) {
+    if (warp == 1 && lane == 0) {
       volatile int no_abort = 0;
       WaitCtx drain{args.status, &no_abort, args.timeout_ns};
       mbar_wait<kPair>(smem_u32(mma_done), 0, drain, kDevTimeoutMma);
@@ -667,7 +652,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
 
 // threads and dynamic shared memory of a launch in x mode XM (mode 1 adds a second gathering warp)
 template <class L, int XM>
-constexpr int resident_threads() { return L::kThreads + (XM == 1 ? 32 : 0); }
+constexpr int resident_threads() { return L::kThreads + (XM == 1 ? 32 : 0) + 32; }
 template <class L, int XM>
 constexpr int resident_smem() { return L::kSmemBytes; }
 
