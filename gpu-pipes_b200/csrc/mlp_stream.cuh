@@ -237,6 +237,19 @@ __host__ __device__ constexpr int ksteps_in(int l, int p, int h) {
   return n <= 0 ? 0 : (n > BK / 16 ? BK / 16 : n);
 }
 
+// y = accumulator (32 fp32 TMEM words) + 32 biases from shared memory, by 16-byte loads
+__device__ __forceinline__ void add_bias32(const uint32_t (&v)[32], const float* bl, float (&y)[32]) {
+  const float4* b4 = reinterpret_cast<const float4*>(bl);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 b = b4[j];
+    y[4 * j] = __uint_as_float(v[4 * j]) + b.x;
+    y[4 * j + 1] = __uint_as_float(v[4 * j + 1]) + b.y;
+    y[4 * j + 2] = __uint_as_float(v[4 * j + 2]) + b.z;
+    y[4 * j + 3] = __uint_as_float(v[4 * j + 3]) + b.w;
+  }
+}
+
 template <class C, int CG>
 __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const ChainArgs& args) {
   using T = typename C::T;
@@ -311,14 +324,18 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
     for (int i = threadIdx.x; i < C::N(l); i += blockDim.x)
       bias_s[L::biasOff(l) + i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
   }
+  int ident_local = 1;
   if constexpr (L::kLN) {
     const T* g = reinterpret_cast<const T*>(args.gamma);
     const T* b = reinterpret_cast<const T*>(args.beta);
     for (int i = threadIdx.x; i < C::N(NL - 1); i += blockDim.x) {
       ln_g[i] = g != nullptr ? Elem<T>::to_f(g[i]) : 1.0f;
       ln_b[i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
+      ident_local &= (ln_g[i] == 1.0f && ln_b[i] == 0.0f) ? 1 : 0;
     }
   }
+  // gamma == 1 and beta == 0 everywhere: the LayerNorm affine step is the identity
+  const bool ln_ident = __syncthreads_and(ident_local) != 0;
   if constexpr (C::TAIL == kTailHead) {
     // head weights [N_last, HEAD_N] (row-major, 16-bit) -> fp32 [N_last][kHeadPad], zero padded
     const T* hw = reinterpret_cast<const T*>(args.head_w);
@@ -847,8 +864,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               tmem_ld32(t_lane + dcol + c * 32, v);
               tmem_wait_ld();
               float y[32];
-#pragma unroll
-              for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(v[i]) + bl[c * 32 + i];
+              add_bias32(v, bl + c * 32, y);
               resid_add(c, y);
               if (c == eg) k = y[0];
 #pragma unroll
@@ -889,25 +905,33 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
               if (c + 2 >= (hf + 1) * hc) release(hf);  // this warp's part of the half is read
               uint32_t pk[16];
               float yr[32];
-#pragma unroll
-              for (int i = 0; i < 32; ++i) yr[i] = __uint_as_float(v[i]) + bl[c * 32 + i];
+              add_bias32(v, bl + c * 32, yr);
               resid_add(c, yr);
-              act_dispatch(L::kLN ? int(kActNone) : act_id, [&](auto actc) {
-                constexpr int A = decltype(actc)::value;
+              if constexpr (L::kLN) {
+                const float nmr = -mean * rstd;
+                if (ln_ident) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  float y0 = yr[2 * i];
-                  float y1 = yr[2 * i + 1];
-                  if constexpr (L::kLN) {
-                    y0 = (y0 - mean) * rstd * ln_g[c * 32 + 2 * i] + ln_b[c * 32 + 2 * i];
-                    y1 = (y1 - mean) * rstd * ln_g[c * 32 + 2 * i + 1] + ln_b[c * 32 + 2 * i + 1];
-                  } else {
-                    y0 = act_t<A>(y0);
-                    y1 = act_t<A>(y1);
+                  for (int i = 0; i < 16; ++i)
+                    pk[i] = Elem<T>::pack(fmaf(yr[2 * i], rstd, nmr), fmaf(yr[2 * i + 1], rstd, nmr));
+                } else {
+                  const float4* g4 = reinterpret_cast<const float4*>(ln_g + c * 32);
+                  const float4* b4 = reinterpret_cast<const float4*>(ln_b + c * 32);
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+                    const float4 g = g4[j], b = b4[j];
+                    pk[2 * j] = Elem<T>::pack(fmaf(fmaf(yr[4 * j], rstd, nmr), g.x, b.x),
+                                              fmaf(fmaf(yr[4 * j + 1], rstd, nmr), g.y, b.y));
+                    pk[2 * j + 1] = Elem<T>::pack(fmaf(fmaf(yr[4 * j + 2], rstd, nmr), g.z, b.z),
+                                                  fmaf(fmaf(yr[4 * j + 3], rstd, nmr), g.w, b.w));
                   }
-                  pk[i] = Elem<T>::pack(y0, y1);
                 }
-              });
+              } else {
+                act_dispatch(act_id, [&](auto actc) {
+                  constexpr int A = decltype(actc)::value;
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) pk[i] = Elem<T>::pack(act_t<A>(yr[2 * i]), act_t<A>(yr[2 * i + 1]));
+                });
+              }
               store_chunk(c, row0, pk);
             }
           }
