@@ -13,13 +13,14 @@
 //
 //   warp 0        TMA producer: all weights once (smem-resident for the CTA's lifetime), then the
 //                 x tiles as 128x64 K panels through an mbarrier ring.
-//   warp 1        TMEM allocator + single-thread tcgen05.mma issuer.
+//   warp 1        TMEM allocator + the tcgen05.mma issuing thread of accumulator buffer 0;
+//                 the last warp issues buffer 1's MMAs.
 //   warps 2..     NBUF epilogue groups of four warps (one per TMEM accumulator buffer); thread t
 //                 of a group owns row t of its tile (TMEM lane t).
 //
 // With NBUF = 2, two row tiles are in flight, so the tensor core works on one tile while the
-// epilogue of the other runs; the MMA thread picks whichever buffer's next job is ready (no
-// head-of-line blocking on an x panel still in flight). TMEM columns:
+// epilogue of the other runs; each buffer's issuing thread queues its next job as soon as the
+// buffer is released, whatever the other buffer is doing. TMEM columns:
 //   buffer b: [256b, 256b+N)        fp32 accumulator of the current layer
 //             [256b+128, +N/2)      16-bit activation of the previous layer, two values per
 //                                   column: the A operand (A-from-TMEM) of the next layer
