@@ -73,6 +73,9 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=8.0)
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--flush", action="store_true",
+                   help="time workloads smaller than 2 x L2 step by step around an L2 flush instead "
+                        "of rotating over copies of their inputs")
     p.add_argument("--graph", action="store_true",
                    help="capture one step in a CUDA graph and time its replays")
     p.add_argument("--kernel-only", action="store_true",
@@ -265,8 +268,25 @@ def main():
     out = torch.empty(w.m, w.n_out, dtype=w.dtype, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    # Inputs + outputs smaller than twice the L2 would be served from L2 on the next step. Such
+    # workloads rotate over R copies of x and out (R * (x + out) >= 4 x 126 MB), so a step's rows
+    # were last touched R - 1 steps earlier, with at least three L2 capacities of other traffic
+    # in between, and come from HBM; the steps then run back to back like the large workloads.
+    # `--flush` times them one by one around a 256 MB L2-flushing write instead.
+    io_bytes = w.m * w.bytes_per_row
+    small = io_bytes < 2 * L2_BYTES
+    flush = small and (args.flush or args.graph)
+    n_rot = 1
+    if small and not flush:
+        n_rot = int(min(256, max(2, -(-4 * L2_BYTES // max(io_bytes, 1)))))
+    xs = [x] + [x.clone() for _ in range(n_rot - 1)]
+    outs = [out] + [torch.empty_like(out) for _ in range(n_rot - 1)]
+    it = [0]
+
     def step():
-        cuda_ext.run_workload_out(w, x, wd, lnd, out)
+        i = it[0] % n_rot
+        it[0] += 1
+        cuda_ext.run_workload_out(w, xs[i], wd, lnd, outs[i])
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -293,11 +313,6 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # Inputs + outputs smaller than twice the L2 would be served from L2 on the next step: those
-    # workloads are timed step by step with an L2 flush (a 256 MB write) between steps, outside
-    # the timed event pairs. Larger ones run back to back.
-    io_bytes = w.m * w.bytes_per_row
-    flush = io_bytes < 2 * L2_BYTES
     flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if flush else None
 
     sampler = ClockSampler(local)
@@ -399,9 +414,14 @@ def main():
                        "chain": w.widths, "tail": ["none", "layernorm", "residual+layernorm"][w.tail],
                        "description": w.description,
                        "l2": ("L2 flushed (256 MB write) between timed steps: x %d MB + out %d MB "
-                              "per GPU < 2 x 126 MB" if flush else
-                              "inputs larger than L2 (x %d MB + out %d MB per GPU)") % (
-                           w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20),
+                              "per GPU < 2 x 126 MB" % (w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20)
+                              if flush else
+                              "steps rotate over %d copies of x and out (x %d MB + out %d MB per GPU "
+                              "each; >= 4 x 126 MB in all), so every step reads its rows from HBM" % (
+                                  n_rot, w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20)
+                              if n_rot > 1 else
+                              "inputs larger than L2 (x %d MB + out %d MB per GPU)" % (
+                                  w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20)),
                        "parallelism": f"rows sharded over {world} GPU(s), weights replicated",
                        "launch": "CUDA graph replay of one captured step" if graph is not None
                                  else "library calls per step"},

@@ -256,6 +256,57 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     return;  // uniform over the cluster: both CTAs have the same layout
   }
 
+  // All weights, once: this CTA's NC columns of every layer, completing on the (leader's) w_full.
+  // The leader issues its loads as soon as its barriers exist, so they overlap the rest of the
+  // set-up (bias and LayerNorm staging: about 2 us of global-load latency); a pair's second CTA
+  // issues its own once the cluster has synchronised, since they complete on the leader's barrier.
+  auto load_weights = [&]() {
+    const uint64_t keep = l2_policy_evict_last();
+    if (leader) mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes * CG);
+    const uint32_t wbar = kPair ? mapa_shared(smem_u32(w_full), 0) : smem_u32(w_full);
+#pragma unroll 1
+    for (int l = 0; l < NL; ++l) {
+      const int kl = l == 0 ? K0 : N;
+      const uint32_t wbase = smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
+      for (int kp = 0; kp < kl / kPanel; ++kp)
+        for (int nb = 0; nb < NC / kPanel; ++nb) {
+          const uint32_t dst = wbase + nb * (kl * 128) + kp * (kPanel * 128);
+          const int c0 = static_cast<int>(rank) * NC + nb * kPanel;
+          if constexpr (kPair) {
+            tma_load_2d_pair(dst, &tm.w[l], wbar, c0, kp * kPanel, keep);
+          } else {
+            tma_load_2d_hint(dst, &tm.w[l], wbar, c0, kp * kPanel, keep);
+          }
+        }
+    }
+  };
+
+  // The g-th x panel of this CTA (unit g / kPanels0 of its units, panel g % kPanels0) into ring
+  // slot g % kXS, completing on the (leader's) x_full of that slot.
+  const int x_units = unit0 < num_units ? (num_units - unit0 + units_step - 1) / units_step : 0;
+  const int x_total = x_units * kPanels0;
+  auto load_x = [&](int g) {
+    if (args.inject == 1) return;
+    const uint64_t stream = l2_policy_evict_first();
+    const int s = g % kXS, p = g % kPanels0;
+    const int unit = unit0 + (g / kPanels0) * units_step;
+    const int row = unit * L::kUnitRows + static_cast<int>(rank) * kBM;
+    const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
+    // x mode 2: panels >= 2 come from the second source
+    const CUtensorMap* xm = (XM == 2 && p >= 2) ? &tm.x2 : &tm.x;
+    const int xc = (XM == 2 && p >= 2) ? (p - 2) * kPanel : p * kPanel;
+    if constexpr (kPair) {
+      if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
+      tma_load_2d_pair(dst, xm, mapa_shared(smem_u32(&x_full[s]), 0), xc, row, stream);
+    } else {
+      mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
+      tma_load_2d_hint(dst, xm, smem_u32(&x_full[s]), xc, row, stream);
+    }
+  };
+  // single CTA: the first ring's worth of x panels goes out with the weights, before the set-up
+  // below (a pair's loads complete on the leader's barriers, so they wait for the cluster sync)
+  const int kXPre = (!kPair && XM != 1) ? (x_total < kXS ? x_total : kXS) : 0;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXS; ++s) {
       mbar_init(smem_u32(&x_full[s]), 1);
@@ -270,6 +321,8 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&l0_turn[b]), 1);
     *abort_flag = 0;
     fence_mbar_init();
+    if (leader) load_weights();
+    for (int g = 0; g < kXPre; ++g) load_x(g);
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm.x);
@@ -286,7 +339,8 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   }
   // bias slices (row 0 of each 8-row x 128-byte atom holds this CTA's NC bias values; rows 1..7
   // and a trailing atom are zero) and the LayerNorm parameters in fp32
-  for (int i = threadIdx.x; i < L::kBiasBytes / 16; i += blockDim.x) {
+  // (warp 0 is issuing the loads above meanwhile)
+  for (int i = static_cast<int>(threadIdx.x) - 32; i >= 0 && i < L::kBiasBytes / 16; i += blockDim.x - 32) {
     const int atom = i >> 6, chunk = i & 63;  // 64 chunks of 16 B per atom
     uint4 val = make_uint4(0, 0, 0, 0);
     const int l = atom / (NC / 64), nb = atom % (NC / 64);
@@ -299,7 +353,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   }
   int ident_local = 1;
   if constexpr (TAIL == kTailLayerNorm) {
-    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    for (int i = static_cast<int>(threadIdx.x) - 32; i >= 0 && i < N; i += blockDim.x - 32) {
       const T* g = reinterpret_cast<const T*>(args.gamma);
       const T* b = reinterpret_cast<const T*>(args.beta);
       ln_g[i] = g != nullptr ? Elem<T>::to_f(g[i]) : 1.0f;
@@ -339,19 +393,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     // nodes[dst] panels (4, 5). Lane l fetches rows 4l..4l+3 of a gathered panel with one
     // tile::gather4 request; both CTAs' requests complete on the leader's x_full.
     const bool src_warp = warp == 0;
-    if (src_warp && lane == 0) {
-      const uint64_t keep = l2_policy_evict_last();
-      if (leader) mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes * CG);
-#pragma unroll 1
-      for (int l = 0; l < NL; ++l) {
-        const int kl = l == 0 ? K0 : N;
-        const uint32_t wbase = smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
-        for (int kp = 0; kp < kl / kPanel; ++kp)
-          for (int nb = 0; nb < NC / kPanel; ++nb)
-            tma_load_2d_pair(wbase + nb * (kl * 128) + kp * (kPanel * 128), &tm.w[l], leader_bar(w_full),
-                             static_cast<int>(rank) * NC + nb * kPanel, kp * kPanel, keep);
-      }
-    }
+    if (src_warp && lane == 0 && !leader) load_weights();
     const uint64_t stream = l2_policy_evict_first();
     const uint64_t keep_nodes = l2_policy_evict_last();
     const int64_t* gidx = args.gidx[src_warp ? 0 : 1];
@@ -407,52 +449,14 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   } else if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      const uint64_t keep = l2_policy_evict_last();
-      const uint64_t stream = l2_policy_evict_first();
-      if (leader) mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes * CG);
-      const uint32_t wbar = leader_bar(w_full);
+      if (!leader) load_weights();
+      // the x ring in panel order; the single-CTA form issued the first kXS loads at set-up
 #pragma unroll 1
-      for (int l = 0; l < NL; ++l) {
-        const int kl = l == 0 ? K0 : N;
-        const uint32_t wbase =
-            smem_u32(smem + L::kOffW + w_layer_offset(l, L::kW0Bytes, L::kWhBytes));
-        for (int kp = 0; kp < kl / kPanel; ++kp)
-          for (int nb = 0; nb < NC / kPanel; ++nb) {
-            const uint32_t dst = wbase + nb * (kl * 128) + kp * (kPanel * 128);
-            const int c0 = static_cast<int>(rank) * NC + nb * kPanel;
-            if constexpr (kPair) {
-              tma_load_2d_pair(dst, &tm.w[l], wbar, c0, kp * kPanel, keep);
-            } else {
-              tma_load_2d_hint(dst, &tm.w[l], wbar, c0, kp * kPanel, keep);
-            }
-          }
+      for (int g = kXPre; g < x_total; ++g) {
+        const int s = g % kXS;
+        if (!mbar_wait<kPair>(smem_u32(&x_empty[s]), ((g / kXS) & 1) ^ 1, wctx, kDevTimeoutProducer)) break;
+        load_x(g);
       }
-      int s = 0;
-      uint32_t ph = 0;
-#pragma unroll 1
-      for (int unit = unit0; unit < num_units; unit += units_step) {
-        const int row = unit * L::kUnitRows + static_cast<int>(rank) * kBM;
-#pragma unroll 1
-        for (int p = 0; p < kPanels0; ++p) {
-          if (!mbar_wait<kPair>(smem_u32(&x_empty[s]), ph ^ 1, wctx, kDevTimeoutProducer))
-            goto producer_done;
-          if (args.inject != 1) {
-            const uint32_t dst = smem_u32(smem + L::kOffX + s * kPanelBytes);
-            // x mode 2: panels >= 2 come from the second source
-            const CUtensorMap* xm = (XM == 2 && p >= 2) ? &tm.x2 : &tm.x;
-            const int xc = (XM == 2 && p >= 2) ? (p - 2) * kPanel : p * kPanel;
-            if constexpr (kPair) {
-              if (leader) mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes * CG);
-              tma_load_2d_pair(dst, xm, leader_bar(&x_full[s]), xc, row, stream);
-            } else {
-              mbar_arrive_expect_tx(smem_u32(&x_full[s]), kPanelBytes);
-              tma_load_2d_hint(dst, xm, smem_u32(&x_full[s]), xc, row, stream);
-            }
-          }
-          if (++s == kXS) { s = 0; ph ^= 1; }
-        }
-      }
-    producer_done:;
     }
     __syncwarp();
   } else if (warp == 1 || warp == kIssWarp1) {

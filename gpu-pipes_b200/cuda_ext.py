@@ -28,6 +28,9 @@ _DT = {torch.float16: L.GP_F16, torch.bfloat16: L.GP_BF16}
 def _check_input(name: str, t: torch.Tensor | None, dtype: torch.dtype | None = None) -> None:
     if t is None:
         return
+    if (type(t) is torch.Tensor and t.is_cuda and t.is_contiguous()
+            and (dtype is None or t.dtype == dtype)):
+        return  # the common case, in one test
     if not isinstance(t, torch.Tensor):
         raise RuntimeError(f"{name} must be a tensor")
     if not t.is_cuda:
@@ -42,8 +45,50 @@ def _ptr(t: torch.Tensor | None):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    """torch's current stream on t's device (the raw handle straight from torch's C layer where
+    available: the Stream object costs a couple of microseconds per call)."""
+    if _raw_stream is not None and t.device.index is not None:
+        return ctypes.c_void_p(_raw_stream(t.device.index))
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+class _on_device:
+    """`with torch.cuda.device(dev)`, skipped when `dev` is already current (the common case;
+    switching costs microseconds of host time per call)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, dev: torch.device):
+        self.idx = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+_SPECS: dict = {}
+
+
+def _spec(widths, acts, tail, dt, ln_eps, skip_layer):
+    """The chain description, built once per distinct chain (the struct is read-only to C)."""
+    key = (tuple(widths), tuple(acts), tail, dt, ln_eps, skip_layer)
+    s = _SPECS.get(key)
+    if s is None:
+        s = _SPECS[key] = L.make_spec(widths, acts, tail, dt, ln_eps, skip_layer)
+    return s
 
 
 def fused_mlp_out(x, weights, biases, out, *, acts, tail=L.TAIL_NONE, gamma=None, beta=None,
@@ -71,11 +116,11 @@ def fused_mlp_out(x, weights, biases, out, *, acts, tail=L.TAIL_NONE, gamma=None
             raise RuntimeError(f"w{i + 1} has shape {tuple(w.shape)}, expected [{k}, N]")
     if out.shape[0] != x.shape[0] or out.shape[1] != widths[-1]:
         raise RuntimeError(f"out has shape {tuple(out.shape)}, expected [{x.shape[0]}, {widths[-1]}]")
-    spec = L.make_spec(widths, acts, tail, dt, ln_eps, skip_layer)
+    spec = _spec(widths, acts, tail, dt, ln_eps, skip_layer)
     n = len(weights)
     wp = (ctypes.c_void_p * n)(*[w.data_ptr() for w in weights])
     bp = (ctypes.c_void_p * n)(*[(b.data_ptr() if b is not None else None) for b in biases])
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         L.check(L.lib().gp_fused_mlp_out(ctypes.byref(spec), x.shape[0], _ptr(x), wp, bp,
                                          _ptr(gamma), _ptr(beta), _ptr(out), _stream(x)))
 
