@@ -76,8 +76,8 @@ def parse():
     p.add_argument("--flush", action="store_true",
                    help="time workloads smaller than 2 x L2 step by step around an L2 flush instead "
                         "of rotating over copies of their inputs")
-    p.add_argument("--graph", action="store_true",
-                   help="capture one step in a CUDA graph and time its replays")
+    p.add_argument("--no-graph", action="store_true",
+                   help="time per-step library calls instead of CUDA-graph replays of captured steps")
     p.add_argument("--kernel-only", action="store_true",
                    help="time the kernel only (no e2e, CPU baseline or clock sampling); for ncu")
     return p.parse_args()
@@ -275,7 +275,7 @@ def main():
     # `--flush` times them one by one around a 256 MB L2-flushing write instead.
     io_bytes = w.m * w.bytes_per_row
     small = io_bytes < 2 * L2_BYTES
-    flush = small and (args.flush or args.graph)
+    flush = small and args.flush
     n_rot = 1
     if small and not flush:
         n_rot = int(min(256, max(2, -(-4 * L2_BYTES // max(io_bytes, 1)))))
@@ -293,17 +293,46 @@ def main():
     torch.cuda.synchronize()
     graph = None
     graph_launches = 0
-    if args.graph:
-        # one step captured after the warm-up (workspaces already at size, so the capture
-        # allocates nothing); replays run the same kernels with no host work per step
-        graph = torch.cuda.CUDAGraph()
+    if not args.no_graph:
+        # One captured step per input copy, after the warm-up (the workspaces are at size, so the
+        # capture allocates nothing). A replay enqueues the step's kernels with no host work, so
+        # a small step (MGN node on one of 8 GPUs: ~23 us) is not bounded by the ~19 us of host
+        # time per library call. The library path itself is what `e2e` measures.
+        graphs = []
         n0 = L.launch_count()
-        with torch.cuda.graph(graph):
-            step()
-        graph_launches = L.launch_count() - n0
+        for _ in range(n_rot):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step()
+            graphs.append(g)
+        graph_launches = (L.launch_count() - n0) / n_rot
+        # and all n_rot steps in one graph, so consecutive small steps also skip the per-graph
+        # launch; the per-copy graphs cover a remainder of fewer than n_rot steps
+        whole = None
+        if n_rot > 1:
+            whole = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(whole):
+                for _ in range(n_rot):
+                    step()
         torch.cuda.synchronize()
-        step = graph.replay  # noqa: F811
-        for _ in range(3):
+        graph = graphs[0]
+
+        def run_steps(k):
+            done = 0
+            if whole is not None:
+                while k - done >= n_rot:
+                    whole.replay()
+                    done += n_rot
+            for i in range(k - done):
+                graphs[i % n_rot].replay()
+
+        git = [0]
+
+        def step():  # noqa: F811
+            graphs[git[0] % n_rot].replay()
+            git[0] += 1
+
+        for _ in range(max(3, n_rot)):
             step()
         torch.cuda.synchronize()
 
@@ -334,14 +363,17 @@ def main():
     else:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
-        for _ in range(args.steps):
-            step()
+        if graph is not None:
+            run_steps(args.steps)
+        else:
+            for _ in range(args.steps):
+                step()
         ev1.record(stream)
         barrier()
         ms = ev0.elapsed_time(ev1)
     launches = L.launch_count() - launches0
     if graph is not None:  # replays enqueue the captured kernels without calling the library
-        launches = graph_launches * args.steps
+        launches = int(round(graph_launches * args.steps))
     clocks = sampler.stop() if not args.kernel_only else None
     if dist is not None:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -423,7 +455,7 @@ def main():
                               "inputs larger than L2 (x %d MB + out %d MB per GPU)" % (
                                   w.m * w.in_width * 2 >> 20, w.m * w.n_out * 2 >> 20)),
                        "parallelism": f"rows sharded over {world} GPU(s), weights replicated",
-                       "launch": "CUDA graph replay of one captured step" if graph is not None
+                       "launch": "CUDA graph replays of the captured steps" if graph is not None
                                  else "library calls per step"},
             "tflops": value * w.flop_per_row / 1e12,
             "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit,
