@@ -47,6 +47,7 @@ struct ChainArgs {
   int64_t n_nodes;
   float* scatter;                     // [n_nodes, N_last] fp32, += out row at gidx[1] (or null)
   void* out2;                         // side output rows [M, N(SIDE)] (stream kernel, SIDE chains)
+  int pdl_early;                      // reads allowed before griddepcontrol.wait: 1 parameters, 2 x
 };
 
 }  // namespace gp

@@ -120,6 +120,78 @@ static std::atomic<int> g_variant{[] {
   return e != nullptr ? std::atoi(e) : 0;
 }()};
 
+// GP_PDL: 0 = plain launches, 2 = programmatic launches without early reads (measurement),
+// otherwise programmatic launches with early reads
+static const int g_pdl_mode = [] {
+  const char* e = std::getenv("GP_PDL");
+  return e == nullptr ? 1 : (e[0] == '0' ? 0 : (e[0] == '2' ? 2 : 1));
+}();
+
+bool pdl_enabled() { return g_pdl_mode != 0; }
+
+namespace {
+struct PdlRecord {
+  int dev = -1;
+  cudaStream_t stream = nullptr;
+  unsigned long long stamp = 0;  // 0: free slot
+  bool unknown = true;
+  int n = 0;
+  uintptr_t lo[PdlIo::kMax];
+  uintptr_t hi[PdlIo::kMax];
+};
+std::mutex g_pdl_mu;
+PdlRecord g_pdl[64];
+unsigned long long g_pdl_clock = 0;
+}  // namespace
+
+PdlLaunch::PdlLaunch(cudaStream_t stream) {
+  g_pdl_mu.lock();
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  // this stream's slot, else the least recently used one (a stream whose record was dropped
+  // allows no early reads until its next launch records again)
+  int hit = -1, lru = 0;
+  for (int i = 0; i < 64; ++i) {
+    if (g_pdl[i].stamp != 0 && g_pdl[i].dev == dev && g_pdl[i].stream == stream) hit = i;
+    if (g_pdl[i].stamp < g_pdl[lru].stamp) lru = i;
+  }
+  if (hit < 0) {
+    hit = lru;
+    g_pdl[hit].dev = dev;
+    g_pdl[hit].stream = stream;
+    g_pdl[hit].unknown = true;
+    g_pdl[hit].n = 0;
+  }
+  g_pdl[hit].stamp = ++g_pdl_clock;
+  slot_ = hit;
+}
+
+PdlLaunch::~PdlLaunch() { g_pdl_mu.unlock(); }
+
+int PdlLaunch::early_flags(const PdlIo& io) const {
+  const PdlRecord& r = g_pdl[slot_];
+  if (g_pdl_mode != 1 || r.unknown || io.overflow) return 0;
+  int flags = 3;
+  for (int i = 0; i < io.n; ++i) {
+    if (io.kind[i] == PdlIo::kWrite) continue;
+    for (int j = 0; j < r.n; ++j)
+      if (io.lo[i] < r.hi[j] && r.lo[j] < io.hi[i]) flags &= io.kind[i] == PdlIo::kParam ? ~1 : ~2;
+  }
+  return flags;
+}
+
+void PdlLaunch::record(const PdlIo& io) {
+  PdlRecord& r = g_pdl[slot_];
+  r.unknown = io.overflow || io.writes_unknown;
+  r.n = 0;
+  for (int i = 0; !r.unknown && i < io.n; ++i)
+    if (io.kind[i] == PdlIo::kWrite) {
+      r.lo[r.n] = io.lo[i];
+      r.hi[r.n] = io.hi[i];
+      ++r.n;
+    }
+}
+
 static int wanted_variant() { return g_variant.load(std::memory_order_relaxed); }
 
 void set_kernel_variant(int v) { g_variant.store(v); }

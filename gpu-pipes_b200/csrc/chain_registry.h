@@ -90,4 +90,71 @@ int noalloc_status(bool clear, int* status);
 // Sets the dynamic shared memory attribute of `kern` once per device.
 int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask);
 
+// Programmatic dependent launch of the persistent chain kernels (on unless the environment sets
+// GP_PDL=0): a launch may start while the stream's previous kernel drains; the kernel initialises
+// its barriers, then waits for that kernel (griddepcontrol.wait) before any global access.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_chain_kernel(void (*kern)(KArgs...), int grid, int block, int smem, cudaStream_t stream,
+                                Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(block), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  // a launch error is left in the runtime's last-error state, which the entry points check
+  (void)cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Early reads under programmatic dependent launch. A chain kernel may read its weights and
+// per-column parameters (bit 1 of ChainArgs::pdl_early) and its input rows (bit 2) before its
+// griddepcontrol.wait, overlapping the previous kernel of the stream, when those bytes do not
+// overlap anything that kernel writes. Every kernel triggers its dependents only after its own
+// wait, so the previous chain kernel is the only one that can still run. PdlLaunch holds the
+// per-(device, stream) record of the last chain launch's writes, under a lock kept from the flag
+// computation through the launch; a stream without a record, and a launch whose writes are not
+// listed exactly, allow no early reads.
+struct PdlIo {
+  static constexpr int kMax = 2 * kMaxLayers + 12;
+  enum Kind : uint8_t { kParam = 0, kX = 1, kWrite = 2 };
+  uintptr_t lo[kMax];
+  uintptr_t hi[kMax];
+  uint8_t kind[kMax];
+  int n = 0;
+  bool overflow = false;        // a range did not fit: nothing early, writes unknown
+  bool writes_unknown = false;  // the next launch on the stream reads nothing early
+  void add(Kind k, const void* p, uint64_t bytes) {
+    if (p == nullptr || bytes == 0) return;
+    if (n == kMax) {
+      overflow = true;
+      return;
+    }
+    lo[n] = reinterpret_cast<uintptr_t>(p);
+    hi[n] = lo[n] + bytes;
+    kind[n] = k;
+    ++n;
+  }
+};
+
+class PdlLaunch {
+ public:
+  explicit PdlLaunch(cudaStream_t stream);
+  ~PdlLaunch();
+  PdlLaunch(const PdlLaunch&) = delete;
+  PdlLaunch& operator=(const PdlLaunch&) = delete;
+  // ChainArgs::pdl_early bits allowed for a launch with these ranges
+  int early_flags(const PdlIo& io) const;
+  // the writes of the launch just made become the stream's record
+  void record(const PdlIo& io);
+
+ private:
+  int slot_;
+};
+
 }  // namespace gp

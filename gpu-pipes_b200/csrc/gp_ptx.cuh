@@ -54,6 +54,17 @@ __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch. launch_dependents lets the next grid of the stream be scheduled
+// once every CTA of this grid has issued it (its CTAs then take SMs as this grid's CTAs exit and
+// run their set-up); wait blocks until the previous grid of the stream has completed and its
+// memory operations are visible. A kernel touches global memory only after its wait. Both are
+// no-ops in a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }

@@ -80,9 +80,22 @@ int launch_tmem(const LaunchCtx& c) {
   }
   ChainArgs args = c.args;
   args.num_tiles = static_cast<int>((c.m + L::kUnitRows - 1) / L::kUnitRows);
+  const uint64_t es = 2, rows = static_cast<uint64_t>(c.m);
+  PdlIo io;
+  for (int l = 0; l < C::NL; ++l) {
+    const void* wl = (C::HIDDEN_F16 && l > 0) ? static_cast<const void*>(static_cast<char*>(scratch) + offs[l]) : c.w[l];
+    io.add(PdlIo::kParam, wl, static_cast<uint64_t>(C::K(l)) * C::N(l) * es);
+    io.add(PdlIo::kParam, args.bias[l], static_cast<uint64_t>(C::N(l)) * es);
+  }
+  io.add(PdlIo::kParam, args.gamma, static_cast<uint64_t>(L::NLast) * es);
+  io.add(PdlIo::kParam, args.beta, static_cast<uint64_t>(L::NLast) * es);
+  io.add(PdlIo::kX, c.x, rows * C::K(0) * es);
+  io.add(PdlIo::kWrite, c.out, rows * L::NLast * es);
+  PdlLaunch pdl(c.stream);
+  args.pdl_early = pdl.early_flags(io);
   if constexpr (CG == 1) {
     const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-    mlp_tmem_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+    launch_chain_kernel(&mlp_tmem_kernel<C>, grid, L::kThreads, L::kSmemBytes, c.stream, tm, args);
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -110,8 +123,9 @@ int launch_tmem(const LaunchCtx& c) {
       mc_slot.store(n, std::memory_order_relaxed);
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
-    mlp_tmem_pair_kernel<C><<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+    launch_chain_kernel(&mlp_tmem_pair_kernel<C>, 2 * clusters, L::kThreads, L::kSmemBytes, c.stream, tm, args);
   }
+  pdl.record(io);
   if (scratch != nullptr) workspace_release(c.stream);
   return GP_OK;
 }

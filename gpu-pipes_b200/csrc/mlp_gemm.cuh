@@ -106,6 +106,7 @@ __device__ __forceinline__ void mlp_gemm_body(const TensorMaps& tm, const GemmAr
   const int units_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if ((smem_u32(smem) & 1023u) != 0) {
+    pdl_wait_prior();
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
     return;
   }
@@ -122,6 +123,9 @@ __device__ __forceinline__ void mlp_gemm_body(const TensorMaps& tm, const GemmAr
     *abort_flag = 0;
     fence_mbar_init();
   }
+  // everything above overlaps the previous kernel of the stream; global memory only from here
+  pdl_wait_prior();
+  if (threadIdx.x == 0) pdl_launch_dependents();  // after this grid's wait
   if (warp == 1) {
     if constexpr (kPair) {
       tmem_alloc_pair(smem_u32(tmem_holder), 512);

@@ -252,6 +252,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
 
   // the swizzled operand layouts assume a 1024-byte aligned shared window
   if ((smem_u32(smem) & 1023u) != 0) {
+    pdl_wait_prior();
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
     return;  // uniform over the cluster: both CTAs have the same layout
   }
@@ -321,21 +322,20 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&l0_turn[b]), 1);
     *abort_flag = 0;
     fence_mbar_init();
-    if (leader) load_weights();
-    for (int g = 0; g < kXPre; ++g) load_x(g);
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm.x);
     prefetch_tmap(&tm.out);
   }
-  if (warp == 1) {
-    if constexpr (kPair) {
-      tmem_alloc_pair(smem_u32(tmem_holder), L::kTmemCols);
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(smem_u32(tmem_holder), L::kTmemCols);
-      tmem_relinquish();
-    }
+  // Everything above overlaps the previous kernel of the stream. Global memory is touched only
+  // after griddepcontrol.wait, except the reads that the launch marked safe (pdl_early: weights,
+  // biases and LayerNorm parameters; x), which go out first.
+  const int early = args.pdl_early;
+  if ((early & 1) == 0) pdl_wait_prior();
+  if (threadIdx.x == 0) {
+    if (leader) load_weights();
+    if (early & 2)
+      for (int g = 0; g < kXPre; ++g) load_x(g);
   }
   // bias slices (row 0 of each 8-row x 128-byte atom holds this CTA's NC bias values; rows 1..7
   // and a trailing atom are zero) and the LayerNorm parameters in fp32
@@ -359,6 +359,21 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
       ln_g[i] = g != nullptr ? Elem<T>::to_f(g[i]) : 1.0f;
       ln_b[i] = b != nullptr ? Elem<T>::to_f(b[i]) : 0.0f;
       ident_local &= (ln_g[i] == 1.0f && ln_b[i] == 0.0f) ? 1 : 0;
+    }
+  }
+  if (early & 1) pdl_wait_prior();
+  if (threadIdx.x == 0) {
+    if ((early & 2) == 0)
+      for (int g = 0; g < kXPre; ++g) load_x(g);
+    pdl_launch_dependents();  // after this grid's wait: only this grid can precede the next one
+  }
+  if (warp == 1) {
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_holder), L::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), L::kTmemCols);
+      tmem_relinquish();
     }
   }
   fence_proxy_async_smem();

@@ -287,6 +287,7 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
   const int units_step = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if ((smem_u32(smem) & 1023u) != 0) {
+    pdl_wait_prior();
     if (threadIdx.x == 0) atomicCAS(args.status, 0, kDevBadSmemAlign);
     return;
   }
@@ -309,15 +310,11 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) prefetch_tmap(&tm.x);
-  if (warp == 1) {
-    if constexpr (kPair) {
-      tmem_alloc_pair(smem_u32(tmem_holder), 512);
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(smem_u32(tmem_holder), 512);
-      tmem_relinquish();
-    }
-  }
+  // Everything above overlaps the previous kernel of the stream. Global memory is touched only
+  // after griddepcontrol.wait, except the per-column parameters when the launch marked them safe
+  // (pdl_early bit 1), which are staged first.
+  const int early = args.pdl_early;
+  if ((early & 1) == 0) pdl_wait_prior();
   // fp32 biases, LayerNorm parameters and head weights
   for (int l = 0; l < NL; ++l) {
     const T* b = reinterpret_cast<const T*>(args.bias[l]);
@@ -346,6 +343,17 @@ __device__ __forceinline__ void mlp_stream_body(const TensorMaps& tm, const Chai
     }
     for (int i = threadIdx.x; i < 16; i += blockDim.x)
       head_b[i] = (i < C::HEAD_N && hb != nullptr) ? Elem<T>::to_f(hb[i]) : 0.0f;
+  }
+  if (early & 1) pdl_wait_prior();
+  if (threadIdx.x == 0) pdl_launch_dependents();  // after this grid's wait: only this grid can precede the next one
+  if (warp == 1) {
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_holder), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   if constexpr (kPair) {

@@ -181,7 +181,15 @@ int na_launch(NoAllocDevice& d, int64_t m, const void* x, const void* w0, const 
   args.timeout_ns = current_timeout_ns();
   args.inject = current_fault_injection();
   const int grid = args.num_tiles < d.sm_count ? args.num_tiles : d.sm_count;
-  mlp_stream_kernel<C><<<grid, Lay::kThreads, Lay::kSmemBytes, stream>>>(tm, args);
+  {
+    // a plain launch (it overlaps no earlier kernel), but its kernel triggers the next launch of
+    // the stream early, so the stream's record must not allow early reads after it
+    PdlLaunch pdl(stream);
+    mlp_stream_kernel<C><<<grid, Lay::kThreads, Lay::kSmemBytes, stream>>>(tm, args);
+    PdlIo io;
+    io.writes_unknown = true;
+    pdl.record(io);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(GP_ERR_CUDA, "launch: %s", cudaGetErrorString(e));
   count_launches(2);  // the weight conversion and the chain kernel

@@ -41,9 +41,28 @@ int launch_resident_cg(const LaunchCtx& c) {
   if (rc != GP_OK) return rc;
   ChainArgs args = c.args;
   args.num_tiles = static_cast<int>((c.m + L::kUnitRows - 1) / L::kUnitRows);
+  const uint64_t es = 2, rows = static_cast<uint64_t>(c.m);
+  PdlIo io;
+  for (int l = 0; l < NL; ++l) {
+    io.add(PdlIo::kParam, c.w[l], static_cast<uint64_t>(l == 0 ? K0 : N) * N * es);
+    io.add(PdlIo::kParam, args.bias[l], N * es);
+  }
+  io.add(PdlIo::kParam, args.gamma, N * es);
+  io.add(PdlIo::kParam, args.beta, N * es);
+  io.add(PdlIo::kX, c.x, rows * (XM == 0 ? K0 : 128) * es);
+  if (XM == 2) io.add(PdlIo::kX, c.x2, rows * (K0 - 128) * es);
+  if (XM == 1) {
+    io.add(PdlIo::kX, args.gnodes, static_cast<uint64_t>(args.n_nodes) * 128 * es);
+    io.add(PdlIo::kX, args.gidx[0], rows * 8);
+    io.add(PdlIo::kX, args.gidx[1], rows * 8);
+  }
+  io.add(PdlIo::kWrite, c.out, rows * N * es);
+  io.add(PdlIo::kWrite, args.scatter, static_cast<uint64_t>(args.n_nodes) * N * 4);
+  PdlLaunch pdl(c.stream);
+  args.pdl_early = pdl.early_flags(io);
   if constexpr (CG == 1) {
     const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-    mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM><<<grid, kThr, kSmem, c.stream>>>(tm, args);
+    launch_chain_kernel(&mlp_resident_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>, grid, kThr, kSmem, c.stream, tm, args);
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -71,9 +90,10 @@ int launch_resident_cg(const LaunchCtx& c) {
       mc_slot.store(n, std::memory_order_relaxed);
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
-    mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>
-        <<<2 * clusters, kThr, kSmem, c.stream>>>(tm, args);
+    launch_chain_kernel(&mlp_resident_pair_kernel<T, K0, N, NL, ACTS, TAIL, NBUF, XM>, 2 * clusters, kThr, kSmem,
+                        c.stream, tm, args);
   }
+  pdl.record(io);
   return GP_OK;
 }
 

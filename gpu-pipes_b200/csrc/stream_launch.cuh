@@ -76,9 +76,30 @@ int launch_stream(const LaunchCtx& c) {
     args.head_b = c.args.bias[C::NL];
   }
   args.num_tiles = static_cast<int>((c.m + kBM * CG - 1) / (kBM * CG));
+  const uint64_t es = 2, rows = static_cast<uint64_t>(c.m);
+  PdlIo io;
+  for (int l = 0; l < C::NL; ++l) {
+    const bool conv = C::HIDDEN_F16 && l > 0;
+    const void* wl = conv ? static_cast<const void*>(static_cast<char*>(scratch) + offs[l]) : c.w[l];
+    io.add(PdlIo::kParam, wl, static_cast<uint64_t>(WeightRows<C>::get(l)) * C::N(l) * es);
+    io.add(PdlIo::kParam, args.bias[l], static_cast<uint64_t>(C::N(l)) * es);
+  }
+  io.add(PdlIo::kParam, args.gamma, static_cast<uint64_t>(C::N(C::NL - 1)) * es);
+  io.add(PdlIo::kParam, args.beta, static_cast<uint64_t>(C::N(C::NL - 1)) * es);
+  if constexpr (C::TAIL == kTailHead) {
+    io.add(PdlIo::kParam, args.head_w, static_cast<uint64_t>(C::N(C::NL - 1)) * C::HEAD_N * es);
+    io.add(PdlIo::kParam, args.head_b, static_cast<uint64_t>(C::HEAD_N) * es);
+  }
+  io.add(PdlIo::kX, c.x, rows * static_cast<uint64_t>(c.x_ld != 0 ? c.x_ld : C::K(0)) * es);
+  if constexpr (L::kSkip2 != 0) io.add(PdlIo::kX, c.x2, rows * C::X2_COLS * es);
+  io.add(PdlIo::kX, args.resid, rows * C::N(C::NL - 1) * es);
+  io.add(PdlIo::kWrite, c.out, rows * static_cast<uint64_t>(c.out_ld != 0 ? c.out_ld : L::kOutN) * es);
+  if constexpr (L::kSide > 0) io.add(PdlIo::kWrite, args.out2, rows * C::N(L::kSide) * es);
+  PdlLaunch pdl(c.stream);
+  args.pdl_early = pdl.early_flags(io);
   if constexpr (CG == 1) {
     const int grid = args.num_tiles < c.sm_count ? args.num_tiles : c.sm_count;
-    mlp_stream_kernel<C><<<grid, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+    launch_chain_kernel(&mlp_stream_kernel<C>, grid, L::kThreads, L::kSmemBytes, c.stream, tm, args);
   } else {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -106,8 +127,9 @@ int launch_stream(const LaunchCtx& c) {
       mc_slot.store(n, std::memory_order_relaxed);
     }
     const int clusters = args.num_tiles < mc ? args.num_tiles : mc;
-    mlp_stream_pair_kernel<C><<<2 * clusters, L::kThreads, L::kSmemBytes, c.stream>>>(tm, args);
+    launch_chain_kernel(&mlp_stream_pair_kernel<C>, 2 * clusters, L::kThreads, L::kSmemBytes, c.stream, tm, args);
   }
+  pdl.record(io);
   if (scratch != nullptr) workspace_release(c.stream);
   return GP_OK;
 }

@@ -56,7 +56,14 @@ int gemm_launch_t(cudaStream_t s, int sm_count, const TensorMaps& tm, const Gemm
     mc_slot.store(n, std::memory_order_relaxed);
   }
   const int clusters = g.num_tiles < mc ? g.num_tiles : mc;
-  mlp_gemm_pair_kernel<ACT, OUT_F32><<<2 * clusters, L::kThreads, L::kSmemBytes, s>>>(tm, g, a_bf16);
+  {
+    // the GEMM reads nothing before its wait; its writes are not listed
+    PdlLaunch pdl(s);
+    launch_chain_kernel(&mlp_gemm_pair_kernel<ACT, OUT_F32>, 2 * clusters, L::kThreads, L::kSmemBytes, s, tm, g, a_bf16);
+    PdlIo io;
+    io.writes_unknown = true;
+    pdl.record(io);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
 }
