@@ -42,6 +42,8 @@ GP_DECLARE(launch_gc_relu_f16_k1024)
 GP_DECLARE(launch_nerf_f16)
 GP_DECLARE(launch_nerf_trunk_f16)
 GP_DECLARE(launch_bert_ffn_bf16)
+GP_DECLARE(launch_bert_ffn_bf16_chain)
+GP_DECLARE(launch_dlrm_top_f16_chain)
 GP_DECLARE(launch_dlrm_top_f16)
 GP_DECLARE(launch_dlrm_top_f16_ref)
 #undef GP_DECLARE2
@@ -105,8 +107,12 @@ static const ChainEntry kChains[] = {
     // chains with activations too wide for one SM: per-layer GEMMs over large row chunks
     {"bert_ffn_bf16", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
      launch_bert_ffn_bf16, 0},
+    {"bert_ffn_bf16_chain", GP_BF16, 2, {1024, 4096, 1024}, {GP_ACT_GELU_TANH, NO}, GP_TAIL_RESIDUAL_LN,
+     launch_bert_ffn_bf16_chain, 1},
     {"dlrm_top_f16", GP_F16, 5, {480, 1024, 1024, 512, 256, 1}, {R, R, R, R, GP_ACT_SIGMOID},
      GP_TAIL_NONE, launch_dlrm_top_f16, 0},
+    {"dlrm_top_f16_chain", GP_F16, 5, {480, 1024, 1024, 512, 256, 1}, {R, R, R, R, GP_ACT_SIGMOID},
+     GP_TAIL_NONE, launch_dlrm_top_f16_chain, 1},
     // the reference app's own top MLP (apps/dlrm_topmlp/pipelined/val.py:11-12): ReLU everywhere
     {"dlrm_top_f16_ref", GP_F16, 5, {512, 1024, 1024, 512, 256, 64}, {R, R, R, R, R},
      GP_TAIL_NONE, launch_dlrm_top_f16_ref, 0},

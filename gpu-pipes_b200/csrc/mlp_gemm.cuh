@@ -345,15 +345,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   mlp_gemm_body<ACT, OUT_F32, 2>(tm, args, ab_bf16);
 }
 
-// Row LayerNorm over fp32 rows of width N (multiple of 128): one warp per row, two passes in
-// registers (mean, then squared deviations), out = (y - mean) / sqrt(var + eps) * gamma + beta.
+// LayerNorm of one fp32 row of width N (multiple of 128) by one warp, two passes in registers
+// (mean, then squared deviations): dst = (y - mean) / sqrt(var + eps) * gamma + beta, 16-bit.
 template <int N>
-__global__ void __launch_bounds__(256)
-    row_layernorm_kernel(const float* __restrict__ y, const void* gamma, const void* beta, int g_bf16,
-                         float eps, int64_t m, void* out, int out_bf16) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= m) return;
+__device__ __forceinline__ void layernorm_row_warp(const float* __restrict__ src, const void* gamma,
+                                                   const void* beta, int g_bf16, float eps,
+                                                   uint16_t* dst, int out_bf16, int lane) {
   constexpr int kPer = N / 128;  // float4 per lane
   // gamma / beta as four 16-bit values per load (when both are 8-byte aligned; the interface
   // only requires 4), issued first so their latency overlaps the row's
@@ -377,11 +374,11 @@ __global__ void __launch_bounds__(256)
     }
   }
   float4 v[kPer];
-  const float4* src = reinterpret_cast<const float4*>(y + row * N);
+  const float4* src4 = reinterpret_cast<const float4*>(src);
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
-    v[i] = src[i * 32 + lane];
+    v[i] = src4[i * 32 + lane];
     s += v[i].x + v[i].y + v[i].z + v[i].w;
   }
 #pragma unroll
@@ -417,8 +414,19 @@ __global__ void __launch_bounds__(256)
       }
       pk[e] = out_bf16 ? Elem<__nv_bfloat16>::pack(a, b) : Elem<__half>::pack(a, b);
     }
-    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + row * N + col) = make_uint2(pk[0], pk[1]);
+    *reinterpret_cast<uint2*>(dst + col) = make_uint2(pk[0], pk[1]);
   }
+}
+
+// Row LayerNorm over fp32 rows of width N (multiple of 128): one warp per row.
+template <int N>
+__global__ void __launch_bounds__(256)
+    row_layernorm_kernel(const float* __restrict__ y, const void* gamma, const void* beta, int g_bf16,
+                         float eps, int64_t m, void* out, int out_bf16) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= m) return;
+  layernorm_row_warp<N>(y + row * N, gamma, beta, g_bf16, eps, static_cast<uint16_t*>(out) + row * N,
+                        out_bf16, threadIdx.x & 31);
 }
 
 }  // namespace gp

@@ -6,16 +6,21 @@
 //                   and the reference app's own widths 512 -> 1024 -> 1024 -> 512 -> 256 -> 64
 //                   with ReLU after every layer (apps/dlrm_topmlp/pipelined/val.py:11-12,
 //                   DlrmMlp([479 + 33, 1024, 1024, 512, 256, 64]); dlrm_topmlp_pl_ext.cu:34-40)
-// Each chain runs over large row chunks whose intermediates live in the per-device workspace
-// (measured faster than L2-sized chunks: fewer launches and partial waves, and the HBM traffic of
-// the intermediates overlaps the GEMMs); each wide layer is one mlp_gemm_pair_kernel launch; the
-// tail (LayerNorm, or the last two DLRM layers with the sigmoid head) is a row kernel / the
-// weight-streaming chain kernel.
+// Default form: each chain runs over large row chunks whose intermediates live in the per-device
+// workspace (measured faster than L2-sized chunks: fewer launches and partial waves, and the HBM
+// traffic of the intermediates overlaps the GEMMs); each wide layer is one mlp_gemm_pair_kernel
+// launch; the tail (LayerNorm, or the last two DLRM layers with the sigmoid head) is a row kernel
+// / the weight-streaming chain kernel. Other form (variant 1): the whole chain as one
+// mlp_gemm_chain_kernel launch with its intermediates in rings of row blocks (mlp_gemm_chain.cuh);
+// measured slower, see the schedules below.
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "chain_registry.h"
 #include "mlp_gemm.cuh"
+#include "mlp_gemm_chain.cuh"
 #include "stream_launch.cuh"
 
 namespace gp {
@@ -143,6 +148,108 @@ struct ChainDlrmTailRef {
   static constexpr bool SPLIT_ACT = false;
 };
 
+// ------------------------------------------------------------------ single-kernel chains
+// Schedule of a fused chain: step lag of each layer (layer 0 at 0) and of the LayerNorm tiles, and
+// the depth (row blocks) of each layer's output ring. GP_CHAIN_SCHED="l1,l2,...;q" overrides the
+// lags of layers 1.. (and the LayerNorm tile, last) and sets every ring depth (measurement only);
+// depths are raised to what keeps every dependency pointing backwards in the tile sequence.
+struct ChainSched {
+  int lag[kChainMaxStages + 1] = {0};
+  int ring[kChainMaxStages] = {0};
+};
+
+void chain_sched_override(ChainSched* sc, int n_lags) {
+  const char* e = std::getenv("GP_CHAIN_SCHED");
+  if (e == nullptr || *e == 0) return;
+  int v[kChainMaxStages + 1] = {0};
+  int n = 0, q = 0;
+  const char* p = e;
+  while (*p != 0 && *p != ';' && n < n_lags) {
+    v[n++] = std::atoi(p);
+    while (*p != 0 && *p != ',' && *p != ';') ++p;
+    if (*p == ',') ++p;
+  }
+  if (*p == ';') q = std::atoi(p + 1);
+  for (int i = 0; i < n; ++i) sc->lag[i + 1] = v[i];
+  if (q > 0)
+    for (int s = 0; s < kChainMaxStages; ++s) sc->ring[s] = q;
+}
+
+int chain_launch(cudaStream_t s, int sm_count, const GemmChainMaps& tm, const GemmChainArgs& g) {
+  using L = GemmChainLayout;
+  static unsigned long long done_mask = 0;
+  static std::atomic<int> max_clusters[64];
+  const void* kern = reinterpret_cast<const void*>(&mlp_gemm_chain_kernel);
+  int rc = ensure_smem_attr(kern, L::kSmemBytes, &done_mask);
+  if (rc != GP_OK) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>& mc_slot = max_clusters[dev & 63];  // filled once per device; racing first calls store the same value
+  int mc = mc_slot.load(std::memory_order_relaxed);
+  if (mc == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(L::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = sm_count / 2;
+    }
+    mc = n;
+    mc_slot.store(n, std::memory_order_relaxed);
+  }
+  // every pair must be resident at once (tiles wait on other pairs' tiles)
+  const int clusters = g.total < mc ? g.total : mc;
+  {
+    PdlLaunch pdl(s);
+    launch_chain_kernel(&mlp_gemm_chain_kernel, 2 * clusters, L::kThreads, L::kSmemBytes, s, tm, g);
+    PdlIo io;
+    io.writes_unknown = true;
+    pdl.record(io);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GP_OK : set_error(GP_ERR_CUDA, "chain launch: %s", cudaGetErrorString(e));
+}
+
+// Fills the schedule fields of g from sc (n_stages layers, optional LayerNorm tiles) and sizes the
+// rings: a ring of q row blocks is overwritten by the row block q later, which must come after
+// that ring's consumers in the sequence (q > consumer lag - producer lag).
+void chain_schedule(GemmChainArgs* g, ChainSched sc, int ln) {
+  const int nb = g->n_blocks;
+  g->total = 0;
+  for (int s = 0; s < g->n_stages; ++s) {
+    g->st[s].lag = sc.lag[s];
+    g->total += nb * g->st[s].n_tiles;
+  }
+  g->ln = ln;
+  g->ln_lag = ln ? sc.lag[g->n_stages] : 0;
+  if (ln) g->total += nb;
+  int last = g->ln_lag;
+  for (int s = 0; s < g->n_stages; ++s) last = sc.lag[s] > last ? sc.lag[s] : last;
+  g->n_steps = last + nb;
+  for (int s = 0; s < g->n_stages; ++s) {
+    const bool consumed = s + 1 < g->n_stages || ln;
+    if (!consumed) {
+      g->st[s].ring_q = 0;
+      continue;
+    }
+    const int next_lag = s + 1 < g->n_stages ? sc.lag[s + 1] : g->ln_lag;
+    int q = sc.ring[s];
+    if (q < next_lag - sc.lag[s] + 1) q = next_lag - sc.lag[s] + 1;
+    if (q > nb) q = nb;
+    g->st[s].ring_q = q;
+  }
+}
+
 }  // namespace
 
 // BERT-large FFN (bf16): hidden activations kept in fp16 (as the other bf16 chains), the second
@@ -246,6 +353,170 @@ int launch_dlrm_top_t(const LaunchCtx& c) {
       t.args.out = t.out;
       rc = launch_stream<Tail>(t);
     }
+  }
+  workspace_release(c.stream);
+  return rc;
+}
+
+// ------------------------------------------------------------------ single-kernel forms
+namespace {
+
+ChainStageArgs chain_stage(int n, int k, int act, int out_kind, int a_bf16, int out_bf16, int bias_off,
+                           const void* bias, int bias_bf16, const void* resid, int resid_bf16) {
+  ChainStageArgs st;
+  std::memset(&st, 0, sizeof(st));
+  st.n = n;
+  st.k = k;
+  st.n_tiles = n / GemmChainLayout::kBN;
+  st.act = act;
+  st.out_kind = out_kind;
+  st.a_bf16 = a_bf16;
+  st.out_bf16 = out_bf16;
+  st.bias_off = bias_off;
+  st.bias = bias;
+  st.bias_bf16 = bias_bf16;
+  st.resid = resid;
+  st.resid_bf16 = resid_bf16;
+  return st;
+}
+
+size_t ring_bytes(int q, int n, int elem) { return align256(size_t(q) * 256 * n * elem); }
+
+}  // namespace
+
+// BERT-large FFN as one kernel: layer 0 (1024 -> 4096, GELU) into an fp16 ring, layer 1 (4096 ->
+// 1024, + x) into an fp32 ring, LayerNorm tiles into out. W2 is used as an fp16 copy (the hidden
+// activations are fp16, as on the layer-by-layer path).
+int launch_bert_ffn_bf16_chain(const LaunchCtx& c) {
+  constexpr int H = 1024, F = 4096;
+  GemmChainArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.m = static_cast<int>(c.m);
+  g.n_blocks = static_cast<int>((c.m + 255) / 256);
+  g.n_stages = 2;
+  g.st[0] = chain_stage(F, H, kActGeluTanh, 0, 1, 0, 0, c.args.bias[0], 1, nullptr, 0);
+  g.st[1] = chain_stage(H, F, kActNone, 1, 0, 0, F, c.args.bias[1], 1, c.x, 1);
+  ChainSched sc;
+  // measured best of the schedules tried (0.342-0.345 ms at M = 16,384; shorter lags stall on
+  // dependencies, e.g. 0.44 ms at 8 / 20 with 16-block rings)
+  sc.lag[1] = 16;
+  sc.lag[2] = 40;
+  sc.ring[0] = 40;
+  sc.ring[1] = 40;
+  chain_sched_override(&sc, 2);
+  chain_schedule(&g, sc, 1);
+  const int nb = g.n_blocks;
+  const size_t w2_bytes = align256(size_t(F) * H * 2);
+  const size_t h_bytes = ring_bytes(g.st[0].ring_q, F, 2);
+  const size_t y_bytes = ring_bytes(g.st[1].ring_q, H, 4);
+  const size_t cnt_ints = size_t(3) * nb + 1;  // completion counters, then the claim counter
+  const size_t cnt_bytes = align256(cnt_ints * sizeof(int));
+  void* ws = nullptr;
+  int rc = workspace_acquire(w2_bytes + h_bytes + y_bytes + cnt_bytes, c.stream, &ws);
+  if (rc != GP_OK) return rc;
+  char* base = static_cast<char*>(ws);
+  void* w2h = base;
+  void* hring = base + w2_bytes;
+  void* yring = base + w2_bytes + h_bytes;
+  int* counters = reinterpret_cast<int*>(base + w2_bytes + h_bytes + y_bytes);
+  const int64_t nw = int64_t(F) * H;
+  bf16_to_f16_kernel<<<static_cast<int>((nw + 1023) / 1024), 256, 0, c.stream>>>(
+      static_cast<const __nv_bfloat16*>(c.w[1]), static_cast<__half*>(w2h), nw);
+  cudaError_t e = cudaMemsetAsync(counters, 0, cnt_ints * sizeof(int), c.stream);
+  if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "counter reset: %s", cudaGetErrorString(e));
+  GemmChainMaps tm;
+  std::memset(&tm, 0, sizeof(tm));
+  const uint64_t hq = uint64_t(g.st[0].ring_q) * 256, yq = uint64_t(g.st[1].ring_q) * 256;
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.a[0], c.x, GP_BF16, c.m, H, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], c.w[0], GP_BF16, H, F, kPanel, 2);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.out[0], hring, GP_F16, hq, F, 32, 32, 64);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.a[1], hring, GP_F16, hq, F, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[1], w2h, GP_F16, F, H, kPanel, 2);
+  if (rc == GP_OK) rc = make_tmap_2d_f32(&tm.out[1], yring, yq, H, 32, 32, 128);
+  if (rc == GP_OK) {
+    g.counters = counters;
+    g.next_tile = counters + cnt_ints - 1;
+    g.ln_n = H;
+    g.ln_ring = static_cast<const float*>(yring);
+    g.gamma = c.args.gamma;
+    g.beta = c.args.beta;
+    g.g_bf16 = 1;
+    g.ln_eps = c.args.ln_eps;
+    g.out = c.out;
+    g.out_bf16 = 1;
+    g.bias_total = F + H;
+    g.status = c.args.status;
+    g.timeout_ns = c.args.timeout_ns;
+    rc = chain_launch(c.stream, c.sm_count, tm, g);
+  }
+  workspace_release(c.stream);
+  return rc;
+}
+
+// DLRM top MLP as one kernel: three wide layers through fp16 rings, then 512 -> 256 (ReLU) with
+// the 256 -> 1 sigmoid head in its epilogue.
+int launch_dlrm_top_f16_chain(const LaunchCtx& c) {
+  const int k0 = c.spec->widths[0];
+  GemmChainArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.m = static_cast<int>(c.m);
+  g.n_blocks = static_cast<int>((c.m + 255) / 256);
+  g.n_stages = 4;
+  g.st[0] = chain_stage(1024, k0, kActRelu, 0, 0, 0, 0, c.args.bias[0], 0, nullptr, 0);
+  g.st[1] = chain_stage(1024, 1024, kActRelu, 0, 0, 0, 1024, c.args.bias[1], 0, nullptr, 0);
+  g.st[2] = chain_stage(512, 1024, kActRelu, 0, 0, 0, 2048, c.args.bias[2], 0, nullptr, 0);
+  g.st[3] = chain_stage(256, 512, kActRelu, 2, 0, 0, 2560, c.args.bias[3], 0, nullptr, 0);
+  ChainSched sc;
+  // measured best of the schedules tried (1.25 ms at M = 262,144; 6 / 20 / 32 with 24-block rings
+  // stalled on dependencies at 2.4 ms)
+  sc.lag[1] = 20;
+  sc.lag[2] = 60;
+  sc.lag[3] = 100;
+  sc.ring[0] = sc.ring[1] = sc.ring[2] = 120;
+  chain_sched_override(&sc, 3);
+  chain_schedule(&g, sc, 0);
+  const int nb = g.n_blocks;
+  const size_t r0 = ring_bytes(g.st[0].ring_q, 1024, 2), r1 = ring_bytes(g.st[1].ring_q, 1024, 2);
+  const size_t r2 = ring_bytes(g.st[2].ring_q, 512, 2);
+  const size_t cnt_ints = size_t(5) * nb + 1;  // completion counters, then the claim counter
+  const size_t cnt_bytes = align256(cnt_ints * sizeof(int));
+  void* ws = nullptr;
+  int rc = workspace_acquire(r0 + r1 + r2 + cnt_bytes, c.stream, &ws);
+  if (rc != GP_OK) return rc;
+  char* base = static_cast<char*>(ws);
+  void* h1 = base;
+  void* h2 = base + r0;
+  void* h3 = base + r0 + r1;
+  int* counters = reinterpret_cast<int*>(base + r0 + r1 + r2);
+  cudaError_t e = cudaMemsetAsync(counters, 0, cnt_ints * sizeof(int), c.stream);
+  if (e != cudaSuccess) rc = set_error(GP_ERR_CUDA, "counter reset: %s", cudaGetErrorString(e));
+  GemmChainMaps tm;
+  std::memset(&tm, 0, sizeof(tm));
+  const uint64_t q0 = uint64_t(g.st[0].ring_q) * 256, q1 = uint64_t(g.st[1].ring_q) * 256;
+  const uint64_t q2 = uint64_t(g.st[2].ring_q) * 256;
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.a[0], c.x, GP_F16, c.m, k0, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[0], c.w[0], GP_F16, k0, 1024, kPanel, 2);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.out[0], h1, GP_F16, q0, 1024, 32, 32, 64);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.a[1], h1, GP_F16, q0, 1024, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[1], c.w[1], GP_F16, 1024, 1024, kPanel, 2);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.out[1], h2, GP_F16, q1, 1024, 32, 32, 64);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.a[2], h2, GP_F16, q1, 1024, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[2], c.w[2], GP_F16, 1024, 512, kPanel, 2);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.out[2], h3, GP_F16, q2, 512, 32, 32, 64);
+  if (rc == GP_OK) rc = make_tmap_2d(&tm.a[3], h3, GP_F16, q2, 512, kPanel, kBM, 128);
+  if (rc == GP_OK) rc = make_tmap_w3d(&tm.w[3], c.w[3], GP_F16, 512, 256, kPanel, 2);
+  if (rc == GP_OK) {
+    tm.out[3] = tm.out[2];  // the head layer stores no rows through a map
+    g.counters = counters;
+    g.next_tile = counters + cnt_ints - 1;
+    g.out = c.out;
+    g.out_bf16 = 0;
+    g.head_w = c.w[4];
+    g.head_b = c.args.bias[4];
+    g.bias_total = 2816;
+    g.status = c.args.status;
+    g.timeout_ns = c.args.timeout_ns;
+    rc = chain_launch(c.stream, c.sm_count, tm, g);
   }
   workspace_release(c.stream);
   return rc;

@@ -94,9 +94,9 @@ def test_ffn_residual_ln_ping_pong(cuda_dev, variant):
     assert r["ok"], r
 
 
-def test_wide_gemm_chain_ping_pong(cuda_dev):
-    """BERT-large FFN, 1024 -> 4096 GELU -> 1024, + x, LayerNorm (GEMM kernel launches through the
-    workspace, then the row LayerNorm)."""
+def test_wide_gemm_chain_ping_pong(cuda_dev, variant):
+    """BERT-large FFN, 1024 -> 4096 GELU -> 1024, + x, LayerNorm (GEMM launches through the
+    workspace and the row LayerNorm; or the single-kernel chain)."""
     m = 1024
     ws, bs, ga, be, wd, bd, gad, bed = _params([1024, 4096, 1024], torch.bfloat16, cuda_dev, 31, scale=0.02)
     x0 = torch.randn(m, 1024, generator=torch.Generator().manual_seed(32)).to(torch.bfloat16)

@@ -1,14 +1,25 @@
 """GPU parity of the wide chains (BERT-large FFN with residual + LayerNorm, DLRM top MLP with the
 sigmoid head) against the CPU oracle, through the C ABI. Row counts cross the chunk boundaries the
-host uses (4,096 rows for BERT, 16,384 for DLRM top); full-size runs are checked on row samples."""
+host uses (4,096 rows for BERT, 16,384 for DLRM top) and, on the single-kernel form, wrap its
+rings of row blocks; full-size runs are checked on row samples."""
 import pytest
 import torch
 
+from gpu_pipes_b200 import _lib as L
 from gpu_pipes_b200 import cuda_ext
 from gpu_pipes_b200 import workloads as W
 from oracle import mlp_oracle as O
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True, params=[0, 1], ids=["default", "other"])
+def variant(request):
+    """Every case on both forms: layer by layer through the workspace, and the single-kernel
+    chain with its intermediates in L2-sized rings (tile sequence with completion counters)."""
+    L.set_kernel_variant(request.param)
+    yield request.param
+    L.set_kernel_variant(0)
 
 
 def _run(w, dev):
