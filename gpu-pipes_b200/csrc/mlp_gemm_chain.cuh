@@ -221,7 +221,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
   uint64_t* tid_full = bars + 24;   // [kT] a claimed position is in tid_val (this CTA's copy)
   uint64_t* tid_empty = bars + 28;  // [kT] (leader's) every reader has taken it
-  volatile int* tid_val = reinterpret_cast<volatile int*>(bars + 32);  // [kT]
+  volatile int* tid_val = reinterpret_cast<volatile int*>(bars + 32);   // [kT] claimed positions
+  volatile int* tid_pack = reinterpret_cast<volatile int*>(bars + 34);  // [kT] their tiles, packed
   float* bias_s = reinterpret_cast<float*>(smem + L::kOffBias);
   float* head_s = reinterpret_cast<float*>(smem + L::kOffHead);  // [kMaxHead] weights, then the bias
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -280,68 +281,85 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
   const int nb = args.n_blocks;
   auto counter = [&](int s, int r) { return args.counters + s * nb + r; };
-  // A reader's next claimed position (>= total: the sequence is done), or -1 if the wait gave up.
-  // Called by one thread per reader (lane 0 of the role), which then releases the slot.
-  auto take = [&](int& slot, uint32_t& tph, int code) -> int {
-    if (!mbar_wait<true>(smem_u32(&tid_full[slot]), tph, wctx, code)) return -1;
-    const int t = tid_val[slot];
+  // A claimed position and its tile: s | j << 3 | r << 8 (decoded once, by the claiming producer).
+  struct Claim {
+    int t;
+    ChainTile tl;
+  };
+  auto unpack = [&](int t, int pk) -> Claim {
+    return Claim{t, ChainTile{pk & 7, pk >> 8, (pk >> 3) & 31}};
+  };
+  // A reader's next claim (t >= total: the sequence is done; t < 0: the wait gave up). Called by
+  // one thread per reader (lane 0 of the role), which then releases the slot.
+  auto take = [&](int& slot, uint32_t& tph, int code) -> Claim {
+    if (!mbar_wait<true>(smem_u32(&tid_full[slot]), tph, wctx, code)) return Claim{-1, ChainTile{0, -1, 0}};
+    const Claim c = unpack(tid_val[slot], tid_pack[slot]);
     mbar_arrive_cluster(leader_bar(&tid_empty[slot]));
     if (++slot == kT) { slot = 0; tph ^= 1; }
-    return t;
+    return c;
   };
-  // Moves the cursor from position `prev` to `t` and decodes the tile there (r < 0: no tile).
-  auto locate = [&](ChainCursor& cur, int& prev, int t) -> ChainTile {
-    cur.advance(args, t - prev);
-    prev = t;
-    ChainTile tl = chain_decode(args, cur);
-    if (tl.r < 0 || tl.r >= nb || cur.step >= args.n_steps) {
-      atomicCAS(args.status, 0, kDevBadSchedule);
-      *abort_flag = 1;
-      tl.r = -1;
-    }
-    return tl;
-  };
+  // read after write: all tiles of the previous layer for this row block have stored
+  auto raw_target = [&](const ChainTile& tl) { return args.st[tl.s - 1].n_tiles * kSignals; };
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (+ claims)
+    // The leader claims positions (one ahead, so the claim's round trip overlaps the loads),
+    // decodes them and publishes position and tile to both CTAs; the other CTA's producer reads
+    // them. The next tile is fetched and its dependency tested a few stages before the current
+    // tile's last load, so the next loads follow without a gap when the dependency is met.
     if (lane == 0) {
       const uint64_t keep = l2_policy_evict_last();
       int s = 0, slot = 0, prev = 0;
       uint32_t ph = 0, tph = 0;
       ChainCursor cur;
-#pragma unroll 1
-      // the leader claims one position ahead: the claim's round trip overlaps the current tile's loads
       int claimed = leader ? atomicAdd(args.next_tile, 1) : 0;
-      while (true) {
-        int t;
-        if (leader) {
-          // publish the claimed position to both CTAs
-          if (!mbar_wait<true>(smem_u32(&tid_empty[slot]), tph ^ 1, wctx, kDevTimeoutProducer)) break;
-          t = claimed;
-          tid_val[slot] = t;
-          st_shared_cluster_u32(mapa_shared(smem_u32(const_cast<int*>(&tid_val[slot])), 1), static_cast<uint32_t>(t));
-          mbar_arrive(smem_u32(&tid_full[slot]));
-          mbar_arrive_cluster(mapa_shared(smem_u32(&tid_full[slot]), 1));
-          if (++slot == kT) { slot = 0; tph ^= 1; }
-          if (t < args.total) claimed = atomicAdd(args.next_tile, 1);
-        } else {
-          t = take(slot, tph, kDevTimeoutProducer);
+      auto fetch = [&]() -> Claim {
+        if (!leader) return take(slot, tph, kDevTimeoutProducer);
+        if (!mbar_wait<true>(smem_u32(&tid_empty[slot]), tph ^ 1, wctx, kDevTimeoutProducer))
+          return Claim{-1, ChainTile{0, -1, 0}};
+        Claim c{claimed, ChainTile{0, 0, 0}};
+        if (c.t < args.total) {
+          claimed = atomicAdd(args.next_tile, 1);
+          cur.advance(args, c.t - prev);
+          prev = c.t;
+          c.tl = chain_decode(args, cur);
+          if (c.tl.r < 0 || c.tl.r >= nb || cur.step >= args.n_steps) {
+            atomicCAS(args.status, 0, kDevBadSchedule);
+            *abort_flag = 1;
+            c.t = -1;  // published as "gave up": every reader stops
+          }
         }
-        if (t < 0 || t >= args.total) break;
-        const ChainTile tl = locate(cur, prev, t);
-        if (tl.r < 0) break;
-        if (tl.s >= args.n_stages) continue;  // LayerNorm tile: no operands
+        const int pk = c.tl.s | (c.tl.j << 3) | (c.tl.r << 8);
+        tid_val[slot] = c.t;
+        tid_pack[slot] = pk;
+        st_shared_cluster_u32(mapa_shared(smem_u32(const_cast<int*>(&tid_val[slot])), 1), static_cast<uint32_t>(c.t));
+        st_shared_cluster_u32(mapa_shared(smem_u32(const_cast<int*>(&tid_pack[slot])), 1), static_cast<uint32_t>(pk));
+        mbar_arrive(smem_u32(&tid_full[slot]));
+        mbar_arrive_cluster(mapa_shared(smem_u32(&tid_full[slot]), 1));
+        if (++slot == kT) { slot = 0; tph ^= 1; }
+        return c;
+      };
+      Claim cur_c = fetch();
+      bool ready = false;  // cur_c's dependency was already seen complete
+#pragma unroll 1
+      while (cur_c.t >= 0 && cur_c.t < args.total) {
+        const ChainTile tl = cur_c.tl;
+        if (tl.s >= args.n_stages) {  // LayerNorm tile: no operands
+          cur_c = fetch();
+          ready = false;
+          continue;
+        }
         const ChainStageArgs& st = args.st[tl.s];
         int arow = tl.r * 256 + static_cast<int>(rank) * kBM;
         if (tl.s > 0) {
-          // read after write: every tile of the previous layer for this row block has stored
-          const ChainStageArgs& pv = args.st[tl.s - 1];
-          if (!wait_counter(counter(tl.s - 1, tl.r), pv.n_tiles * kSignals, wctx, kDevTimeoutDependency)) break;
+          if (!ready && !wait_counter(counter(tl.s - 1, tl.r), raw_target(tl), wctx, kDevTimeoutDependency)) break;
           fence_proxy_async_global();
-          arow = (tl.r % pv.ring_q) * 256 + static_cast<int>(rank) * kBM;
+          arow = (tl.r % args.st[tl.s - 1].ring_q) * 256 + static_cast<int>(rank) * kBM;
         }
         const int bblk = tl.j * (L::kBN / 64) + static_cast<int>(rank) * (L::kBN / 128);
         const int kpanels = (st.k + kPanel - 1) / kPanel;
+        const int kp_fetch = kpanels > 3 ? kpanels - 3 : 0;
+        Claim next{-1, ChainTile{0, -1, 0}};
         bool ok = true;
 #pragma unroll 1
         for (int kp = 0; kp < kpanels; ++kp) {
@@ -352,23 +370,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
           tma_load_2d_pair(stg, &tm.a[tl.s], fb, kp * kPanel, arow, keep);
           tma_load_3d_pair(stg + L::kABytes, &tm.w[tl.s], fb, 0, kp * kPanel, bblk, keep);
           if (++s == kS) { s = 0; ph ^= 1; }
+          if (kp == kp_fetch) {
+            next = fetch();
+            ready = false;
+            if (next.t >= 0 && next.t < args.total && next.tl.s > 0 && next.tl.s < args.n_stages)
+              ready = ld_acquire_gpu(counter(next.tl.s - 1, next.tl.r)) >= raw_target(next.tl);
+          }
         }
         if (!ok) break;
+        cur_c = next;
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (pair leader)
     if (lane == 0 && leader) {
-      int s = 0, g = 0, slot = 0, prev = 0;
+      int s = 0, g = 0, slot = 0;
       uint32_t ph = 0, tph = 0, eph[2] = {0, 0};
-      ChainCursor cur;
 #pragma unroll 1
       while (true) {
-        const int t = take(slot, tph, kDevTimeoutMma);
-        if (t < 0 || t >= args.total) break;
-        const ChainTile tl = locate(cur, prev, t);
-        if (tl.r < 0) break;
+        const Claim c = take(slot, tph, kDevTimeoutMma);
+        if (c.t < 0 || c.t >= args.total) break;
+        const ChainTile tl = c.tl;
         if (tl.s >= args.n_stages) continue;
         const ChainStageArgs& st = args.st[tl.s];
         const int b = g & 1;
@@ -414,9 +437,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     const int eg = (warp - 2) >> 2;    // even / odd 32-column chunks
     const int ew = warp - 2;           // epilogue warp 0..7
     uint8_t* stg = smem + L::kOffStg + ew * L::kStgWarpBytes;
-    int sb = 0, g = 0, slot = 0, prev = 0;
+    int sb = 0, g = 0, slot = 0;
     uint32_t aph[2] = {0, 0}, tph = 0;
-    ChainCursor cur;
     // Completion of a tile's TMA stores is signalled one tile late (after the next tile's stores are
     // issued), so the warp does not sit out the store latency; a pending signal is flushed before
     // any wait that might depend on it.
@@ -433,12 +455,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     };
 #pragma unroll 1
     while (true) {
-      int t = 0;
-      if (lane == 0) t = take(slot, tph, kDevTimeoutEpilogue);
-      t = __shfl_sync(0xffffffffu, t, 0);
+      Claim c{0, ChainTile{0, 0, 0}};
+      if (lane == 0) c = take(slot, tph, kDevTimeoutEpilogue);
+      const int t = __shfl_sync(0xffffffffu, c.t, 0);
       if (t < 0 || t >= args.total) break;
-      const ChainTile tl = locate(cur, prev, t);
-      if (tl.r < 0) break;
+      const ChainTile tl{__shfl_sync(0xffffffffu, c.tl.s, 0), __shfl_sync(0xffffffffu, c.tl.r, 0),
+                         __shfl_sync(0xffffffffu, c.tl.j, 0)};
       if (tl.s >= args.n_stages) {
         // LayerNorm tile: this CTA's 128 rows of the row block, one warp per row
         const ChainStageArgs& lst = args.st[args.n_stages - 1];
