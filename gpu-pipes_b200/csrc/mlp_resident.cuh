@@ -258,9 +258,9 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   }
 
   // All weights, once: this CTA's NC columns of every layer, completing on the (leader's) w_full.
-  // The leader issues its loads as soon as its barriers exist, so they overlap the rest of the
-  // set-up (bias and LayerNorm staging: about 2 us of global-load latency); a pair's second CTA
-  // issues its own once the cluster has synchronised, since they complete on the leader's barrier.
+  // Issued as soon as the barriers exist (a pair's after its first cluster sync, since both CTAs'
+  // loads complete on the leader's barrier), so they overlap the rest of the set-up (bias and
+  // LayerNorm staging: about 2 us of global-load latency).
   auto load_weights = [&]() {
     const uint64_t keep = l2_policy_evict_last();
     if (leader) mbar_arrive_expect_tx(smem_u32(w_full), L::kWBytes * CG);
@@ -304,9 +304,9 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
       tma_load_2d_hint(dst, xm, smem_u32(&x_full[s]), xc, row, stream);
     }
   };
-  // single CTA: the first ring's worth of x panels goes out with the weights, before the set-up
-  // below (a pair's loads complete on the leader's barriers, so they wait for the cluster sync)
-  const int kXPre = (!kPair && XM != 1) ? (x_total < kXS ? x_total : kXS) : 0;
+  // the first ring's worth of x panels goes out with the weights, before the set-up below (each
+  // CTA of a pair its own half, after the first cluster sync)
+  const int kXPre = XM != 1 ? (x_total < kXS ? x_total : kXS) : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kXS; ++s) {
@@ -327,13 +327,17 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     prefetch_tmap(&tm.x);
     prefetch_tmap(&tm.out);
   }
+  // a pair's barriers are initialised in both CTAs before either issues loads that complete on
+  // the leader's (a cluster barrier touches no global memory, so this also overlaps the previous
+  // kernel)
+  if constexpr (kPair) cluster_sync_all();
   // Everything above overlaps the previous kernel of the stream. Global memory is touched only
   // after griddepcontrol.wait, except the reads that the launch marked safe (pdl_early: weights,
   // biases and LayerNorm parameters; x), which go out first.
   const int early = args.pdl_early;
   if ((early & 1) == 0) pdl_wait_prior();
   if (threadIdx.x == 0) {
-    if (leader) load_weights();
+    load_weights();
     if (early & 2)
       for (int g = 0; g < kXPre; ++g) load_x(g);
   }
@@ -408,7 +412,6 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
     // nodes[dst] panels (4, 5). Lane l fetches rows 4l..4l+3 of a gathered panel with one
     // tile::gather4 request; both CTAs' requests complete on the leader's x_full.
     const bool src_warp = warp == 0;
-    if (src_warp && lane == 0 && !leader) load_weights();
     const uint64_t stream = l2_policy_evict_first();
     const uint64_t keep_nodes = l2_policy_evict_last();
     const int64_t* gidx = args.gidx[src_warp ? 0 : 1];
@@ -464,8 +467,7 @@ __device__ __forceinline__ void mlp_resident_body(const TensorMaps& tm, const Ch
   } else if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      if (!leader) load_weights();
-      // the x ring in panel order; the single-CTA form issued the first kXS loads at set-up
+      // the x ring in panel order; the first kXS loads went out at set-up
 #pragma unroll 1
       for (int g = kXPre; g < x_total; ++g) {
         const int s = g % kXS;
