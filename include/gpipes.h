@@ -260,7 +260,12 @@ GP_API int gp_fused_mlp_host(const gp_mlp_spec* spec, int64_t m, const void* x_h
 GP_API const char* gp_last_error(void);
 
 /* Synchronise `device` and read its status word (0 = ok, else a device-side code); with
- * clear != 0 reset it to 0. Returns GP_OK or GP_ERR_CUDA. */
+ * clear != 0 reset it to 0. Returns GP_OK or GP_ERR_CUDA. Codes (the first one raised is kept):
+ *   0x1xx-0x3xx a bounded wait ran out (producer, MMA issuer, epilogue), 0x400 weights never
+ *   arrived, 0x500 dynamic shared memory misaligned, 0x600 a gather/scatter index outside
+ *   [0, n_nodes) (that row read as zeros), 0x700 a wait on another tile's completion counter
+ *   ran out (single-kernel wide chains), 0x800 a tile outside the chain's schedule (no memory
+ *   touched). */
 GP_API int gp_device_status(int device, int clear, int* status_out);
 
 /* Budget of every device-side wait, in nanoseconds (default 2e9). 0 restores the default. */
@@ -271,8 +276,10 @@ GP_API int gp_set_timeout_ns(uint64_t ns);
 GP_API int gp_set_fault_injection(int mode);
 
 /* Kernel choice where several are compiled for one chain: 0 = default, 1 = the other form
- * (the MeshGraphNet family has a single-CTA and a CTA-pair kernel; the default is the faster
- * one measured for that input width). Process-wide; for A/B measurement and tests. The
+ * (the MeshGraphNet family has a single-CTA and a CTA-pair kernel, the default being the faster
+ * one measured for that input width; chains with one wide first layer have a TMEM-activation and
+ * a weight-streaming kernel; BERT-large FFN and DLRM top run layer by layer, or as one kernel with
+ * their intermediates in rings of row blocks). Process-wide; for A/B measurement and tests. The
  * environment variable GP_KERNEL_VARIANT sets the initial value. No reference counterpart. */
 GP_API int gp_set_kernel_variant(int variant);
 
