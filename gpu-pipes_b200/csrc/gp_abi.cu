@@ -439,9 +439,16 @@ int fused_mlp_host(const gp_mlp_spec* spec, int64_t m, const void* x_host, const
   if (spec->n_layers < 1 || spec->n_layers > GP_MAX_LAYERS) return set_error(GP_ERR_ARG, "n_layers = %d", spec->n_layers);
   const size_t xrow = static_cast<size_t>(spec->widths[0]) * 2;
   const size_t orow = static_cast<size_t>(spec->widths[spec->n_layers]) * 2;
-  if (chunk_rows <= 0) {  // about eight chunks, at least 65,536 rows each, whole tiles
+  if (chunk_rows <= 0) {
+    // about 16 MB of rows (x + out) per chunk and at least eight chunks, so the first upload and
+    // the last download, which nothing overlaps, stay short; at least 4,096 rows, below which
+    // the per-chunk launch and copy costs dominate. Measured end to end (MGN node, 1,048,576
+    // rows: 9.7e7 rows/s with 131,072-row chunks, 1.02e8 with 32,768; MGN edge, 65,536 rows in
+    // one chunk: 4.8e7, in 8,192-row chunks 6.4e7).
+    const int64_t by_bytes = static_cast<int64_t>((size_t(16) << 20) / (xrow + orow));
     chunk_rows = (m + 7) / 8;
-    if (chunk_rows < 65536) chunk_rows = 65536;
+    if (chunk_rows > by_bytes) chunk_rows = by_bytes;
+    if (chunk_rows < 4096) chunk_rows = 4096;
   }
   chunk_rows = (chunk_rows + 255) / 256 * 256;
   if (chunk_rows > m) chunk_rows = m;
