@@ -243,8 +243,8 @@ GP_API int gp_gc_edges_bf16_noalloc_out(int64_t m, int act, const void* x,
 
 /* gp_fused_mlp_out on HOST buffers: x_host [m, widths[0]] in, out_host [m, widths[n_layers]] out
  * (16-bit; pinned memory for overlap, pageable works but copies synchronously). The rows go in
- * chunks of chunk_rows (0: about 16 MB of rows, at least 8 chunks and 4,096 rows) through double-buffered device staging:
- * the H2D copy of chunk i+1 and the D2H copy of chunk i-1 run on two library streams while chunk
+ * chunks of chunk_rows (0: about 16 MB of rows, at least 8 chunks and 4,096 rows) through
+ * double-buffered device staging: the H2D copy of chunk i+1 and the D2H copy of chunk i-1 run on two library streams while chunk
  * i computes on `stream`, so a call costs about the larger of the two PCIe directions instead of
  * their sum. Weights, biases, gamma and beta are device pointers as for gp_fused_mlp_out. Returns
  * after enqueueing; `stream` waits for the last D2H copy, so synchronising `stream` makes
