@@ -152,6 +152,10 @@ unsigned long long g_pdl_clock = 0;
 
 PdlLaunch::PdlLaunch(cudaStream_t stream) {
   g_pdl_mu.lock();
+  // the legacy handle and NULL name the same stream; the per-thread handle names a different
+  // stream in every host thread, so launches on it are not tracked (no early reads)
+  if (stream == cudaStreamLegacy) stream = nullptr;
+  untracked_ = stream == cudaStreamPerThread;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
   // this stream's slot, else the least recently used one (a stream whose record was dropped
@@ -176,7 +180,7 @@ PdlLaunch::~PdlLaunch() { g_pdl_mu.unlock(); }
 
 int PdlLaunch::early_flags(const PdlIo& io) const {
   const PdlRecord& r = g_pdl[slot_];
-  if (g_pdl_mode != 1 || r.unknown || io.overflow) return 0;
+  if (g_pdl_mode != 1 || untracked_ || r.unknown || io.overflow) return 0;
   int flags = 3;
   for (int i = 0; i < io.n; ++i) {
     if (io.kind[i] == PdlIo::kWrite) continue;

@@ -155,6 +155,7 @@ class PdlLaunch {
 
  private:
   int slot_;
+  bool untracked_;
 };
 
 }  // namespace gp
