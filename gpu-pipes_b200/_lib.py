@@ -65,6 +65,7 @@ EXPORTED_SYMBOLS = (
     "gp_set_timeout_ns",
     "gp_set_fault_injection",
     "gp_launch_count",
+    "gp_debug_pdl_flags",
     "gp_set_kernel_variant",
 )
 
@@ -147,6 +148,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.gp_set_kernel_variant.restype = _INT
     lib.gp_launch_count.argtypes = []
     lib.gp_launch_count.restype = ctypes.c_uint64
+    lib.gp_debug_pdl_flags.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                                       ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_int),
+                                       ctypes.c_int]
+    lib.gp_debug_pdl_flags.restype = ctypes.c_int
 
 
 def lib() -> ctypes.CDLL:
@@ -209,3 +214,13 @@ def set_kernel_variant(v: int) -> None:
 
 def launch_count() -> int:
     return int(lib().gp_launch_count())
+
+
+def pdl_flags(stream: int, ranges, record: bool = True) -> int:
+    """gp_debug_pdl_flags: ranges are (address, bytes, kind) with kind 0 parameter, 1 input rows,
+    2 written, 3 writes not listed. Returns the early-read bits (negative on error)."""
+    n = len(ranges)
+    ptrs = (ctypes.c_void_p * max(n, 1))(*[r[0] for r in ranges])
+    sizes = (ctypes.c_uint64 * max(n, 1))(*[r[1] for r in ranges])
+    kinds = (ctypes.c_int * max(n, 1))(*[r[2] for r in ranges])
+    return int(lib().gp_debug_pdl_flags(ctypes.c_void_p(stream), n, ptrs, sizes, kinds, int(record)))

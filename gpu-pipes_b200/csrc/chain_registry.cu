@@ -202,6 +202,22 @@ void PdlLaunch::record(const PdlIo& io) {
     }
 }
 
+int pdl_probe(cudaStream_t stream, int n, const void* const* ptrs, const uint64_t* bytes, const int* kinds,
+              bool record) {
+  PdlIo io;
+  for (int i = 0; i < n; ++i) {
+    if (kinds[i] == 3) {
+      io.writes_unknown = true;
+      continue;
+    }
+    io.add(static_cast<PdlIo::Kind>(kinds[i]), ptrs[i], bytes[i]);
+  }
+  PdlLaunch pdl(stream);
+  const int flags = pdl.early_flags(io);
+  if (record) pdl.record(io);
+  return flags;
+}
+
 static int wanted_variant() { return g_variant.load(std::memory_order_relaxed); }
 
 void set_kernel_variant(int v) { g_variant.store(v); }

@@ -87,6 +87,11 @@ void count_launches(int n);
 // when `clear` is set. The caller synchronises the device first.
 int noalloc_status(bool clear, int* status);
 
+// The early-read decision and record update of one launch, without launching (diagnostics):
+// kinds 0 parameter, 1 x, 2 written, 3 writes not listed. Returns the pdl_early bits.
+int pdl_probe(cudaStream_t stream, int n, const void* const* ptrs, const uint64_t* bytes, const int* kinds,
+              bool record);
+
 // Sets the dynamic shared memory attribute of `kern` once per device.
 int ensure_smem_attr(const void* kern, int bytes, unsigned long long* done_mask);
 

@@ -891,6 +891,16 @@ int gp_set_fault_injection(int mode) {
 
 uint64_t gp_launch_count(void) { return g_launches.load(); }
 
+int gp_debug_pdl_flags(void* stream, int n, const void* const* ptrs, const uint64_t* bytes, const int* kinds,
+                       int record) {
+  clear_error();
+  if (n < 0 || (n > 0 && (ptrs == nullptr || bytes == nullptr || kinds == nullptr)))
+    return set_error(GP_ERR_ARG, "range arrays missing");
+  for (int i = 0; i < n; ++i)
+    if (kinds[i] < 0 || kinds[i] > 3) return set_error(GP_ERR_ARG, "range kind %d unknown", kinds[i]);
+  return pdl_probe(static_cast<cudaStream_t>(stream), n, ptrs, bytes, kinds, record != 0);
+}
+
 int gp_set_kernel_variant(int variant) {
   if (variant < 0 || variant > 1) return set_error(GP_ERR_ARG, "kernel variant %d unknown", variant);
   set_kernel_variant(variant);

@@ -286,6 +286,16 @@ GP_API int gp_set_kernel_variant(int variant);
 /* Number of kernels this library has launched in this process (for launch-count claims). */
 GP_API uint64_t gp_launch_count(void);
 
+/* The launch-overlap bookkeeping of one launch on `stream`, without launching (diagnostics and
+ * tests). Ranges: kinds 0 = weights / per-column parameters, 1 = input rows, 2 = written,
+ * 3 = writes not listed (ptr and bytes ignored). Returns the early-read bits such a launch would
+ * get (1: parameters, 2: input rows may be read before the previous kernel completes; 0 when
+ * they overlap what the stream's last chain launch writes, when the stream has no record, or with
+ * GP_PDL=0 / 2), or a negative GP_ERR_*; with record != 0 the ranges' writes become the stream's
+ * record, as a real launch's would. No reference counterpart. */
+GP_API int gp_debug_pdl_flags(void* stream, int n, const void* const* ptrs, const uint64_t* bytes,
+                              const int* kinds, int record);
+
 #ifdef __cplusplus
 }
 #endif
