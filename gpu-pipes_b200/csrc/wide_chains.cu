@@ -14,7 +14,6 @@
 // mlp_gemm_chain_kernel launch with its intermediates in rings of row blocks (mlp_gemm_chain.cuh);
 // measured slower, see the schedules below.
 #include <atomic>
-#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 
@@ -151,8 +150,9 @@ struct ChainDlrmTailRef {
 // ------------------------------------------------------------------ single-kernel chains
 // Schedule of a fused chain: step lag of each layer (layer 0 at 0) and of the LayerNorm tiles, and
 // the depth (row blocks) of each layer's output ring. GP_CHAIN_SCHED="l1,l2,...;q" overrides the
-// lags of layers 1.. (and the LayerNorm tile, last) and sets every ring depth (measurement only);
-// depths are raised to what keeps every dependency pointing backwards in the tile sequence.
+// lags of layers 1.. (and the LayerNorm tile, last; non-decreasing) and sets every ring depth
+// (measurement only); depths are raised to what keeps every dependency pointing backwards in the
+// tile sequence.
 struct ChainSched {
   int lag[kChainMaxStages + 1] = {0};
   int ring[kChainMaxStages] = {0};
@@ -170,6 +170,10 @@ void chain_sched_override(ChainSched* sc, int n_lags) {
     if (*p == ',') ++p;
   }
   if (*p == ';') q = std::atoi(p + 1);
+  // lags must not decrease (a layer's tiles of a row block come after the previous layer's in
+  // the sequence, the LayerNorm tile after the last layer's); otherwise the override is ignored
+  for (int i = 0; i < n; ++i)
+    if (v[i] < (i == 0 ? 0 : v[i - 1])) return;
   for (int i = 0; i < n; ++i) sc->lag[i + 1] = v[i];
   if (q > 0)
     for (int s = 0; s < kChainMaxStages; ++s) sc->ring[s] = q;
@@ -207,7 +211,7 @@ int chain_launch(cudaStream_t s, int sm_count, const GemmChainMaps& tm, const Ge
     mc = n;
     mc_slot.store(n, std::memory_order_relaxed);
   }
-  // every pair must be resident at once (tiles wait on other pairs' tiles)
+  // at most the co-resident clusters; a pair that is not resident claims no tile, so no tile waits on it
   const int clusters = g.total < mc ? g.total : mc;
   {
     PdlLaunch pdl(s);
