@@ -902,7 +902,7 @@ int gp_debug_pdl_flags(void* stream, int n, const void* const* ptrs, const uint6
 }
 
 int gp_set_kernel_variant(int variant) {
-  if (variant < 0 || variant > 1) return set_error(GP_ERR_ARG, "kernel variant %d unknown", variant);
+  if (variant < 0 || variant > 2) return set_error(GP_ERR_ARG, "kernel variant %d unknown", variant);
   set_kernel_variant(variant);
   return GP_OK;
 }

@@ -275,12 +275,14 @@ GP_API int gp_set_timeout_ns(uint64_t ns);
  * bounded waits run out (no GPU fault; the kernel exits with a timeout status). 0 = off. */
 GP_API int gp_set_fault_injection(int mode);
 
-/* Kernel choice where several are compiled for one chain: 0 = default, 1 = the other form
- * (the MeshGraphNet family has a single-CTA and a CTA-pair kernel, the default being the faster
- * one measured for that input width; chains with one wide first layer have a TMEM-activation and
- * a weight-streaming kernel; BERT-large FFN and DLRM top run layer by layer, or as one kernel with
- * their intermediates in rings of row blocks). Process-wide; for A/B measurement and tests. The
- * environment variable GP_KERNEL_VARIANT sets the initial value. No reference counterpart. */
+/* Kernel choice where several are compiled for one chain: 0 = default, 1 = the other form,
+ * 2 = a third form where one exists (a chain without the requested form runs its default).
+ * The MeshGraphNet family has a single-CTA and a CTA-pair kernel (the default is the faster one
+ * measured for that input width). Chains with one wide first layer have a TMEM-activation kernel
+ * (0), the weight-streaming kernel (1) and a CTA-pair TMEM kernel (2). BERT-large FFN and DLRM top
+ * run layer by layer (0) or as one kernel with their intermediates in rings of row blocks (1).
+ * Process-wide; for A/B measurement and tests. The environment variable GP_KERNEL_VARIANT sets the
+ * initial value. No reference counterpart. */
 GP_API int gp_set_kernel_variant(int variant);
 
 /* Number of kernels this library has launched in this process (for launch-count claims). */

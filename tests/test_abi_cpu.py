@@ -202,3 +202,16 @@ def test_dlrm_entry_points_reject_uncompiled_widths():
                                   None, _fake(0x32000), None, _fake(0x20000), None) == L.GP_ERR_UNSUPPORTED
     assert lib.gp_dlrm_topmlp_out(256, 512, 1, _fake(0x10000), w, None, _fake(0x20000), None) == L.GP_ERR_UNSUPPORTED
     assert lib.gp_dlrm_topmlp_out(256, 480, 64, _fake(0x10000), w, None, _fake(0x20000), None) == L.GP_ERR_UNSUPPORTED
+
+
+def test_kernel_variant_range():
+    """Forms 0-2 are selectable (a chain without the requested form runs its default); others are
+    rejected."""
+    lib = L.lib()
+    try:
+        for v in (0, 1, 2):
+            assert lib.gp_set_kernel_variant(v) == L.GP_OK
+        assert lib.gp_set_kernel_variant(3) == L.GP_ERR_ARG
+        assert lib.gp_set_kernel_variant(-1) == L.GP_ERR_ARG
+    finally:
+        lib.gp_set_kernel_variant(0)
