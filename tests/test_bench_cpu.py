@@ -1,0 +1,45 @@
+"""bench.py's reference arm on the CPU: one JSON line with the contract's keys, and under
+torchrun (2 ranks) exactly one line, from rank 0, with every rank exiting 0."""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _line(out: str) -> dict:
+    lines = [ln for ln in out.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out
+    return json.loads(lines[0])
+
+
+def _check_reference_line(d: dict, n_gpus: int) -> None:
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["impl"] == "reference"
+    assert d["n_gpus"] == n_gpus and d["value"] > 0 and d["unit"] == "rows/s"
+    assert d["higher_is_better"] is True
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["cores"] >= 1 and cb["kind"] in ("port", "reference") and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"]
+
+
+def test_reference_arm_one_process():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "test_mlp", "--m", "4096",
+                        "--steps", "1", "--warmup", "1"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    _check_reference_line(_line(r.stdout), 1)
+
+
+def test_reference_arm_two_ranks():
+    env = dict(os.environ, OMP_NUM_THREADS="4")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29741", "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--config", "bert_addln", "--steps", "1", "--warmup", "1"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    _check_reference_line(_line(r.stdout), 2)
