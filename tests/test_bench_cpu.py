@@ -2,6 +2,7 @@
 torchrun (2 ranks) exactly one line, from rank 0, with every rank exiting 0."""
 import json
 import os
+import socket
 import subprocess
 import sys
 from pathlib import Path
@@ -35,10 +36,16 @@ def test_reference_arm_one_process():
     _check_reference_line(_line(r.stdout), 1)
 
 
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def test_reference_arm_two_ranks():
     env = dict(os.environ, OMP_NUM_THREADS="4")
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-                        "--master-addr", "127.0.0.1", "--master-port", "29741", "bench.py", "--impl", "reference",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), "bench.py", "--impl", "reference",
                         "--gpus", "2", "--config", "bert_addln", "--steps", "1", "--warmup", "1"],
                        cwd=ROOT, capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stderr[-2000:]
