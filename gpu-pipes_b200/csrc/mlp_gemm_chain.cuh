@@ -80,6 +80,7 @@ struct GemmChainArgs {
   int bias_total;  // staged bias floats (sum of the layers' n)
   int* status;
   unsigned long long timeout_ns;
+  int inject;  // fault injection 1: completion signals are dropped, so dependency waits run out
 };
 
 struct GemmChainMaps {
@@ -281,6 +282,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   const WaitCtx wctx{args.status, abort_flag, args.timeout_ns};
   const int nb = args.n_blocks;
   auto counter = [&](int s, int r) { return args.counters + s * nb + r; };
+  auto signal = [&](int* c, int v) {
+    if (args.inject != 1) red_release_gpu_add(c, v);
+  };
   // A claimed position and its tile: s | j << 3 | r << 8 (decoded once, by the claiming producer).
   struct Claim {
     int t;
@@ -448,7 +452,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       if (lane == 0) {
         bulk_wait_group<0>();
         fence_proxy_async_global();
-        red_release_gpu_add(counter(pend_s, pend_r), 1);
+        signal(counter(pend_s, pend_r), 1);
       }
       __syncwarp();
       pend_s = -1;
@@ -482,7 +486,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         __syncwarp();
         if (lane == 0) {
           __threadfence();
-          red_release_gpu_add(counter(args.n_stages, tl.r), 1);
+          signal(counter(args.n_stages, tl.r), 1);
         }
         continue;
       }
@@ -611,14 +615,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         flush();
         __threadfence();
         __syncwarp();
-        if (lane == 0) red_release_gpu_add(counter(tl.s, tl.r), 1);
+        if (lane == 0) signal(counter(tl.s, tl.r), 1);
       } else {
         // the previous tile's stores are the groups before this tile's four
         if (pend_s >= 0) {
           if (lane == 0) {
             bulk_wait_group<L::kBN / 64>();
             fence_proxy_async_global();
-            red_release_gpu_add(counter(pend_s, pend_r), 1);
+            signal(counter(pend_s, pend_r), 1);
           }
           __syncwarp();
         }

@@ -451,6 +451,7 @@ int launch_bert_ffn_bf16_chain(const LaunchCtx& c) {
     g.bias_total = F + H;
     g.status = c.args.status;
     g.timeout_ns = c.args.timeout_ns;
+    g.inject = c.args.inject;
     rc = chain_launch(c.stream, c.sm_count, tm, g);
   }
   workspace_release(c.stream);
@@ -520,6 +521,7 @@ int launch_dlrm_top_f16_chain(const LaunchCtx& c) {
     g.bias_total = 2816;
     g.status = c.args.status;
     g.timeout_ns = c.args.timeout_ns;
+    g.inject = c.args.inject;
     rc = chain_launch(c.stream, c.sm_count, tm, g);
   }
   workspace_release(c.stream);

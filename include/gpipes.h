@@ -271,7 +271,8 @@ GP_API int gp_device_status(int device, int clear, int* status_out);
 /* Budget of every device-side wait, in nanoseconds (default 2e9). 0 restores the default. */
 GP_API int gp_set_timeout_ns(uint64_t ns);
 
-/* Fault injection for tests: mode 1 makes the producer skip every input load so the consumers'
+/* Fault injection for tests: mode 1 makes the producer skip every input load (the single-kernel
+ * wide chains: drops the completion signals between tiles) so the consumers'
  * bounded waits run out (no GPU fault; the kernel exits with a timeout status). 0 = off. */
 GP_API int gp_set_fault_injection(int mode);
 

@@ -100,3 +100,32 @@ def test_bert_ffn_gamma_beta_4_byte_aligned(cuda_dev):
                               (g_off, b_off), out2)
     torch.cuda.synchronize()
     assert torch.equal(out, out2)
+
+
+def test_chain_dependency_timeout_is_reported(cuda_dev, variant):
+    """Single-kernel form only. Host-side fault injection drops every completion signal, so the
+    later layers' dependency waits run out after 5 ms. The kernel exits cleanly, the status word
+    reports it, and the next call on the same context is correct."""
+    if variant != 1:
+        pytest.skip("the single-kernel form only")
+    w = W.DLRM_TOP.with_m(3000)
+    x, layers, ln, _ = _run(w, cuda_dev)
+    xd = x.to(cuda_dev)
+    wd = [(a.to(cuda_dev), b.to(cuda_dev)) for a, b in layers]
+    out = torch.empty(w.m, w.n_out, dtype=w.dtype, device=cuda_dev)
+    assert L.device_status(0, clear=True) == 0
+    try:
+        L.set_timeout_ns(5_000_000)
+        L.set_fault_injection(1)
+        cuda_ext.run_workload_out(w, xd, wd, None, out)
+        torch.cuda.synchronize()
+    finally:
+        L.set_fault_injection(0)
+        L.set_timeout_ns(0)
+    st = L.device_status(0, clear=True)
+    assert st in (0x700, 0x100, 0x200, 0x300), hex(st)
+    assert L.device_status(0) == 0
+    out.zero_()
+    cuda_ext.run_workload_out(w, xd, wd, None, out)
+    torch.cuda.synchronize()
+    _check(w, x, layers, ln, out, [(0, w.m)])
